@@ -1,0 +1,738 @@
+// C ABI: resident corpus handles and the entry points declared in
+// include/maxsim_b200.h.  Host-side validation reproduces the reference's
+// argument errors (cpp/maxsim/cuda_extension.cu:1806-1824, :2690-2707,
+// :2958-2966, :3224-3235); scoring routes to the tensor-core engine for
+// dim-128 scans it supports and to the SIMT engine otherwise.
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/maxsim_b200.h"
+#include "common.cuh"
+
+namespace msb {
+void launch_simt_scan(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, bool, float*,
+                      cudaStream_t);
+void launch_quantize_rows(const float*, int64_t, int, int8_t*, float*, int32_t*, int32_t*, bool, cudaStream_t);
+void launch_topk_rows(const float*, int64_t, int, int64_t, int, const int64_t*, bool, float*, int64_t*, cudaStream_t);
+void launch_pack_int4(const float*, int64_t, int, bool, uint8_t*, float*, float*, void*, cudaStream_t);
+void launch_pack_signs(const float*, int64_t, int, uint8_t*, float*, cudaStream_t);
+bool tc_scan_supported(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, bool residual);
+void launch_tc_scan(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, float*, void* ws,
+                    size_t ws_bytes, cudaStream_t);
+size_t tc_scan_workspace_bytes(const DocsView&, const QueryView&, const TargetsView&);
+
+static std::atomic<int64_t> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+static std::atomic<int> g_engine{0};  // 0 auto, 1 SIMT, 2 tensor core
+}  // namespace msb
+
+using namespace msb;
+
+static thread_local std::string g_last_error;
+
+namespace {
+
+struct DeviceBuf {
+  void* ptr = nullptr;
+  size_t cap = 0;
+  void ensure(size_t bytes, const char* what) {
+    if (bytes <= cap) return;
+    void* next = nullptr;
+    check(cudaMalloc(&next, bytes), what);
+    if (ptr) cudaFree(ptr);
+    ptr = next;
+    cap = bytes;
+  }
+  void release() {
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    cap = 0;
+  }
+  template <class T>
+  T* as() const { return static_cast<T*>(ptr); }
+};
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+template <class F>
+int guarded(F&& f) {
+  try {
+    f();
+    return MSB_OK;
+  } catch (const InvalidArgument& e) {
+    g_last_error = e.what();
+    return MSB_ERR_INVALID_ARGUMENT;
+  } catch (const NotSupported& e) {
+    g_last_error = e.what();
+    return MSB_ERR_NOT_SUPPORTED;
+  } catch (const CudaFailure& e) {
+    g_last_error = e.what();
+    return MSB_ERR_CUDA;
+  } catch (const std::bad_alloc&) {
+    g_last_error = "host allocation failed";
+    return MSB_ERR_INTERNAL;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return MSB_ERR_INTERNAL;
+  }
+}
+
+void validate_offsets(const int64_t* off, int64_t num_docs, int64_t num_tokens) {
+  if (num_docs < 0) throw InvalidArgument("offsets must contain at least [0, num_doc_tokens]");
+  if (off[0] != 0) throw InvalidArgument("offsets must start at 0");
+  if (off[num_docs] != num_tokens) throw InvalidArgument("offsets must end at num_doc_tokens");
+  for (int64_t i = 1; i <= num_docs; ++i)
+    if (off[i] < off[i - 1]) throw InvalidArgument("offsets must be monotonically nondecreasing");
+}
+
+}  // namespace
+
+struct msb_docs {
+  int format = 0;
+  int dim = 0;
+  int device = 0;
+  int64_t num_docs = 0;
+  int64_t num_tokens = 0;
+  float scale = 1.0F;
+  float residual_scale = 1.0F;
+  bool has_token_scale = false;
+  bool has_doc_scale = false;
+  bool has_residual = false;
+  cudaStream_t stream = nullptr;
+  DeviceBuf codes, offsets, token_scale, doc_scale, residual_codes, residual_token_scale;
+  // Workspace (grows monotonically, reused across calls).
+  DeviceBuf w_query, w_qcodes, w_qwords, w_qscale, w_qsum, w_scores, w_cands, w_weights, w_top_s, w_top_i,
+      w_override, w_fine, w_tc;
+  std::vector<int64_t> host_offsets;
+
+  size_t bytes_per_token() const { return format == kFormatInt4 ? dim / 2 : dim / 8; }
+  int64_t resident_bytes() const {
+    return static_cast<int64_t>(codes.cap + offsets.cap + token_scale.cap + doc_scale.cap + residual_codes.cap +
+                                residual_token_scale.cap);
+  }
+  int64_t workspace_bytes() const {
+    return static_cast<int64_t>(w_query.cap + w_qcodes.cap + w_qwords.cap + w_qscale.cap + w_qsum.cap +
+                                w_scores.cap + w_cands.cap + w_weights.cap + w_top_s.cap + w_top_i.cap +
+                                w_override.cap + w_fine.cap + w_tc.cap);
+  }
+  ~msb_docs() {
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    DeviceBuf* all[] = {&codes,   &offsets,  &token_scale, &doc_scale, &residual_codes, &residual_token_scale,
+                        &w_query, &w_qcodes, &w_qwords,    &w_qscale,  &w_qsum,         &w_scores,
+                        &w_cands, &w_weights, &w_top_s,    &w_top_i,   &w_override,     &w_fine,
+                        &w_tc};
+    for (DeviceBuf* b : all) b->release();
+    if (stream) cudaStreamDestroy(stream);
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+namespace {
+
+cudaStream_t pick_stream(msb_docs* h, void* s) { return s ? static_cast<cudaStream_t>(s) : h->stream; }
+
+struct Resolved {
+  DocsView docs;
+  ReduceView red;
+  bool residual;
+  int mode;
+};
+
+// Validate options against the handle; weights/override are device pointers.
+Resolved resolve(msb_docs* h, const msb_score_opts* o, int batch, int qtok, const float* d_weights,
+                 const float* d_override) {
+  if (!o) throw InvalidArgument("options must not be NULL");
+  if (o->reducer < kMaxSim || o->reducer > kSmooth)
+    throw InvalidArgument("reducer must be one of 'maxsim', 'weighted_maxsim', 'topk2', 'topk4', or 'smoothsim'");
+  if (!(o->temperature > 0.0F) || !std::isfinite(o->temperature))
+    throw InvalidArgument("temperature must be finite and > 0");
+  if (o->reducer == kWeighted) {
+    if (!o->weights) throw InvalidArgument("query_weights are required for reducer='weighted_maxsim'");
+    if (o->weight_rows != 1 && o->weight_rows != batch)
+      throw InvalidArgument("query_weights must have shape [query_tokens] or [batch, query_tokens]");
+  } else if (o->weights) {
+    throw InvalidArgument("query_weights are only valid for reducer='weighted_maxsim'");
+  }
+  if (o->query_mode != kQueryF32 && o->query_mode != kQueryI8) throw InvalidArgument("unknown query mode");
+  if (o->query_mode == kQueryI8 && o->reducer != kMaxSim)
+    throw InvalidArgument("int8 queries support reducer='maxsim' only");
+  Resolved r{};
+  DocsView& d = r.docs;
+  d.codes = h->codes.as<uint8_t>();
+  d.offsets = h->offsets.as<int64_t>();
+  d.num_docs = h->num_docs;
+  d.num_tokens = h->num_tokens;
+  d.dim = h->dim;
+  d.format = h->format;
+  r.residual = o->use_residual != 0;
+  if (h->format == kFormatInt4) {
+    d.token_scale = h->has_token_scale ? h->token_scale.as<float>() : nullptr;
+    d.scale = h->scale;
+    if (r.residual) {
+      if (!h->has_residual)
+        throw InvalidArgument("residual int4 data was requested but is not loaded on this CUDA handle");
+      if (o->query_mode != kQueryF32) throw InvalidArgument("residual scoring takes fp32 queries");
+      d.codes2 = h->residual_codes.as<uint8_t>();
+      d.token_scale2 = h->residual_token_scale.as<float>();
+      d.scale2 = h->residual_scale;
+    }
+  } else {
+    if (r.residual) throw InvalidArgument("residual scoring requires an int4 handle");
+    if (o->use_token_scale) {
+      if (!h->has_token_scale)
+        throw InvalidArgument("token scale vector was requested but is not loaded on this CUDA handle");
+      d.token_scale = h->token_scale.as<float>();
+    }
+    if (d_override) {
+      if (o->use_doc_scale) throw InvalidArgument("scale_vector_override and use_scale_vector cannot both be set");
+      d.doc_scale = d_override;
+    } else if (o->use_doc_scale) {
+      if (!h->has_doc_scale)
+        throw InvalidArgument("scale vector was requested but is not loaded on this CUDA handle");
+      d.doc_scale = h->doc_scale.as<float>();
+    }
+    d.scale = o->scale;
+  }
+  r.red.reducer = o->reducer;
+  r.red.weights = d_weights;
+  r.red.weights_batched = (o->reducer == kWeighted && o->weight_rows == batch && batch > 1) ? 1 : 0;
+  r.red.temperature = o->temperature;
+  r.mode = o->query_mode;
+  (void)qtok;
+  return r;
+}
+
+// Run one scan into d_out [B, T].  d_query is a device pointer.
+void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, int qtok, const TargetsView& tg,
+              float* d_out, cudaStream_t stream) {
+  const int64_t T = tg.ids ? tg.count : h->num_docs;
+  if (batch == 0 || T == 0) return;
+  if (qtok == 0) {
+    check(cudaMemsetAsync(d_out, 0, sizeof(float) * static_cast<size_t>(batch) * T, stream), "zero scores");
+    return;
+  }
+  QueryView qv{};
+  qv.f32 = d_query;
+  qv.batch = batch;
+  qv.qtok = qtok;
+  qv.mode = r.mode;
+  if (r.mode == kQueryI8) {
+    const int64_t rows = static_cast<int64_t>(batch) * qtok;
+    h->w_qcodes.ensure(static_cast<size_t>(rows) * h->dim, "cudaMalloc int8 query codes");
+    h->w_qwords.ensure(static_cast<size_t>(rows) * h->dim, "cudaMalloc int8 query words");
+    h->w_qscale.ensure(static_cast<size_t>(rows) * sizeof(float), "cudaMalloc int8 query scales");
+    h->w_qsum.ensure(static_cast<size_t>(rows) * sizeof(int32_t), "cudaMalloc int8 query sums");
+    launch_quantize_rows(d_query, rows, h->dim, h->w_qcodes.as<int8_t>(), h->w_qscale.as<float>(),
+                         h->w_qsum.as<int32_t>(), h->w_qwords.as<int32_t>(), h->format == kFormatInt4, stream);
+    qv.i8 = h->w_qcodes.as<int8_t>();
+    qv.i8_words = h->w_qwords.as<int32_t>();
+    qv.row_scale = h->w_qscale.as<float>();
+    qv.row_sum = h->w_qsum.as<int32_t>();
+  }
+  const int engine = g_engine.load();
+  const bool tc_ok = tc_scan_supported(r.docs, qv, r.red, tg, r.residual);
+  if (engine == 2 && !tc_ok) throw NotSupported("the tensor-core engine does not support this scan");
+  if (tc_ok && engine != 1) {
+    const size_t ws = tc_scan_workspace_bytes(r.docs, qv, tg);
+    h->w_tc.ensure(ws > 0 ? ws : 16, "cudaMalloc tensor-core scan workspace");
+    launch_tc_scan(r.docs, qv, r.red, tg, d_out, h->w_tc.ptr, h->w_tc.cap, stream);
+    return;
+  }
+  launch_simt_scan(r.docs, qv, r.red, tg, r.residual, d_out, stream);
+}
+
+void check_query(msb_docs* h, const void* q, int batch, int qtok) {
+  if (batch < 0 || qtok < 0) throw InvalidArgument("query must have shape [batch, query_tokens, dim]");
+  if (!q && static_cast<int64_t>(batch) * qtok > 0) throw InvalidArgument("query pointer is NULL");
+  (void)h;
+}
+
+void check_candidates(msb_docs* h, const int64_t* c, int64_t m) {
+  for (int64_t i = 0; i < m; ++i)
+    if (c[i] < 0 || c[i] >= h->num_docs)
+      throw InvalidArgument("candidate_indices entries must be between 0 and num_docs - 1");
+}
+
+// Copy host weights/override to device scratch; returns device pointers.
+void stage_host_options(msb_docs* h, const msb_score_opts* o, int batch, int qtok, cudaStream_t s,
+                        const float** d_w, const float** d_ov) {
+  *d_w = nullptr;
+  *d_ov = nullptr;
+  if (o && o->reducer == kWeighted && o->weights) {
+    const int rows = o->weight_rows == batch ? batch : 1;
+    const size_t bytes = sizeof(float) * static_cast<size_t>(rows) * qtok;
+    if (bytes) {
+      h->w_weights.ensure(bytes, "cudaMalloc reducer query-weight cache");
+      check(cudaMemcpyAsync(h->w_weights.ptr, o->weights, bytes, cudaMemcpyHostToDevice, s), "copy query weights");
+      *d_w = h->w_weights.as<float>();
+    } else {
+      *d_w = reinterpret_cast<const float*>(o->weights);  // never dereferenced
+    }
+  }
+  if (o && o->doc_scale_override) {
+    const size_t bytes = sizeof(float) * static_cast<size_t>(h->num_docs);
+    h->w_override.ensure(bytes > 0 ? bytes : 4, "cudaMalloc reducer scale-vector cache");
+    check(cudaMemcpyAsync(h->w_override.ptr, o->doc_scale_override, bytes, cudaMemcpyHostToDevice, s),
+          "copy scale-vector override");
+    *d_ov = h->w_override.as<float>();
+  }
+}
+
+const float* stage_query(msb_docs* h, const float* q, int batch, int qtok, cudaStream_t s) {
+  const size_t bytes = sizeof(float) * static_cast<size_t>(batch) * qtok * h->dim;
+  if (!bytes) return nullptr;
+  h->w_query.ensure(bytes, "cudaMalloc resident query cache");
+  check(cudaMemcpyAsync(h->w_query.ptr, q, bytes, cudaMemcpyHostToDevice, s), "copy query to device");
+  return h->w_query.as<float>();
+}
+
+msb_docs* create_common(int32_t format, int32_t dim, int64_t num_tokens, const int64_t* offsets_host,
+                        int64_t num_docs) {
+  if (format != kFormatInt4 && format != kFormatBinary) throw InvalidArgument("unknown format");
+  if (format == kFormatInt4 && (dim <= 0 || dim % 2 != 0)) throw InvalidArgument("dim must be positive and divisible by 2");
+  if (dim <= 0 || dim % 8 != 0) throw InvalidArgument("dim must be positive and divisible by 8");
+  if (num_tokens < 0) throw InvalidArgument("packed must have shape [num_doc_tokens, bytes]");
+  if (!offsets_host || num_docs < 1) throw InvalidArgument("offsets must contain at least [0, num_doc_tokens]");
+  if (num_docs > 0x7FFFFFFF) throw NotSupported("more than 2^31 - 1 documents per handle");
+  validate_offsets(offsets_host, num_docs, num_tokens);
+  auto* h = new msb_docs();
+  h->format = format;
+  h->dim = dim;
+  h->num_docs = num_docs;
+  h->num_tokens = num_tokens;
+  cudaGetDevice(&h->device);
+  check(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking), "create handle stream");
+  h->host_offsets.assign(offsets_host, offsets_host + num_docs + 1);
+  return h;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* msb_last_error(void) { return g_last_error.c_str(); }
+int msb_version(void) { return 1; }
+int64_t msb_launch_count(void) { return g_launches.load(); }
+
+int msb_set_option(const char* name, int64_t value) {
+  return guarded([&] {
+    if (!name) throw InvalidArgument("option name is NULL");
+    if (std::strcmp(name, "engine") == 0) {
+      if (value < 0 || value > 2) throw InvalidArgument("engine must be 0 (auto), 1 (SIMT) or 2 (tensor core)");
+      g_engine.store(static_cast<int>(value));
+      return;
+    }
+    throw InvalidArgument(std::string("unknown option: ") + name);
+  });
+}
+
+int msb_get_option(const char* name, int64_t* value) {
+  return guarded([&] {
+    if (!name || !value) throw InvalidArgument("NULL argument");
+    if (std::strcmp(name, "engine") == 0) {
+      *value = g_engine.load();
+      return;
+    }
+    throw InvalidArgument(std::string("unknown option: ") + name);
+  });
+}
+
+int msb_docs_create(int32_t format, int32_t dim, const uint8_t* codes, int64_t num_tokens, const int64_t* offsets,
+                    int64_t num_docs, float scale, msb_docs** out) {
+  return guarded([&] {
+    if (!out) throw InvalidArgument("out is NULL");
+    *out = nullptr;
+    if (format == kFormatInt4 && (!(scale > 0.0F) || !std::isfinite(scale)))
+      throw InvalidArgument("scale must be finite and > 0");
+    msb_docs* h = create_common(format, dim, num_tokens, offsets, num_docs);
+    try {
+      h->scale = format == kFormatInt4 ? scale : 1.0F;
+      const size_t cbytes = h->bytes_per_token() * static_cast<size_t>(num_tokens);
+      if (cbytes) {
+        if (!codes) throw InvalidArgument("packed pointer is NULL");
+        h->codes.ensure(cbytes, "cudaMalloc packed docs");
+        check(cudaMemcpyAsync(h->codes.ptr, codes, cbytes, cudaMemcpyHostToDevice, h->stream),
+              "copy packed docs to device");
+      }
+      h->offsets.ensure(sizeof(int64_t) * (num_docs + 1), "cudaMalloc offsets");
+      check(cudaMemcpyAsync(h->offsets.ptr, offsets, sizeof(int64_t) * (num_docs + 1), cudaMemcpyHostToDevice,
+                            h->stream),
+            "copy offsets to device");
+      check(cudaStreamSynchronize(h->stream), "synchronize upload");
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+int msb_docs_create_device(int32_t format, int32_t dim, const uint8_t* codes, int64_t num_tokens,
+                           const int64_t* offsets_device, const int64_t* offsets_host, int64_t num_docs, float scale,
+                           msb_docs** out) {
+  return guarded([&] {
+    if (!out) throw InvalidArgument("out is NULL");
+    *out = nullptr;
+    if (format == kFormatInt4 && (!(scale > 0.0F) || !std::isfinite(scale)))
+      throw InvalidArgument("scale must be finite and > 0");
+    msb_docs* h = create_common(format, dim, num_tokens, offsets_host, num_docs);
+    try {
+      h->scale = format == kFormatInt4 ? scale : 1.0F;
+      const size_t cbytes = h->bytes_per_token() * static_cast<size_t>(num_tokens);
+      if (cbytes) {
+        h->codes.ensure(cbytes, "cudaMalloc packed docs");
+        check(cudaMemcpyAsync(h->codes.ptr, codes, cbytes, cudaMemcpyDeviceToDevice, h->stream), "copy packed docs");
+      }
+      h->offsets.ensure(sizeof(int64_t) * (num_docs + 1), "cudaMalloc offsets");
+      const void* src = offsets_device ? static_cast<const void*>(offsets_device) : offsets_host;
+      check(cudaMemcpyAsync(h->offsets.ptr, src, sizeof(int64_t) * (num_docs + 1), cudaMemcpyDefault, h->stream),
+            "copy offsets");
+      check(cudaStreamSynchronize(h->stream), "synchronize upload");
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+int msb_docs_destroy(msb_docs* docs) {
+  return guarded([&] { delete docs; });
+}
+
+int msb_docs_get_info(const msb_docs* h, msb_docs_info* info) {
+  return guarded([&] {
+    if (!h || !info) throw InvalidArgument("NULL argument");
+    info->format = h->format;
+    info->dim = h->dim;
+    info->num_docs = h->num_docs;
+    info->num_tokens = h->num_tokens;
+    info->packed_size = static_cast<int64_t>(h->bytes_per_token()) * h->num_tokens;
+    info->scale = h->scale;
+    info->residual_scale = h->residual_scale;
+    info->has_token_scale = h->has_token_scale;
+    info->has_doc_scale = h->has_doc_scale;
+    info->has_residual = h->has_residual;
+    info->device = h->device;
+    info->resident_bytes = h->resident_bytes();
+    info->workspace_bytes = h->workspace_bytes();
+  });
+}
+
+int msb_docs_set_token_scales(msb_docs* h, const float* scales, int64_t count, int32_t require_positive) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    if (count != h->num_tokens) throw InvalidArgument("token scale vector must have shape [num_doc_tokens]");
+    if (require_positive)
+      for (int64_t i = 0; i < count; ++i)
+        if (!(scales[i] > 0.0F) || !std::isfinite(scales[i]))
+          throw InvalidArgument("token scales must be finite and > 0");
+    DeviceGuard g(h->device);
+    const size_t bytes = sizeof(float) * static_cast<size_t>(count);
+    h->token_scale.ensure(bytes > 0 ? bytes : 4, "cudaMalloc resident token scale vector");
+    if (bytes) {
+      check(cudaMemcpyAsync(h->token_scale.ptr, scales, bytes, cudaMemcpyHostToDevice, h->stream),
+            "copy token scale vector to device");
+      check(cudaStreamSynchronize(h->stream), "synchronize token scale upload");
+    }
+    h->has_token_scale = true;
+  });
+}
+
+int msb_docs_set_token_scales_device(msb_docs* h, const float* scales, int64_t count) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    if (count != h->num_tokens) throw InvalidArgument("token scale vector must have shape [num_doc_tokens]");
+    DeviceGuard g(h->device);
+    const size_t bytes = sizeof(float) * static_cast<size_t>(count);
+    h->token_scale.ensure(bytes > 0 ? bytes : 4, "cudaMalloc resident token scale vector");
+    if (bytes) {
+      check(cudaMemcpyAsync(h->token_scale.ptr, scales, bytes, cudaMemcpyDeviceToDevice, h->stream),
+            "copy token scale vector");
+      check(cudaStreamSynchronize(h->stream), "synchronize token scale upload");
+    }
+    h->has_token_scale = true;
+  });
+}
+
+int msb_docs_clear_token_scales(msb_docs* h) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    h->has_token_scale = false;
+  });
+}
+
+int msb_docs_set_doc_scales(msb_docs* h, const float* scales, int64_t count) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    if (count != h->num_docs) throw InvalidArgument("scale vector must have shape [num_docs]");
+    DeviceGuard g(h->device);
+    const size_t bytes = sizeof(float) * static_cast<size_t>(count);
+    h->doc_scale.ensure(bytes, "cudaMalloc resident scale vector");
+    check(cudaMemcpyAsync(h->doc_scale.ptr, scales, bytes, cudaMemcpyHostToDevice, h->stream),
+          "copy scale vector to device");
+    check(cudaStreamSynchronize(h->stream), "synchronize scale upload");
+    h->has_doc_scale = true;
+  });
+}
+
+int msb_docs_clear_doc_scales(msb_docs* h) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    h->has_doc_scale = false;
+  });
+}
+
+int msb_docs_set_residual(msb_docs* h, const uint8_t* codes, int64_t num_tokens, float scale,
+                          const float* token_scales) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    if (h->format != kFormatInt4) throw InvalidArgument("residual int4 data requires an int4 handle");
+    if (num_tokens != h->num_tokens)
+      throw InvalidArgument("residual packed data must have shape [num_doc_tokens, dim / 2]");
+    if (!(scale > 0.0F) || !std::isfinite(scale)) throw InvalidArgument("residual scale must be finite and > 0");
+    for (int64_t i = 0; i < num_tokens; ++i)
+      if (!(token_scales[i] > 0.0F) || !std::isfinite(token_scales[i]))
+        throw InvalidArgument("residual token scales must be finite and > 0");
+    DeviceGuard g(h->device);
+    const size_t cbytes = h->bytes_per_token() * static_cast<size_t>(num_tokens);
+    const size_t sbytes = sizeof(float) * static_cast<size_t>(num_tokens);
+    h->residual_codes.ensure(cbytes > 0 ? cbytes : 4, "cudaMalloc resident int4 residual data");
+    h->residual_token_scale.ensure(sbytes > 0 ? sbytes : 4, "cudaMalloc resident int4 residual token scales");
+    if (cbytes)
+      check(cudaMemcpyAsync(h->residual_codes.ptr, codes, cbytes, cudaMemcpyHostToDevice, h->stream),
+            "copy int4 residual data to device");
+    if (sbytes)
+      check(cudaMemcpyAsync(h->residual_token_scale.ptr, token_scales, sbytes, cudaMemcpyHostToDevice, h->stream),
+            "copy int4 residual token scales to device");
+    check(cudaStreamSynchronize(h->stream), "synchronize residual upload");
+    h->residual_scale = scale;
+    h->has_residual = true;
+  });
+}
+
+int msb_docs_clear_residual(msb_docs* h) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    h->has_residual = false;
+  });
+}
+
+int msb_docs_score(msb_docs* h, const float* query, int32_t batch, int32_t qtok, const msb_score_opts* opts,
+                   const int64_t* candidates, int64_t num_candidates, float* out) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    check_query(h, query, batch, qtok);
+    if (candidates) check_candidates(h, candidates, num_candidates);
+    DeviceGuard g(h->device);
+    cudaStream_t s = h->stream;
+    const float *d_w, *d_ov;
+    stage_host_options(h, opts, batch, qtok, s, &d_w, &d_ov);
+    Resolved r = resolve(h, opts, batch, qtok, d_w, d_ov);
+    const int64_t T = candidates ? num_candidates : h->num_docs;
+    if (batch == 0 || T == 0) return;
+    const float* d_q = stage_query(h, query, batch, qtok, s);
+    TargetsView tg{};
+    if (candidates) {
+      h->w_cands.ensure(sizeof(int64_t) * T, "cudaMalloc reducer candidate cache");
+      check(cudaMemcpyAsync(h->w_cands.ptr, candidates, sizeof(int64_t) * T, cudaMemcpyHostToDevice, s),
+            "copy reducer candidates to device");
+      tg.ids = h->w_cands.as<int64_t>();
+      tg.count = T;
+    }
+    const size_t obytes = sizeof(float) * static_cast<size_t>(batch) * T;
+    h->w_scores.ensure(obytes, "cudaMalloc resident score cache");
+    run_scan(h, r, d_q, batch, qtok, tg, h->w_scores.as<float>(), s);
+    check(cudaMemcpyAsync(out, h->w_scores.ptr, obytes, cudaMemcpyDeviceToHost, s), "copy output to host");
+    check(cudaStreamSynchronize(s), "synchronize scoring");
+  });
+}
+
+int msb_docs_topk(msb_docs* h, const float* query, int32_t batch, int32_t qtok, int32_t k, const msb_score_opts* opts,
+                  float* out_scores, int64_t* out_ids) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    if (k < 1 || k > h->num_docs) throw InvalidArgument("k must be between 1 and num_docs");
+    check_query(h, query, batch, qtok);
+    DeviceGuard g(h->device);
+    cudaStream_t s = h->stream;
+    const float *d_w, *d_ov;
+    stage_host_options(h, opts, batch, qtok, s, &d_w, &d_ov);
+    Resolved r = resolve(h, opts, batch, qtok, d_w, d_ov);
+    if (batch == 0) return;
+    const float* d_q = stage_query(h, query, batch, qtok, s);
+    h->w_scores.ensure(sizeof(float) * static_cast<size_t>(batch) * h->num_docs, "cudaMalloc full score cache");
+    h->w_top_s.ensure(sizeof(float) * static_cast<size_t>(batch) * k, "cudaMalloc top score cache");
+    h->w_top_i.ensure(sizeof(int64_t) * static_cast<size_t>(batch) * k, "cudaMalloc top index cache");
+    TargetsView tg{};
+    run_scan(h, r, d_q, batch, qtok, tg, h->w_scores.as<float>(), s);
+    launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, k, nullptr, false,
+                     h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
+    check(cudaMemcpyAsync(out_scores, h->w_top_s.ptr, sizeof(float) * static_cast<size_t>(batch) * k,
+                          cudaMemcpyDeviceToHost, s),
+          "copy top scores to host");
+    check(cudaMemcpyAsync(out_ids, h->w_top_i.ptr, sizeof(int64_t) * static_cast<size_t>(batch) * k,
+                          cudaMemcpyDeviceToHost, s),
+          "copy top indices to host");
+    check(cudaStreamSynchronize(s), "synchronize top-k");
+  });
+}
+
+int msb_docs_cascade_topk(msb_docs* h, const float* query, int32_t batch, int32_t qtok, int32_t k, int32_t m,
+                          const msb_score_opts* opts, float* out_scores, int64_t* out_ids) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    if (k < 1 || k > m || m > h->num_docs)
+      throw InvalidArgument("cascade sizes must satisfy 1 <= k <= candidates <= num_docs");
+    if (!h->has_residual || !h->has_token_scale)
+      throw InvalidArgument("the cascade requires per-token prefix scales and residual int4 data");
+    check_query(h, query, batch, qtok);
+    DeviceGuard g(h->device);
+    cudaStream_t s = h->stream;
+    const float *d_w, *d_ov;
+    stage_host_options(h, opts, batch, qtok, s, &d_w, &d_ov);
+    msb_score_opts prefix_opts = *opts;
+    prefix_opts.use_residual = 0;
+    prefix_opts.query_mode = kQueryF32;
+    Resolved rp = resolve(h, &prefix_opts, batch, qtok, d_w, d_ov);
+    msb_score_opts fine_opts = prefix_opts;
+    fine_opts.use_residual = 1;
+    Resolved rf = resolve(h, &fine_opts, batch, qtok, d_w, d_ov);
+    if (batch == 0) return;
+    const float* d_q = stage_query(h, query, batch, qtok, s);
+    const size_t B = static_cast<size_t>(batch);
+    h->w_top_s.ensure(sizeof(float) * B * k, "cudaMalloc top score cache");
+    h->w_top_i.ensure(sizeof(int64_t) * B * k, "cudaMalloc top index cache");
+    if (m == h->num_docs) {
+      h->w_scores.ensure(sizeof(float) * B * h->num_docs, "cudaMalloc full score cache");
+      run_scan(h, rf, d_q, batch, qtok, TargetsView{}, h->w_scores.as<float>(), s);
+      launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, k, nullptr, false,
+                       h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
+    } else {
+      h->w_scores.ensure(sizeof(float) * B * h->num_docs, "cudaMalloc coarse score cache");
+      h->w_cands.ensure(sizeof(int64_t) * B * m, "cudaMalloc cascade candidate cache");
+      h->w_fine.ensure(sizeof(float) * B * m * 2, "cudaMalloc cascade fine score cache");
+      run_scan(h, rp, d_q, batch, qtok, TargetsView{}, h->w_scores.as<float>(), s);
+      // Per-row top-M of the prefix scores (values land in the second half of w_fine).
+      float* top_m_scores = h->w_fine.as<float>() + B * m;
+      launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, m, nullptr, false, top_m_scores,
+                       h->w_cands.as<int64_t>(), s);
+      TargetsView tg{};
+      tg.ids = h->w_cands.as<int64_t>();
+      tg.count = m;
+      tg.per_row = 1;
+      // Rescoring of per-row candidate lists always runs on the SIMT engine.
+      launch_simt_scan(rf.docs, QueryView{d_q, nullptr, nullptr, nullptr, nullptr, batch, qtok, kQueryF32}, rf.red,
+                       tg, true, h->w_fine.as<float>(), s);
+      launch_topk_rows(h->w_fine.as<float>(), m, batch, m, k, h->w_cands.as<int64_t>(), true,
+                       h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
+    }
+    check(cudaMemcpyAsync(out_scores, h->w_top_s.ptr, sizeof(float) * B * k, cudaMemcpyDeviceToHost, s),
+          "copy cascade scores to host");
+    check(cudaMemcpyAsync(out_ids, h->w_top_i.ptr, sizeof(int64_t) * B * k, cudaMemcpyDeviceToHost, s),
+          "copy cascade indices to host");
+    check(cudaStreamSynchronize(s), "synchronize cascade");
+  });
+}
+
+int msb_docs_score_device(msb_docs* h, const float* query, int32_t batch, int32_t qtok, const msb_score_opts* opts,
+                          const int64_t* candidates, int64_t num_candidates, float* out, void* stream) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    check_query(h, query, batch, qtok);
+    DeviceGuard g(h->device);
+    cudaStream_t s = pick_stream(h, stream);
+    Resolved r = resolve(h, opts, batch, qtok, opts ? opts->weights : nullptr, opts ? opts->doc_scale_override : nullptr);
+    TargetsView tg{};
+    if (candidates) {
+      tg.ids = candidates;
+      tg.count = num_candidates;
+    }
+    run_scan(h, r, query, batch, qtok, tg, out, s);
+  });
+}
+
+int msb_docs_topk_device(msb_docs* h, const float* query, int32_t batch, int32_t qtok, int32_t k,
+                         const msb_score_opts* opts, float* out_scores, int64_t* out_ids, void* stream) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    if (k < 1 || k > h->num_docs) throw InvalidArgument("k must be between 1 and num_docs");
+    check_query(h, query, batch, qtok);
+    DeviceGuard g(h->device);
+    cudaStream_t s = pick_stream(h, stream);
+    Resolved r = resolve(h, opts, batch, qtok, opts ? opts->weights : nullptr, opts ? opts->doc_scale_override : nullptr);
+    if (batch == 0) return;
+    h->w_scores.ensure(sizeof(float) * static_cast<size_t>(batch) * h->num_docs, "cudaMalloc full score cache");
+    run_scan(h, r, query, batch, qtok, TargetsView{}, h->w_scores.as<float>(), s);
+    launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, k, nullptr, false, out_scores, out_ids,
+                     s);
+  });
+}
+
+int msb_topk_rows_device(const float* scores, int64_t ld, int32_t rows, int64_t count, int32_t k,
+                         const int64_t* tie_ids, int32_t tie_batched, float* out_scores, int64_t* out_ids,
+                         void* stream) {
+  return guarded([&] {
+    if (ld < count) throw InvalidArgument("ld must be >= count");
+    launch_topk_rows(scores, ld, rows, count, k, tie_ids, tie_batched != 0, out_scores, out_ids,
+                     static_cast<cudaStream_t>(stream));
+  });
+}
+
+int msb_quantize_query_int8_device(const float* query, int64_t rows, int32_t dim, int8_t* codes, float* scales,
+                                   void* stream) {
+  return guarded([&] {
+    if (dim <= 0 || dim % 8 != 0) throw InvalidArgument("dim must be positive and divisible by 8");
+    launch_quantize_rows(query, rows, dim, codes, scales, nullptr, nullptr, false, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int msb_pack_int4_device(const float* x, int64_t n, int32_t dim, int32_t per_token, uint8_t* codes,
+                         float* token_scales, float* tensor_scale, void* stream) {
+  return guarded([&] {
+    if (dim <= 0 || dim % 8 != 0) throw InvalidArgument("dim must be positive and divisible by 8");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (per_token) {
+      if (!token_scales) throw InvalidArgument("token_scales is NULL");
+      launch_pack_int4(x, n, dim, true, codes, token_scales, nullptr, nullptr, s);
+      return;
+    }
+    void* scratch = nullptr;
+    check(cudaMalloc(&scratch, 16), "cudaMalloc absmax scratch");
+    try {
+      launch_pack_int4(x, n, dim, false, codes, nullptr, tensor_scale, scratch, s);
+    } catch (...) {
+      cudaFree(scratch);
+      throw;
+    }
+    cudaFree(scratch);
+  });
+}
+
+int msb_pack_signs_device(const float* x, int64_t n, int32_t dim, uint8_t* bits, float* mean_abs, void* stream) {
+  return guarded([&] {
+    if (dim <= 0 || dim % 8 != 0) throw InvalidArgument("dim must be positive and divisible by 8");
+    launch_pack_signs(x, n, dim, bits, mean_abs, static_cast<cudaStream_t>(stream));
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,210 @@
+// Row-wise top-k selection: score descending, ties to the lower id.
+//
+// Tie policy of the reference: cpp/maxsim/cuda_extension.cu:1629-1692 and
+// src/maxsim/_api.py:732-735 (lexsort by (-score, id)); with explicit tie ids
+// it is src/maxsim/cascade.py:436-453 (ties broken by candidate doc id).
+//
+// Two paths, one block of 1024 threads per row:
+//   * small rows (T <= kSortCap): bitonic sort of (ordered key, tie id) in
+//     shared memory -- used for candidate lists, shard merges and short rows;
+//   * long rows: 4-pass 8-bit radix select of the k-th largest ordered key,
+//     then collection of everything above it plus the lowest-index ties, and
+//     a bitonic sort of the k survivors.
+#include "common.cuh"
+
+namespace msb {
+
+constexpr int kTopkThreads = 1024;
+constexpr int kSortCap = 4096;
+
+// Sort (composite descending, then payload) pairs held in shared memory.
+__device__ void bitonic_sort_desc(uint64_t* key, uint32_t* pos, int n_pow2) {
+  for (int size = 2; size <= n_pow2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < n_pow2; i += blockDim.x) {
+        int partner = i ^ stride;
+        if (partner > i) {
+          bool descending = (i & size) == 0;
+          uint64_t a = key[i], b = key[partner];
+          bool swap = descending ? (a < b) : (a > b);
+          if (swap) {
+            key[i] = b;
+            key[partner] = a;
+            uint32_t t = pos[i];
+            pos[i] = pos[partner];
+            pos[partner] = t;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+__device__ __forceinline__ uint64_t composite(uint32_t okey, uint32_t tie) {
+  return (static_cast<uint64_t>(okey) << 32) | static_cast<uint64_t>(0xFFFFFFFFu - tie);
+}
+
+__global__ void __launch_bounds__(kTopkThreads) topk_sort_kernel(const float* __restrict__ scores, int64_t ld,
+                                                                  int64_t T, int k, const int64_t* __restrict__ tie_ids,
+                                                                  int tie_batched, float* __restrict__ out_s,
+                                                                  int64_t* __restrict__ out_id) {
+  extern __shared__ unsigned char smem_raw[];
+  int n = 1;
+  while (n < T) n <<= 1;
+  uint64_t* key = reinterpret_cast<uint64_t*>(smem_raw);
+  uint32_t* pos = reinterpret_cast<uint32_t*>(key + n);
+  const int row = blockIdx.x;
+  const float* s = scores + static_cast<int64_t>(row) * ld;
+  const int64_t* tie = tie_ids ? tie_ids + (tie_batched ? static_cast<int64_t>(row) * T : 0) : nullptr;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    if (i < T) {
+      uint32_t t = tie ? static_cast<uint32_t>(tie[i]) : static_cast<uint32_t>(i);
+      key[i] = composite(float_to_ordered(s[i]), t);
+      pos[i] = static_cast<uint32_t>(i);
+    } else {
+      key[i] = 0;
+      pos[i] = 0xFFFFFFFFu;
+    }
+  }
+  __syncthreads();
+  bitonic_sort_desc(key, pos, n);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    uint32_t p = pos[i];
+    out_s[static_cast<int64_t>(row) * k + i] = s[p];
+    out_id[static_cast<int64_t>(row) * k + i] = tie ? tie[p] : static_cast<int64_t>(p);
+  }
+}
+
+__global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(const float* __restrict__ scores, int64_t ld,
+                                                                    int64_t T, int k, float* __restrict__ out_s,
+                                                                    int64_t* __restrict__ out_id) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_prefix, s_mask, s_remaining, s_taken, s_ties_taken;
+  __shared__ uint32_t warp_count[kTopkThreads / 32];
+  int n = 1;
+  while (n < k) n <<= 1;
+  uint64_t* key = reinterpret_cast<uint64_t*>(smem_raw);
+  uint32_t* pos = reinterpret_cast<uint32_t*>(key + n);
+  const int row = blockIdx.x;
+  const float* s = scores + static_cast<int64_t>(row) * ld;
+
+  if (threadIdx.x == 0) {
+    s_prefix = 0;
+    s_mask = 0;
+    s_remaining = static_cast<uint32_t>(k);
+    s_taken = 0;
+    s_ties_taken = 0;
+  }
+  __syncthreads();
+  // Radix select of the k-th largest ordered key, most significant byte first.
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix, mask = s_mask;
+    for (int64_t i = threadIdx.x; i < T; i += blockDim.x) {
+      uint32_t kk = float_to_ordered(s[i]);
+      if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 0xFFu], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t need = s_remaining, acc = 0;
+      int digit = 255;
+      for (; digit > 0; --digit) {
+        if (acc + hist[digit] >= need) break;
+        acc += hist[digit];
+      }
+      s_prefix = prefix | (static_cast<uint32_t>(digit) << shift);
+      s_mask = mask | (0xFFu << shift);
+      s_remaining = need - acc;
+    }
+    __syncthreads();
+  }
+  const uint32_t kth = s_prefix;          // exact k-th largest ordered key
+  const uint32_t ties_needed = s_remaining;  // how many elements equal to kth to keep
+  // Collect strictly greater keys (at most k - ties_needed of them).
+  for (int64_t i = threadIdx.x; i < T; i += blockDim.x) {
+    uint32_t kk = float_to_ordered(s[i]);
+    if (kk > kth) {
+      uint32_t slot = atomicAdd(&s_taken, 1u);
+      key[slot] = composite(kk, static_cast<uint32_t>(i));
+      pos[slot] = static_cast<uint32_t>(i);
+    }
+  }
+  __syncthreads();
+  // Ties: keep the lowest indices, scanning chunks in index order.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t base = 0; base < T; base += blockDim.x) {
+    if (s_ties_taken >= ties_needed) break;
+    const int64_t i = base + threadIdx.x;
+    const bool tie = i < T && float_to_ordered(s[i]) == kth;
+    const uint32_t ballot = __ballot_sync(0xFFFFFFFFu, tie);
+    if (lane == 0) warp_count[warp] = __popc(ballot);
+    __syncthreads();
+    if (tie) {
+      uint32_t before = s_ties_taken;
+      for (int w = 0; w < warp; ++w) before += warp_count[w];
+      before += __popc(ballot & ((1u << lane) - 1u));
+      if (before < ties_needed) {
+        uint32_t slot = s_taken + (before - s_ties_taken);
+        key[slot] = composite(kth, static_cast<uint32_t>(i));
+        pos[slot] = static_cast<uint32_t>(i);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t total = 0;
+      for (int w = 0; w < kTopkThreads / 32; ++w) total += warp_count[w];
+      uint32_t got = total < ties_needed - s_ties_taken ? total : ties_needed - s_ties_taken;
+      s_taken += got;
+      s_ties_taken += got;
+    }
+    __syncthreads();
+  }
+  for (int i = k + threadIdx.x; i < n; i += blockDim.x) {
+    key[i] = 0;
+    pos[i] = 0xFFFFFFFFu;
+  }
+  __syncthreads();
+  bitonic_sort_desc(key, pos, n);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    uint32_t p = pos[i];
+    out_s[static_cast<int64_t>(row) * k + i] = s[p];
+    out_id[static_cast<int64_t>(row) * k + i] = static_cast<int64_t>(p);
+  }
+}
+
+static int next_pow2(int64_t v) {
+  int n = 1;
+  while (n < v) n <<= 1;
+  return n;
+}
+
+void launch_topk_rows(const float* scores, int64_t ld, int rows, int64_t T, int k, const int64_t* tie_ids,
+                      bool tie_batched, float* out_s, int64_t* out_id, cudaStream_t stream) {
+  if (rows <= 0) return;
+  if (k < 1 || k > T) throw InvalidArgument("k must be between 1 and the number of targets");
+  if (T > 0xFFFFFFF0LL) throw NotSupported("top-k rows longer than 2^32 - 16 are not supported");
+  if (T <= kSortCap) {
+    const size_t smem = static_cast<size_t>(next_pow2(T)) * (sizeof(uint64_t) + sizeof(uint32_t));
+    topk_sort_kernel<<<rows, kTopkThreads, smem, stream>>>(scores, ld, T, k, tie_ids, tie_batched ? 1 : 0, out_s,
+                                                            out_id);
+    count_launch();
+    check(cudaGetLastError(), "launch top-k sort kernel");
+    return;
+  }
+  if (tie_ids) throw NotSupported("explicit tie ids are supported for rows of at most 4096 targets");
+  if (k > 8192) throw NotSupported("k above 8192 is not supported for long rows");
+  const size_t smem = static_cast<size_t>(next_pow2(k)) * (sizeof(uint64_t) + sizeof(uint32_t));
+  if (smem > 48 * 1024) {
+    check(cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem)),
+          "raise top-k shared memory limit");
+  }
+  topk_select_kernel<<<rows, kTopkThreads, smem, stream>>>(scores, ld, T, k, out_s, out_id);
+  count_launch();
+  check(cudaGetLastError(), "launch top-k select kernel");
+}
+
+}  // namespace msb
