@@ -273,7 +273,9 @@ def main() -> None:
     n_batches = NUM_QUERIES // BATCH
     info = ShardInfo(rank=rank, world_size=world, doc_lo=page_lo, doc_hi=page_hi, num_docs_total=NUM_PAGES)
     searcher = ShardedReranker(handle, info, int8_query=True)
-    stream = torch.cuda.current_stream(device)
+    work_stream = torch.cuda.Stream(device)  # every timed launch goes to this stream
+    torch.cuda.set_stream(work_stream)
+    stream = work_stream
 
     def step(i):
         return searcher.search_device(queries[i % n_batches], TOP_K)

@@ -22,7 +22,7 @@
  *     monotonically and are reused across calls (reference :2350-2360), so a
  *     handle must not be used by two threads at once.
  *   - `*_device` entry points take device pointers and enqueue work on
- *     `stream` (a cudaStream_t; NULL selects the handle's own stream) without
+ *     `stream` (a cudaStream_t; NULL is the legacy default stream) without
  *     synchronising.  The other entry points take host pointers and return
  *     after the results are in host memory, like the reference methods.
  *   - No entry point falls back to the CPU.

@@ -120,6 +120,7 @@ struct msb_docs {
   DeviceBuf w_query, w_qcodes, w_qwords, w_qscale, w_qsum, w_scores, w_cands, w_weights, w_top_s, w_top_i,
       w_override, w_fine, w_tc;
   std::vector<int64_t> host_offsets;
+  bool tc_used = false;  // the tensor-core engine ran since the last error check
 
   size_t bytes_per_token() const { return format == kFormatInt4 ? dim / 2 : dim / 8; }
   int64_t resident_bytes() const {
@@ -148,7 +149,8 @@ struct msb_docs {
 
 namespace {
 
-cudaStream_t pick_stream(msb_docs* h, void* s) { return s ? static_cast<cudaStream_t>(s) : h->stream; }
+// Device entry points run on the caller's stream as given (NULL = the legacy default stream).
+cudaStream_t pick_stream(msb_docs*, void* s) { return static_cast<cudaStream_t>(s); }
 
 struct Resolved {
   DocsView docs;
@@ -179,6 +181,7 @@ Resolved resolve(msb_docs* h, const msb_score_opts* o, int batch, int qtok, cons
   DocsView& d = r.docs;
   d.codes = h->codes.as<uint8_t>();
   d.offsets = h->offsets.as<int64_t>();
+  d.host_offsets = h->host_offsets.data();
   d.num_docs = h->num_docs;
   d.num_tokens = h->num_tokens;
   d.dim = h->dim;
@@ -255,9 +258,22 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
     const size_t ws = tc_scan_workspace_bytes(r.docs, qv, tg);
     h->w_tc.ensure(ws > 0 ? ws : 16, "cudaMalloc tensor-core scan workspace");
     launch_tc_scan(r.docs, qv, r.red, tg, d_out, h->w_tc.ptr, h->w_tc.cap, stream);
+    h->tc_used = true;
     return;
   }
   launch_simt_scan(r.docs, qv, r.red, tg, r.residual, d_out, stream);
+}
+
+// After a synchronising host-buffer call: surface a bounded-wait timeout of the
+// tensor-core kernel (its first 4 workspace bytes) as a CUDA error.
+void check_tc_flag(msb_docs* h, cudaStream_t s) {
+  if (!h->tc_used) return;
+  h->tc_used = false;
+  int flag = 0;
+  check(cudaMemcpyAsync(&flag, h->w_tc.ptr, sizeof(int), cudaMemcpyDeviceToHost, s), "read tc error flag");
+  check(cudaStreamSynchronize(s), "synchronize tc error flag");
+  if (flag != 0)
+    throw CudaFailure("tensor-core scan aborted: a pipeline wait timed out (code " + std::to_string(flag) + ")");
 }
 
 void check_query(msb_docs* h, const void* q, int batch, int qtok) {
@@ -564,6 +580,7 @@ int msb_docs_score(msb_docs* h, const float* query, int32_t batch, int32_t qtok,
     run_scan(h, r, d_q, batch, qtok, tg, h->w_scores.as<float>(), s);
     check(cudaMemcpyAsync(out, h->w_scores.ptr, obytes, cudaMemcpyDeviceToHost, s), "copy output to host");
     check(cudaStreamSynchronize(s), "synchronize scoring");
+    check_tc_flag(h, s);
   });
 }
 
@@ -594,6 +611,7 @@ int msb_docs_topk(msb_docs* h, const float* query, int32_t batch, int32_t qtok, 
                           cudaMemcpyDeviceToHost, s),
           "copy top indices to host");
     check(cudaStreamSynchronize(s), "synchronize top-k");
+    check_tc_flag(h, s);
   });
 }
 
@@ -651,6 +669,7 @@ int msb_docs_cascade_topk(msb_docs* h, const float* query, int32_t batch, int32_
     check(cudaMemcpyAsync(out_ids, h->w_top_i.ptr, sizeof(int64_t) * B * k, cudaMemcpyDeviceToHost, s),
           "copy cascade indices to host");
     check(cudaStreamSynchronize(s), "synchronize cascade");
+    check_tc_flag(h, s);
   });
 }
 

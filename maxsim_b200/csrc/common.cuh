@@ -48,6 +48,7 @@ struct DocsView {
   const float* token_scale2;   // residual token scales [N]
   const int64_t* offsets;      // [D + 1]
   const float* doc_scale;      // [D] or nullptr (binary scale vector)
+  const int64_t* host_offsets;  // host copy of offsets (work partitioning)
   int64_t num_docs;
   int64_t num_tokens;
   int dim;

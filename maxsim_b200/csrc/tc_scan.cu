@@ -1,11 +1,652 @@
-// Tensor-core (tcgen05) scan engine -- placeholder until the sm_100a kernel lands.
+// Tensor-core (tcgen05) MaxSim scan for dim-128 corpora, int8 queries.
+//
+// D[query row, token] = sum_k A[row, k] * B[token, k] runs on the 5th-gen
+// tensor cores (tcgen05.mma kind::i8, int32 accumulators in TMEM); the
+// CUDA cores do the part the tensor core cannot: per-token scale before the
+// maximum, the segmented (per document) maximum over ragged token ranges, and
+// the sum over a query's rows.  Semantics are the reference kernel's
+// (cpp/maxsim/cuda_extension.cu:1507-1627): exact int32 dot, fl(float(dot) *
+// s_t), maximum per query row, doc += fl(best * qscale) in row order, * scale.
+//
+// Layout of the work
+//   * A query tile is 128 TMEM lanes = floor(128 / Q) whole queries (Q rows
+//     each); query rows are int8, K permuted to the nibble order of the codes.
+//   * A work unit is (query tile, contiguous document range of ~W tokens);
+//     units are ordered range-major so the CTAs working on the query tiles of
+//     one range run together and share its codes through L2.
+//   * Persistent CTAs; each owns TMEM for two accumulators of TILE_N columns.
+//   * Warp roles: warps 0-3 epilogue (warp w reads TMEM lanes 32w..32w+31),
+//     warp 4 TMEM allocation + MMA issue (one thread), warps 5-8 producers.
+//   * Producers load 64-byte int4 rows with 16-byte vector loads, expand each
+//     nibble to a signed byte holding (code + 8) in [1, 15] (one LOP3 per 4
+//     values), and store the tile in the no-swizzle K-major UMMA layout
+//     (8x16-byte core matrices).  The +8 offset is removed exactly in the
+//     epilogue: dot(q, code) = acc - 8 * sum(q).
+//   * The epilogue converts acc to float with an exact integer-bias trick
+//     (|dot| < 2^22), multiplies by the token scale, and reduces with
+//     three-input max.  Document ends inside a tile come from a per-tile
+//     segment list the producers write next to the tile.
+// Every mbarrier wait is bounded (%globaltimer); on timeout the kernel raises
+// an error flag, drains, frees its TMEM and returns.
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
 #include "common.cuh"
 
 namespace msb {
-bool tc_scan_supported(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, bool) { return false; }
-size_t tc_scan_workspace_bytes(const DocsView&, const QueryView&, const TargetsView&) { return 0; }
-void launch_tc_scan(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, float*, void*, size_t,
-                    cudaStream_t) {
-  throw NotSupported("tensor-core scan engine not built");
+namespace tc {
+
+constexpr int kTileN = 128;       // tokens per tile (MMA N)
+constexpr int kStages = 4;        // smem ring depth
+constexpr int kAccBufs = 2;       // TMEM accumulators
+constexpr int kEpiWarps = 4;
+constexpr int kProdWarps = 4;
+constexpr int kMmaWarp = kEpiWarps;
+constexpr int kThreads = (kEpiWarps + 1 + kProdWarps) * 32;  // 288
+constexpr int kSegGroup = 8;      // finalised documents per epilogue flush
+constexpr uint32_t kTmemCols = kAccBufs * kTileN;             // 256
+constexpr uint64_t kTimeoutNs = 4000000000ull;                // 4 s per wait
+
+struct Unit {
+  int64_t d_lo, d_hi;    // documents [d_lo, d_hi)
+  int64_t tok_lo, tok_hi;
+  int32_t qtile;
+  int32_t pad;
+};
+
+struct Params {
+  const uint8_t* codes;
+  const float* token_scale;   // nullptr: tensor scale (integer maximum)
+  const int64_t* offsets;
+  const int32_t* qwords;      // [B*Q, 32] nibble-order int8 words
+  const float* qscale;        // [B*Q]
+  const int32_t* qsum;        // [B*Q]
+  const Unit* units;
+  int num_units;
+  int batch;
+  int qtok;
+  int qpt;                    // queries per tile
+  float scale;                // tensor scale applied to the document score
+  int64_t num_docs;           // output row stride
+  float* out;                 // [B, num_docs]
+  int* error;                 // set to a non-zero code on timeout
+};
+
+// Shared-memory layout (bytes).
+constexpr int kATileBytes = 128 * 128;                 // 16 KB
+constexpr int kBTileBytes = kTileN * 128;              // 16 KB
+struct StageMeta {
+  float scale[kTileN];
+  int16_t seg_end[kTileN];   // exclusive end column of each document ending in the tile
+  int32_t seg_doc[kTileN];
+  int32_t nseg;
+  int32_t valid;             // valid columns
+};
+constexpr int kMetaBytes = ((sizeof(StageMeta) + 127) / 128) * 128;
+constexpr int kOffA = 0;
+constexpr int kOffB = kOffA + 2 * kATileBytes;
+constexpr int kOffMeta = kOffB + kStages * kBTileBytes;
+constexpr int kOffRow = kOffMeta + kStages * kMetaBytes;
+constexpr int kRowBytes = kSegGroup * 128 * 4;
+constexpr int kOffBar = kOffRow + kRowBytes + 128 + 64;  // + per-group doc ids
+constexpr int kNumBars = 2 * kStages + 2 * kAccBufs + 4;
+constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 64 + 1024;  // + alignment slack
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: false on timeout (after raising the error flag and abort bit).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int code) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 63u) == 63u) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > kTimeoutNs) {
+        *abort_flag = 1;
+        atomicExch(err, code);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void named_bar(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  // K-major, no swizzle: 8-row x 16-byte core matrices; LBO between core
+  // matrices along K, SBO between 8-row groups; version 1 (bits 46-47).
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Byte offset of (row, 16-byte K chunk) in a no-swizzle K-major tile of 128-byte rows.
+__device__ __forceinline__ uint32_t tile_off(int row, int kchunk) {
+  return static_cast<uint32_t>((row >> 3) * 1024 + kchunk * 128 + (row & 7) * 16);
+}
+
+// ---------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------
+template <bool kTokenScale>
+__global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                         ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* full = bars;                         // [kStages] producers -> MMA
+  uint64_t* empty = bars + kStages;              // [kStages] MMA commit + epilogue -> producers
+  uint64_t* acc_full = bars + 2 * kStages;       // [kAccBufs] MMA -> epilogue
+  uint64_t* acc_empty = acc_full + kAccBufs;     // [kAccBufs] epilogue -> MMA
+  uint64_t* a_full = acc_empty + kAccBufs;       // [2] producers -> MMA
+  uint64_t* a_empty = a_full + 2;                // [2] MMA commit -> producers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* rowval = reinterpret_cast<float*>(smem + kOffRow);            // [kSegGroup][128]
+  int32_t* group_doc = reinterpret_cast<int32_t*>(smem + kOffRow + kRowBytes);  // [kSegGroup]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int Q = p.qtok;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], kProdWarps);
+      mbar_init(&empty[s], 1 + kEpiWarps);
+    }
+    for (int a = 0; a < kAccBufs; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], kEpiWarps);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&a_full[a], kProdWarps);
+      mbar_init(&a_empty[a], 1);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp > kMmaWarp) {
+    // =================== producers ===================
+    const int ptid = threadIdx.x - (kMmaWarp + 1) * 32;  // 0..127
+    const int pwarp = warp - (kMmaWarp + 1);
+    int stage = 0;
+    uint32_t phase = 0;
+    int iter = 0;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
+      const Unit unit = p.units[u];
+      // ---- query tile (A operand) ----
+      const int abuf = iter & 1;
+      if (iter >= 2 && !mbar_wait(&a_empty[abuf], ((iter >> 1) - 1) & 1, abort_flag, p.error, 11)) goto done;
+      {
+        unsigned char* A = smem + kOffA + abuf * kATileBytes;
+        const int row = ptid;  // one query row per producer thread
+        const int b = unit.qtile * p.qpt + row / Q;
+        const bool valid = row < p.qpt * Q && b < p.batch;
+        const int4* src = reinterpret_cast<const int4*>(p.qwords + (static_cast<int64_t>(b) * Q + row % Q) * 32);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          int4 v = valid ? __ldg(src + c) : make_int4(0, 0, 0, 0);
+          *reinterpret_cast<int4*>(A + tile_off(row, c)) = v;
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[abuf]);
+      }
+      // ---- token tiles ----
+      int64_t next_doc = unit.d_lo;  // first document whose end has not been passed
+      for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.error, 12)) goto done;
+        unsigned char* Bt = smem + kOffB + stage * kBTileBytes;
+        StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kOffMeta + stage * kMetaBytes);
+        const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
+        {
+          const int r = ptid;  // one token per producer thread
+          if (r < valid) {
+            const int4* src = reinterpret_cast<const int4*>(p.codes + (t0 + r) * 64);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const int4 v = __ldg(src + c);
+              const uint32_t w[4] = {static_cast<uint32_t>(v.x), static_cast<uint32_t>(v.y),
+                                     static_cast<uint32_t>(v.z), static_cast<uint32_t>(v.w)};
+              uint32_t o[8];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint32_t x = w[i] ^ 0x88888888u;  // two's-complement nibble -> code + 8
+                o[2 * i] = x & 0x0F0F0F0Fu;             // even dims (low nibbles)
+                o[2 * i + 1] = (x >> 4) & 0x0F0F0F0Fu;  // odd dims (high nibbles)
+              }
+              *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
+              *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+            }
+            meta->scale[r] = kTokenScale ? __ldg(p.token_scale + t0 + r) : 1.0F;
+          }
+        }
+        // Documents ending inside (t0, t0 + valid]: producer warp 0 walks the offsets.
+        if (pwarp == 0) {
+          int nseg = 0;
+          const int64_t tile_end = t0 + valid;
+          while (true) {
+            const int64_t d = next_doc + lane;
+            const bool in = d < unit.d_hi;
+            const int64_t e = in ? __ldg(p.offsets + d + 1) : INT64_MAX;
+            const int64_t s = in ? __ldg(p.offsets + d) : INT64_MAX;
+            const bool ends = in && e <= tile_end;
+            const bool nonempty = ends && e > s;
+            const uint32_t end_mask = __ballot_sync(0xFFFFFFFFu, ends);
+            const uint32_t ne_mask = __ballot_sync(0xFFFFFFFFu, nonempty);
+            if (nonempty) {
+              const int slot = nseg + __popc(ne_mask & ((1u << lane) - 1u));
+              meta->seg_end[slot] = static_cast<int16_t>(e - t0);
+              meta->seg_doc[slot] = static_cast<int32_t>(d);
+            }
+            nseg += __popc(ne_mask);
+            const int consumed = __popc(end_mask);  // ends are monotone: a prefix of the lanes
+            next_doc += consumed;
+            if (consumed < 32) break;
+          }
+          if (lane == 0) {
+            meta->nseg = nseg;
+            meta->valid = valid;
+          }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[stage]);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // =================== MMA issuer ===================
+    constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kTileN >> 3) << 17) |
+                               (static_cast<uint32_t>(128 >> 4) << 24);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int iter = 0;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
+      const Unit unit = p.units[u];
+      const int abuf = iter & 1;
+      if (!mbar_wait(&a_full[abuf], (iter >> 1) & 1, abort_flag, p.error, 21)) goto done;
+      const uint32_t a_addr = smem_u32(smem + kOffA + abuf * kATileBytes);
+      for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, p.error, 22)) goto done;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.error, 23)) goto done;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t b_addr = smem_u32(smem + kOffB + stage * kBTileBytes);
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTileN);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = umma_desc(a_addr + 256u * k, 128u, 1024u);
+            const uint64_t bd = umma_desc(b_addr + 256u * k, 128u, 1024u);
+            mma_i8(d_tmem, ad, bd, idesc, k > 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          mma_commit(&acc_full[acc]);
+        }
+        __syncwarp();
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+        if (++acc == kAccBufs) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (lane == 0) mma_commit(&a_empty[abuf]);
+      __syncwarp();
+    }
+  } else {
+    // =================== epilogue (warps 0-3, TMEM lanes 32w..32w+31) ===================
+    const int row = threadIdx.x;  // 0..127 = TMEM lane = query-tile row
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+      const Unit unit = p.units[u];
+      const int qi = row / Q;                       // query within the tile
+      const int b = unit.qtile * p.qpt + qi;
+      const bool row_valid = row < p.qpt * Q && b < p.batch;
+      const int64_t grow = static_cast<int64_t>(b) * Q + row % Q;
+      const float qs = row_valid ? __ldg(p.qscale + grow) : 0.0F;
+      // acc + bias reinterpreted as float is 1.5 * 2^23 + dot exactly (|dot| < 2^22).
+      const int32_t bias = row_valid ? 0x4B400000 - 8 * __ldg(p.qsum + grow) : 0x4B400000;
+      const int n_queries = min(p.qpt, p.batch - unit.qtile * p.qpt);
+      float run = kLowest;       // running maximum of the open document (scaled)
+      int32_t run_i = INT32_MIN;  // tensor-scale variant: integer maximum of acc
+      int pending = 0;            // documents waiting in rowval
+      for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
+        if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.error, 31)) goto done;
+        // The stage's producer phase is complete and cannot advance before this
+        // warp releases the stage; waiting on it acquires the metadata writes.
+        if (!mbar_wait(&full[stage], phase, abort_flag, p.error, 32)) goto done;
+        tc_fence_after();
+        const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + kOffMeta + stage * kMetaBytes);
+        const int valid = meta->valid;
+        const int nseg = meta->nseg;
+        int seg = 0;
+        int next_end = nseg > 0 ? meta->seg_end[0] : 1 << 30;
+        for (int c0 = 0; c0 < valid; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + lane_base + static_cast<uint32_t>(acc * kTileN + c0), r);
+          const int cend = min(c0 + 32, valid);
+          if (next_end > c0 + 32 && cend == c0 + 32) {
+            // fast path: 32 columns of one open document
+            if (kTokenScale) {
+              float v[32];
+              const float4* sc4 = reinterpret_cast<const float4*>(meta->scale + c0);
+#pragma unroll
+              for (int j4 = 0; j4 < 8; ++j4) {
+                const float4 s4 = sc4[j4];
+                const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int j = 4 * j4 + e;
+                  v[j] = __fmul_rn(__fadd_rn(__int_as_float(static_cast<int32_t>(r[j]) + bias), -12582912.0F), sv[e]);
+                }
+              }
+              float m = run;
+#pragma unroll
+              for (int j = 0; j < 32; j += 2) m = fmax3(m, v[j], v[j + 1]);
+              run = m;
+            } else {
+              int32_t m = run_i;
+#pragma unroll
+              for (int j = 0; j < 32; j += 2) m = __vimax3_s32(m, static_cast<int32_t>(r[j]), static_cast<int32_t>(r[j + 1]));
+              run_i = m;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int col = c0 + j;
+              if (col < cend) {
+                if (kTokenScale) {
+                  const float v = __fmul_rn(__fadd_rn(__int_as_float(static_cast<int32_t>(r[j]) + bias), -12582912.0F),
+                                            meta->scale[col]);
+                  run = fmaxf(run, v);
+                } else {
+                  run_i = max(run_i, static_cast<int32_t>(r[j]));
+                }
+                if (col + 1 == next_end) {
+                  // document ends here: stage its per-row value
+                  float best;
+                  if (kTokenScale) {
+                    best = run;
+                  } else {
+                    best = __fadd_rn(__int_as_float(run_i + bias), -12582912.0F);
+                  }
+                  rowval[pending * 128 + row] = row_valid ? __fmul_rn(best, qs) : 0.0F;
+                  if (row == 0) group_doc[pending] = meta->seg_doc[seg];
+                  run = kLowest;
+                  run_i = INT32_MIN;
+                  ++seg;
+                  next_end = seg < nseg ? meta->seg_end[seg] : 1 << 30;
+                  if (++pending == kSegGroup) {
+                    named_bar(1, kEpiWarps * 32);
+                    for (int x = row; x < pending * n_queries; x += kEpiWarps * 32) {
+                      const int g = x / n_queries, qq = x % n_queries;
+                      float sacc = 0.0F;
+                      for (int k = 0; k < Q; ++k) sacc = __fadd_rn(sacc, rowval[g * 128 + qq * Q + k]);
+                      p.out[static_cast<int64_t>(unit.qtile * p.qpt + qq) * p.num_docs + group_doc[g]] =
+                          __fmul_rn(sacc, p.scale);
+                    }
+                    named_bar(1, kEpiWarps * 32);
+                    pending = 0;
+                  }
+                }
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&acc_empty[acc]);
+          mbar_arrive(&empty[stage]);
+        }
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+        if (++acc == kAccBufs) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // flush the unit's remaining finished documents
+      named_bar(1, kEpiWarps * 32);
+      for (int x = row; x < pending * n_queries; x += kEpiWarps * 32) {
+        const int g = x / n_queries, qq = x % n_queries;
+        float sacc = 0.0F;
+        for (int k = 0; k < Q; ++k) sacc = __fadd_rn(sacc, rowval[g * 128 + qq * Q + k]);
+        p.out[static_cast<int64_t>(unit.qtile * p.qpt + qq) * p.num_docs + group_doc[g]] = __fmul_rn(sacc, p.scale);
+      }
+      named_bar(1, kEpiWarps * 32);
+    }
+  }
+done:
+  // Drain: the MMA warp waits (bounded) until its last commit has landed so
+  // no tensor-core operation still targets TMEM when it is released.
+  if (warp == kMmaWarp && *abort_flag) {
+    // on abort, outstanding MMAs finish on their own; give them time to land
+    const uint64_t t0 = global_ns();
+    while (global_ns() - t0 < 1000000ull) {
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+}  // namespace tc
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+namespace {
+
+struct TcPlan {
+  int qpt;
+  int n_qtiles;
+  int64_t range_tokens;
+};
+
+TcPlan plan_for(const DocsView& d, const QueryView& q) {
+  TcPlan pl{};
+  pl.qpt = 128 / q.qtok;
+  pl.n_qtiles = (q.batch + pl.qpt - 1) / pl.qpt;
+  // ~4 units per CTA slot, at least 8 tiles per range.
+  const int64_t slots = 148LL * 4;
+  int64_t w = (d.num_tokens * pl.n_qtiles + slots - 1) / slots;
+  w = std::max<int64_t>(w, 8 * tc::kTileN);
+  pl.range_tokens = ((w + tc::kTileN - 1) / tc::kTileN) * tc::kTileN;
+  return pl;
+}
+
+}  // namespace
+
+bool tc_scan_supported(const DocsView& d, const QueryView& q, const ReduceView& r, const TargetsView& tg,
+                       bool residual) {
+  return !residual && d.format == kFormatInt4 && d.dim == 128 && q.mode == kQueryI8 && r.reducer == kMaxSim &&
+         tg.ids == nullptr && q.qtok >= 1 && q.qtok <= 128 && q.batch >= 1 && d.num_docs <= 0x7FFFFFFF &&
+         d.host_offsets != nullptr;
+}
+
+size_t tc_scan_workspace_bytes(const DocsView& d, const QueryView& q, const TargetsView&) {
+  const TcPlan pl = plan_for(d, q);
+  const int64_t max_ranges = d.num_docs + (d.num_tokens / pl.range_tokens) + 2;
+  return 256 + sizeof(tc::Unit) * static_cast<size_t>(max_ranges) * pl.n_qtiles;
+}
+
+struct UnitCacheKey {
+  const void* ws;
+  const int64_t* offsets;
+  int64_t num_docs, num_tokens, range_tokens;
+  int n_qtiles;
+  bool operator==(const UnitCacheKey& o) const {
+    return ws == o.ws && offsets == o.offsets && num_docs == o.num_docs && num_tokens == o.num_tokens &&
+           range_tokens == o.range_tokens && n_qtiles == o.n_qtiles;
+  }
+};
+
+void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, const TargetsView&, float* out, void* ws,
+                    size_t ws_bytes, cudaStream_t stream) {
+  // The unit table depends only on the corpus and the query tiling; it is
+  // built once per (workspace, corpus, tiling) and kept in the workspace.
+  static std::mutex cache_mu;
+  static std::vector<std::pair<UnitCacheKey, int>> cache;  // key -> number of units
+  const TcPlan pl = plan_for(d, q);
+  const UnitCacheKey key{ws, d.offsets, d.num_docs, d.num_tokens, pl.range_tokens, pl.n_qtiles};
+  int* err = static_cast<int*>(ws);
+  tc::Unit* d_units = reinterpret_cast<tc::Unit*>(static_cast<unsigned char*>(ws) + 256);
+  int num_units = -1;
+  {
+    std::lock_guard<std::mutex> lock(cache_mu);
+    for (auto& e : cache)
+      if (e.first == key) num_units = e.second;
+  }
+  // Empty documents never appear in a tile; their score is 0.
+  check(cudaMemsetAsync(out, 0, sizeof(float) * static_cast<size_t>(q.batch) * d.num_docs, stream), "zero scores");
+  if (num_units < 0) {
+    // Document ranges of ~range_tokens tokens (host offsets), range-major units.
+    std::vector<tc::Unit> units;
+    const int64_t* off = d.host_offsets;
+    int64_t lo = 0;
+    while (lo < d.num_docs) {
+      const int64_t target = off[lo] + pl.range_tokens;
+      const int64_t* it = std::lower_bound(off + lo + 1, off + d.num_docs + 1, target);
+      int64_t hi = static_cast<int64_t>(it - off);
+      if (hi > d.num_docs) hi = d.num_docs;
+      if (hi <= lo) hi = lo + 1;
+      if (off[hi] > off[lo])
+        for (int t = 0; t < pl.n_qtiles; ++t) units.push_back(tc::Unit{lo, hi, off[lo], off[hi], t, 0});
+      lo = hi;
+    }
+    const size_t need = 256 + sizeof(tc::Unit) * units.size();
+    if (need > ws_bytes) throw CudaFailure("tensor-core scan workspace too small");
+    if (!units.empty()) {
+      check(cudaMemcpyAsync(d_units, units.data(), sizeof(tc::Unit) * units.size(), cudaMemcpyHostToDevice, stream),
+            "upload tc work units");
+      check(cudaStreamSynchronize(stream), "synchronize tc unit upload");
+    }
+    num_units = static_cast<int>(units.size());
+    std::lock_guard<std::mutex> lock(cache_mu);
+    for (auto it = cache.begin(); it != cache.end();)
+      it = it->first.ws == ws ? cache.erase(it) : it + 1;
+    cache.emplace_back(key, num_units);
+  }
+  if (num_units == 0) return;
+  check(cudaMemsetAsync(err, 0, sizeof(int), stream), "clear tc error flag");
+  tc::Params prm{};
+  prm.codes = d.codes;
+  prm.token_scale = d.token_scale;
+  prm.offsets = d.offsets;
+  prm.qwords = q.i8_words;
+  prm.qscale = q.row_scale;
+  prm.qsum = q.row_sum;
+  prm.units = d_units;
+  prm.num_units = num_units;
+  prm.batch = q.batch;
+  prm.qtok = q.qtok;
+  prm.qpt = pl.qpt;
+  prm.scale = d.scale;
+  prm.num_docs = d.num_docs;
+  prm.out = out;
+  prm.error = err;
+  int dev = 0, sms = 0;
+  check(cudaGetDevice(&dev), "get device");
+  check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "query SM count");
+  const int grid = std::min<int>(sms, prm.num_units);
+  if (d.token_scale) {
+    check(cudaFuncSetAttribute(tc::tc_scan_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes),
+          "set tc smem");
+    tc::tc_scan_kernel<true><<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(prm);
+  } else {
+    check(cudaFuncSetAttribute(tc::tc_scan_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes),
+          "set tc smem");
+    tc::tc_scan_kernel<false><<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(prm);
+  }
+  count_launch();
+  check(cudaGetLastError(), "launch tensor-core scan kernel");
+}
+
 }  // namespace msb
