@@ -37,6 +37,10 @@ static thread_local std::string g_last_error;
 
 namespace {
 
+// Extra bytes after offsets and token scales: the tensor-core engine copies
+// 16-byte-aligned supersets of these arrays with the bulk-copy engine.
+constexpr size_t kTailPad = 64;
+
 struct DeviceBuf {
   void* ptr = nullptr;
   size_t cap = 0;
@@ -389,7 +393,7 @@ int msb_docs_create(int32_t format, int32_t dim, const uint8_t* codes, int64_t n
         check(cudaMemcpyAsync(h->codes.ptr, codes, cbytes, cudaMemcpyHostToDevice, h->stream),
               "copy packed docs to device");
       }
-      h->offsets.ensure(sizeof(int64_t) * (num_docs + 1), "cudaMalloc offsets");
+      h->offsets.ensure(sizeof(int64_t) * (num_docs + 1) + kTailPad, "cudaMalloc offsets");
       check(cudaMemcpyAsync(h->offsets.ptr, offsets, sizeof(int64_t) * (num_docs + 1), cudaMemcpyHostToDevice,
                             h->stream),
             "copy offsets to device");
@@ -418,7 +422,7 @@ int msb_docs_create_device(int32_t format, int32_t dim, const uint8_t* codes, in
         h->codes.ensure(cbytes, "cudaMalloc packed docs");
         check(cudaMemcpyAsync(h->codes.ptr, codes, cbytes, cudaMemcpyDeviceToDevice, h->stream), "copy packed docs");
       }
-      h->offsets.ensure(sizeof(int64_t) * (num_docs + 1), "cudaMalloc offsets");
+      h->offsets.ensure(sizeof(int64_t) * (num_docs + 1) + kTailPad, "cudaMalloc offsets");
       const void* src = offsets_device ? static_cast<const void*>(offsets_device) : offsets_host;
       check(cudaMemcpyAsync(h->offsets.ptr, src, sizeof(int64_t) * (num_docs + 1), cudaMemcpyDefault, h->stream),
             "copy offsets");
@@ -464,7 +468,7 @@ int msb_docs_set_token_scales(msb_docs* h, const float* scales, int64_t count, i
           throw InvalidArgument("token scales must be finite and > 0");
     DeviceGuard g(h->device);
     const size_t bytes = sizeof(float) * static_cast<size_t>(count);
-    h->token_scale.ensure(bytes > 0 ? bytes : 4, "cudaMalloc resident token scale vector");
+    h->token_scale.ensure(bytes + kTailPad, "cudaMalloc resident token scale vector");
     if (bytes) {
       check(cudaMemcpyAsync(h->token_scale.ptr, scales, bytes, cudaMemcpyHostToDevice, h->stream),
             "copy token scale vector to device");
@@ -480,7 +484,7 @@ int msb_docs_set_token_scales_device(msb_docs* h, const float* scales, int64_t c
     if (count != h->num_tokens) throw InvalidArgument("token scale vector must have shape [num_doc_tokens]");
     DeviceGuard g(h->device);
     const size_t bytes = sizeof(float) * static_cast<size_t>(count);
-    h->token_scale.ensure(bytes > 0 ? bytes : 4, "cudaMalloc resident token scale vector");
+    h->token_scale.ensure(bytes + kTailPad, "cudaMalloc resident token scale vector");
     if (bytes) {
       check(cudaMemcpyAsync(h->token_scale.ptr, scales, bytes, cudaMemcpyDeviceToDevice, h->stream),
             "copy token scale vector");

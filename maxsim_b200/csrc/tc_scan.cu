@@ -38,18 +38,22 @@ namespace msb {
 namespace tc {
 
 constexpr int kTileN = 128;       // tokens per tile (MMA N)
-constexpr int kStages = 4;        // smem ring depth
+constexpr int kStages = 4;        // expanded-tile ring (B operand + tile metadata)
+constexpr int kRaw = 6;           // raw-code ring filled by bulk copies
 constexpr int kAccBufs = 2;       // TMEM accumulators
-constexpr int kEpiWarps = 4;
-constexpr int kProdWarps = 4;
-constexpr int kMmaWarp = kEpiWarps;
-constexpr int kThreads = (kEpiWarps + 1 + kProdWarps) * 32;  // 288
-constexpr int kSegGroup = 8;      // finalised documents per epilogue flush
+constexpr int kEpiWarps = 8;      // two per TMEM lane quarter, each owning 64 of a tile's columns
+constexpr int kXWarps = 4;        // expanders
+constexpr int kMmaWarp = kEpiWarps;            // warp 8
+constexpr int kXWarp0 = kMmaWarp + 1;          // warps 9..12
+constexpr int kLoadWarp = kXWarp0 + kXWarps;   // warp 13
+constexpr int kThreads = (kLoadWarp + 1) * 32; // 448
+constexpr int kSegGroup = 8;      // finished documents per epilogue flush
+constexpr int kMaxRangeDocs = 1024;
 constexpr uint32_t kTmemCols = kAccBufs * kTileN;             // 256
 constexpr uint64_t kTimeoutNs = 4000000000ull;                // 4 s per wait
 
 struct Unit {
-  int64_t d_lo, d_hi;    // documents [d_lo, d_hi)
+  int64_t d_lo, d_hi;    // documents [d_lo, d_hi), at most kMaxRangeDocs
   int64_t tok_lo, tok_hi;
   int32_t qtile;
   int32_t pad;
@@ -73,9 +77,13 @@ struct Params {
   int* error;                 // set to a non-zero code on timeout
 };
 
-// Shared-memory layout (bytes).
+// Shared-memory layout (bytes, from a 1024-aligned base).
 constexpr int kATileBytes = 128 * 128;                 // 16 KB
 constexpr int kBTileBytes = kTileN * 128;              // 16 KB
+constexpr int kRawCodeBytes = kTileN * 64;             // 8 KB
+constexpr int kRawScaleFloats = kTileN + 4;            // aligned superset of the tile's scales
+constexpr int kRawBytes = ((kRawCodeBytes + kRawScaleFloats * 4 + 127) / 128) * 128;
+constexpr int kUoffEntries = kMaxRangeDocs + 4;
 struct StageMeta {
   float scale[kTileN];
   int16_t seg_end[kTileN];   // exclusive end column of each document ending in the tile
@@ -86,12 +94,15 @@ struct StageMeta {
 constexpr int kMetaBytes = ((sizeof(StageMeta) + 127) / 128) * 128;
 constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + 2 * kATileBytes;
-constexpr int kOffMeta = kOffB + kStages * kBTileBytes;
-constexpr int kOffRow = kOffMeta + kStages * kMetaBytes;
-constexpr int kRowBytes = kSegGroup * 128 * 4;
-constexpr int kOffBar = kOffRow + kRowBytes + 128 + 64;  // + per-group doc ids
-constexpr int kNumBars = 2 * kStages + 2 * kAccBufs + 4;
+constexpr int kOffRaw = kOffB + kStages * kBTileBytes;
+constexpr int kOffMeta = kOffRaw + kRaw * kRawBytes;
+constexpr int kOffUoff = kOffMeta + kStages * kMetaBytes;
+constexpr int kOffRow = kOffUoff + 2 * kUoffEntries * 8;
+constexpr int kRowBytes = kSegGroup * 2 * 128 * 4;     // [group][half][row]
+constexpr int kOffBar = kOffRow + kRowBytes + 128;     // + per-group doc ids
+constexpr int kNumBars = 2 * kStages + 2 * kRaw + 2 * kAccBufs + 4 + 4;
 constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 64 + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 // ---------------------------------------------------------------------------
 // PTX wrappers
@@ -182,24 +193,63 @@ __device__ __forceinline__ uint32_t tile_off(int row, int kchunk) {
   return static_cast<uint32_t>((row >> 3) * 1024 + kchunk * 128 + (row & 7) * 16);
 }
 
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// 1D bulk copy global -> shared (TMA engine), completing transaction bytes on `bar`.
+// Both addresses 16-byte aligned, size a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
+struct Ring {
+  int idx = 0;
+  uint32_t phase = 0;
+  template <int N>
+  __device__ __forceinline__ void next() {
+    if (++idx == N) {
+      idx = 0;
+      phase ^= 1;
+    }
+  }
+};
+
 template <bool kTokenScale>
 __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                          ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* full = bars;                         // [kStages] producers -> MMA
-  uint64_t* empty = bars + kStages;              // [kStages] MMA commit + epilogue -> producers
-  uint64_t* acc_full = bars + 2 * kStages;       // [kAccBufs] MMA -> epilogue
+  uint64_t* full = bars;                         // [kStages]  expanders -> MMA (and epilogue metadata)
+  uint64_t* empty = full + kStages;              // [kStages]  MMA commit + epilogue -> expanders
+  uint64_t* raw_full = empty + kStages;          // [kRaw]     bulk copies -> expanders
+  uint64_t* raw_empty = raw_full + kRaw;         // [kRaw]     expanders -> loader
+  uint64_t* acc_full = raw_empty + kRaw;         // [kAccBufs] MMA -> epilogue
   uint64_t* acc_empty = acc_full + kAccBufs;     // [kAccBufs] epilogue -> MMA
-  uint64_t* a_full = acc_empty + kAccBufs;       // [2] producers -> MMA
-  uint64_t* a_empty = a_full + 2;                // [2] MMA commit -> producers
+  uint64_t* a_full = acc_empty + kAccBufs;       // [2]        expanders -> MMA
+  uint64_t* a_empty = a_full + 2;                // [2]        MMA commit -> expanders
+  uint64_t* u_full = a_empty + 2;                // [2]        unit offsets bulk copy -> segment warp
+  uint64_t* u_empty = u_full + 2;                // [2]        segment warp -> loader
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* rowval = reinterpret_cast<float*>(smem + kOffRow);            // [kSegGroup][128]
+  float* rowval = reinterpret_cast<float*>(smem + kOffRow);                      // [group][half][128]
   int32_t* group_doc = reinterpret_cast<int32_t*>(smem + kOffRow + kRowBytes);  // [kSegGroup]
 
   const int warp = threadIdx.x >> 5;
@@ -208,16 +258,22 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], kProdWarps);
+      mbar_init(&full[s], kXWarps);
       mbar_init(&empty[s], 1 + kEpiWarps);
+    }
+    for (int s = 0; s < kRaw; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], kXWarps);
     }
     for (int a = 0; a < kAccBufs; ++a) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], kEpiWarps);
     }
     for (int a = 0; a < 2; ++a) {
-      mbar_init(&a_full[a], kProdWarps);
+      mbar_init(&a_full[a], kXWarps);
       mbar_init(&a_empty[a], 1);
+      mbar_init(&u_full[a], 1);
+      mbar_init(&u_empty[a], 1);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -233,21 +289,51 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp > kMmaWarp) {
-    // =================== producers ===================
-    const int ptid = threadIdx.x - (kMmaWarp + 1) * 32;  // 0..127
-    const int pwarp = warp - (kMmaWarp + 1);
-    int stage = 0;
-    uint32_t phase = 0;
+  if (warp == kLoadWarp) {
+    // =================== loader: bulk copies run ahead of the expanders ===================
+    if (lane == 0) {
+      Ring raw;
+      int iter = 0;
+      for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
+        const Unit unit = p.units[u];
+        const int ub = iter & 1;
+        if (iter >= 2 && !mbar_wait(&u_empty[ub], ((iter >> 1) - 1) & 1, abort_flag, p.error, 41)) goto done;
+        {
+          // offsets[d_lo .. d_hi] as a 16-byte-aligned superset (the buffer is padded)
+          const int64_t first = unit.d_lo & ~1LL;
+          const int64_t count = ((unit.d_hi + 1 - first) + 1) & ~1LL;
+          const uint32_t bytes = static_cast<uint32_t>(count * 8);
+          mbar_expect_tx(&u_full[ub], bytes);
+          bulk_g2s(smem + kOffUoff + ub * kUoffEntries * 8, p.offsets + first, bytes, &u_full[ub]);
+        }
+        for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
+          if (!mbar_wait(&raw_empty[raw.idx], raw.phase ^ 1, abort_flag, p.error, 42)) goto done;
+          const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
+          unsigned char* rb = smem + kOffRaw + raw.idx * kRawBytes;
+          const uint32_t code_bytes = static_cast<uint32_t>(valid) * 64u;
+          uint32_t scale_bytes = 0;
+          const int64_t s_first = t0 & ~3LL;
+          if (kTokenScale) scale_bytes = static_cast<uint32_t>(((t0 + valid - s_first + 3) & ~3LL) * 4);
+          mbar_expect_tx(&raw_full[raw.idx], code_bytes + scale_bytes);
+          bulk_g2s(rb, p.codes + t0 * 64, code_bytes, &raw_full[raw.idx]);
+          if (kTokenScale) bulk_g2s(rb + kRawCodeBytes, p.token_scale + s_first, scale_bytes, &raw_full[raw.idx]);
+          raw.next<kRaw>();
+        }
+      }
+    }
+  } else if (warp >= kXWarp0) {
+    // =================== expanders: int4 -> (code + 8) bytes, UMMA layout ===================
+    const int xtid = threadIdx.x - kXWarp0 * 32;  // 0..127
+    const int xwarp = warp - kXWarp0;
+    Ring raw, stg;
     int iter = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
       const Unit unit = p.units[u];
-      // ---- query tile (A operand) ----
       const int abuf = iter & 1;
       if (iter >= 2 && !mbar_wait(&a_empty[abuf], ((iter >> 1) - 1) & 1, abort_flag, p.error, 11)) goto done;
       {
         unsigned char* A = smem + kOffA + abuf * kATileBytes;
-        const int row = ptid;  // one query row per producer thread
+        const int row = xtid;  // one query row per expander thread
         const int b = unit.qtile * p.qpt + row / Q;
         const bool valid = row < p.qpt * Q && b < p.batch;
         const int4* src = reinterpret_cast<const int4*>(p.qwords + (static_cast<int64_t>(b) * Q + row % Q) * 32);
@@ -260,44 +346,49 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[abuf]);
       }
-      // ---- token tiles ----
+      const int ub = iter & 1;
+      const int64_t* uoff = reinterpret_cast<const int64_t*>(smem + kOffUoff + ub * kUoffEntries * 8);
+      const int64_t ufirst = unit.d_lo & ~1LL;
+      if (xwarp == 0 && !mbar_wait(&u_full[ub], (iter >> 1) & 1, abort_flag, p.error, 13)) goto done;
       int64_t next_doc = unit.d_lo;  // first document whose end has not been passed
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
-        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.error, 12)) goto done;
-        unsigned char* Bt = smem + kOffB + stage * kBTileBytes;
-        StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kOffMeta + stage * kMetaBytes);
+        if (!mbar_wait(&raw_full[raw.idx], raw.phase, abort_flag, p.error, 14)) goto done;
+        if (!mbar_wait(&empty[stg.idx], stg.phase ^ 1, abort_flag, p.error, 12)) goto done;
+        const unsigned char* rb = smem + kOffRaw + raw.idx * kRawBytes;
+        unsigned char* Bt = smem + kOffB + stg.idx * kBTileBytes;
+        StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kOffMeta + stg.idx * kMetaBytes);
         const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
-        {
-          const int r = ptid;  // one token per producer thread
-          if (r < valid) {
-            const int4* src = reinterpret_cast<const int4*>(p.codes + (t0 + r) * 64);
+        const int r = xtid;  // one token per expander thread
+        if (r < valid) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const int4 v = __ldg(src + c);
-              const uint32_t w[4] = {static_cast<uint32_t>(v.x), static_cast<uint32_t>(v.y),
-                                     static_cast<uint32_t>(v.z), static_cast<uint32_t>(v.w)};
-              uint32_t o[8];
+          for (int step = 0; step < 4; ++step) {
+            const int c = (step + (r >> 1)) & 3;  // rotated chunk order: conflict-free shared loads
+            const uint4 v = *reinterpret_cast<const uint4*>(rb + r * 64 + c * 16);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            uint32_t o[8];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const uint32_t x = w[i] ^ 0x88888888u;  // two's-complement nibble -> code + 8
-                o[2 * i] = x & 0x0F0F0F0Fu;             // even dims (low nibbles)
-                o[2 * i + 1] = (x >> 4) & 0x0F0F0F0Fu;  // odd dims (high nibbles)
-              }
-              *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
-              *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t x = w[i] ^ 0x88888888u;  // two's-complement nibble -> code + 8
+              o[2 * i] = x & 0x0F0F0F0Fu;             // even dims (low nibbles)
+              o[2 * i + 1] = (x >> 4) & 0x0F0F0F0Fu;  // odd dims (high nibbles)
             }
-            meta->scale[r] = kTokenScale ? __ldg(p.token_scale + t0 + r) : 1.0F;
+            *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+          if (kTokenScale) {
+            const float* rs = reinterpret_cast<const float*>(rb + kRawCodeBytes);
+            meta->scale[r] = rs[(t0 & 3) + r];
           }
         }
-        // Documents ending inside (t0, t0 + valid]: producer warp 0 walks the offsets.
-        if (pwarp == 0) {
+        // Documents ending inside (t0, t0 + valid]: expander warp 0 walks the unit's offsets in smem.
+        if (xwarp == 0) {
           int nseg = 0;
           const int64_t tile_end = t0 + valid;
           while (true) {
             const int64_t d = next_doc + lane;
             const bool in = d < unit.d_hi;
-            const int64_t e = in ? __ldg(p.offsets + d + 1) : INT64_MAX;
-            const int64_t s = in ? __ldg(p.offsets + d) : INT64_MAX;
+            const int64_t e = in ? uoff[d + 1 - ufirst] : INT64_MAX;
+            const int64_t s = in ? uoff[d - ufirst] : INT64_MAX;
             const bool ends = in && e <= tile_end;
             const bool nonempty = ends && e > s;
             const uint32_t end_mask = __ballot_sync(0xFFFFFFFFu, ends);
@@ -319,21 +410,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
         }
         fence_proxy_async();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full[stage]);
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1;
+        if (lane == 0) {
+          mbar_arrive(&full[stg.idx]);
+          mbar_arrive(&raw_empty[raw.idx]);
         }
+        raw.next<kRaw>();
+        stg.next<kStages>();
       }
+      if (xwarp == 0 && lane == 0) mbar_arrive(&u_empty[ub]);
     }
   } else if (warp == kMmaWarp) {
     // =================== MMA issuer ===================
     constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kTileN >> 3) << 17) |
                                (static_cast<uint32_t>(128 >> 4) << 24);
-    int stage = 0;
-    uint32_t phase = 0;
-    int acc = 0;
-    uint32_t acc_phase = 0;
+    Ring stg, acc;
     int iter = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
       const Unit unit = p.units[u];
@@ -341,171 +431,170 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       if (!mbar_wait(&a_full[abuf], (iter >> 1) & 1, abort_flag, p.error, 21)) goto done;
       const uint32_t a_addr = smem_u32(smem + kOffA + abuf * kATileBytes);
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
-        if (!mbar_wait(&full[stage], phase, abort_flag, p.error, 22)) goto done;
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.error, 23)) goto done;
+        if (!mbar_wait(&full[stg.idx], stg.phase, abort_flag, p.error, 22)) goto done;
+        if (!mbar_wait(&acc_empty[acc.idx], acc.phase ^ 1, abort_flag, p.error, 23)) goto done;
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t b_addr = smem_u32(smem + kOffB + stage * kBTileBytes);
-          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTileN);
+          const uint32_t b_addr = smem_u32(smem + kOffB + stg.idx * kBTileBytes);
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc.idx * kTileN);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = umma_desc(a_addr + 256u * k, 128u, 1024u);
             const uint64_t bd = umma_desc(b_addr + 256u * k, 128u, 1024u);
             mma_i8(d_tmem, ad, bd, idesc, k > 0 ? 1u : 0u);
           }
-          mma_commit(&empty[stage]);
-          mma_commit(&acc_full[acc]);
+          mma_commit(&empty[stg.idx]);
+          mma_commit(&acc_full[acc.idx]);
         }
         __syncwarp();
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1;
-        }
-        if (++acc == kAccBufs) {
-          acc = 0;
-          acc_phase ^= 1;
-        }
+        stg.next<kStages>();
+        acc.next<kAccBufs>();
       }
       if (lane == 0) mma_commit(&a_empty[abuf]);
       __syncwarp();
     }
   } else {
-    // =================== epilogue (warps 0-3, TMEM lanes 32w..32w+31) ===================
-    const int row = threadIdx.x;  // 0..127 = TMEM lane = query-tile row
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    int stage = 0;
-    uint32_t phase = 0;
-    int acc = 0;
-    uint32_t acc_phase = 0;
+    // =================== epilogue: warps 0-7; lane quarter = warp % 4, column half = warp / 4 ===========
+    const int row = threadIdx.x & 127;            // TMEM lane = query-tile row
+    const int half = threadIdx.x >> 7;            // columns [64*half, 64*half + 64) of every tile
+    const int etid = threadIdx.x;                 // 0..255
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    Ring stg, acc;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
       const Unit unit = p.units[u];
-      const int qi = row / Q;                       // query within the tile
+      const int qi = row / Q;
       const int b = unit.qtile * p.qpt + qi;
       const bool row_valid = row < p.qpt * Q && b < p.batch;
       const int64_t grow = static_cast<int64_t>(b) * Q + row % Q;
-      const float qs = row_valid ? __ldg(p.qscale + grow) : 0.0F;
       // acc + bias reinterpreted as float is 1.5 * 2^23 + dot exactly (|dot| < 2^22).
       const int32_t bias = row_valid ? 0x4B400000 - 8 * __ldg(p.qsum + grow) : 0x4B400000;
+      const float qs = row_valid ? __ldg(p.qscale + grow) : 0.0F;
       const int n_queries = min(p.qpt, p.batch - unit.qtile * p.qpt);
-      float run = kLowest;       // running maximum of the open document (scaled)
+      float run = kLowest;        // running maximum of the open document over this half's columns
       int32_t run_i = INT32_MIN;  // tensor-scale variant: integer maximum of acc
-      int pending = 0;            // documents waiting in rowval
+      int pending = 0;
+      auto emit = [&](int32_t doc) {
+        float best;
+        if (kTokenScale) best = run;
+        else best = run_i == INT32_MIN ? kLowest : __fadd_rn(__int_as_float(run_i + bias), -12582912.0F);
+        // fl(max(a, b) * qs) == max(fl(a * qs), fl(b * qs)) for qs > 0, so halves are scaled first.
+        rowval[(pending * 2 + half) * 128 + row] = row_valid ? __fmul_rn(best, qs) : 0.0F;
+        if (etid == 0) group_doc[pending] = doc;
+        run = kLowest;
+        run_i = INT32_MIN;
+        if (++pending == kSegGroup) {
+          named_bar(1, kEpiWarps * 32);
+          for (int x = etid; x < pending * n_queries; x += kEpiWarps * 32) {
+            const int g = x / n_queries, qq = x % n_queries;
+            float sacc = 0.0F;
+            for (int k = 0; k < Q; ++k) {
+              const int rr = qq * Q + k;
+              sacc = __fadd_rn(sacc, fmaxf(rowval[(g * 2) * 128 + rr], rowval[(g * 2 + 1) * 128 + rr]));
+            }
+            p.out[static_cast<int64_t>(unit.qtile * p.qpt + qq) * p.num_docs + group_doc[g]] = __fmul_rn(sacc, p.scale);
+          }
+          named_bar(1, kEpiWarps * 32);
+          pending = 0;
+        }
+      };
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
-        if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.error, 31)) goto done;
-        // The stage's producer phase is complete and cannot advance before this
+        if (!mbar_wait(&acc_full[acc.idx], acc.phase, abort_flag, p.error, 31)) goto done;
+        // The stage's expander phase is complete and cannot advance before this
         // warp releases the stage; waiting on it acquires the metadata writes.
-        if (!mbar_wait(&full[stage], phase, abort_flag, p.error, 32)) goto done;
+        if (!mbar_wait(&full[stg.idx], stg.phase, abort_flag, p.error, 32)) goto done;
         tc_fence_after();
-        const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + kOffMeta + stage * kMetaBytes);
+        const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + kOffMeta + stg.idx * kMetaBytes);
         const int valid = meta->valid;
         const int nseg = meta->nseg;
-        int seg = 0;
-        int next_end = nseg > 0 ? meta->seg_end[0] : 1 << 30;
-        for (int c0 = 0; c0 < valid; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(tmem_base + lane_base + static_cast<uint32_t>(acc * kTileN + c0), r);
-          const int cend = min(c0 + 32, valid);
-          if (next_end > c0 + 32 && cend == c0 + 32) {
-            // fast path: 32 columns of one open document
-            if (kTokenScale) {
-              float v[32];
-              const float4* sc4 = reinterpret_cast<const float4*>(meta->scale + c0);
+        const int h0 = 64 * half;
+        const int h1 = min(h0 + 64, valid);
+        float v[64];
+        int32_t vi[64];
+        if (h1 > h0) {
+          uint32_t r[64];
+          const uint32_t taddr = tmem_base + lane_base + static_cast<uint32_t>(acc.idx * kTileN + h0);
+          tmem_ld32_nowait(taddr, r);
+          tmem_ld32_nowait(taddr + 32, r + 32);
+          tmem_wait_ld();
+          if (kTokenScale) {
+            const float4* sc4 = reinterpret_cast<const float4*>(meta->scale + h0);
 #pragma unroll
-              for (int j4 = 0; j4 < 8; ++j4) {
-                const float4 s4 = sc4[j4];
-                const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+            for (int j4 = 0; j4 < 16; ++j4) {
+              const float4 s4 = sc4[j4];
+              const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const int j = 4 * j4 + e;
-                  v[j] = __fmul_rn(__fadd_rn(__int_as_float(static_cast<int32_t>(r[j]) + bias), -12582912.0F), sv[e]);
-                }
+              for (int e = 0; e < 4; ++e) {
+                const int j = 4 * j4 + e;
+                v[j] = __fmul_rn(__fadd_rn(__int_as_float(static_cast<int32_t>(r[j]) + bias), -12582912.0F), sv[e]);
               }
-              float m = run;
-#pragma unroll
-              for (int j = 0; j < 32; j += 2) m = fmax3(m, v[j], v[j + 1]);
-              run = m;
-            } else {
-              int32_t m = run_i;
-#pragma unroll
-              for (int j = 0; j < 32; j += 2) m = __vimax3_s32(m, static_cast<int32_t>(r[j]), static_cast<int32_t>(r[j + 1]));
-              run_i = m;
             }
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int col = c0 + j;
-              if (col < cend) {
-                if (kTokenScale) {
-                  const float v = __fmul_rn(__fadd_rn(__int_as_float(static_cast<int32_t>(r[j]) + bias), -12582912.0F),
-                                            meta->scale[col]);
-                  run = fmaxf(run, v);
-                } else {
-                  run_i = max(run_i, static_cast<int32_t>(r[j]));
-                }
-                if (col + 1 == next_end) {
-                  // document ends here: stage its per-row value
-                  float best;
-                  if (kTokenScale) {
-                    best = run;
-                  } else {
-                    best = __fadd_rn(__int_as_float(run_i + bias), -12582912.0F);
-                  }
-                  rowval[pending * 128 + row] = row_valid ? __fmul_rn(best, qs) : 0.0F;
-                  if (row == 0) group_doc[pending] = meta->seg_doc[seg];
-                  run = kLowest;
-                  run_i = INT32_MIN;
-                  ++seg;
-                  next_end = seg < nseg ? meta->seg_end[seg] : 1 << 30;
-                  if (++pending == kSegGroup) {
-                    named_bar(1, kEpiWarps * 32);
-                    for (int x = row; x < pending * n_queries; x += kEpiWarps * 32) {
-                      const int g = x / n_queries, qq = x % n_queries;
-                      float sacc = 0.0F;
-                      for (int k = 0; k < Q; ++k) sacc = __fadd_rn(sacc, rowval[g * 128 + qq * Q + k]);
-                      p.out[static_cast<int64_t>(unit.qtile * p.qpt + qq) * p.num_docs + group_doc[g]] =
-                          __fmul_rn(sacc, p.scale);
-                    }
-                    named_bar(1, kEpiWarps * 32);
-                    pending = 0;
-                  }
-                }
+            for (int j = 0; j < 64; ++j) vi[j] = static_cast<int32_t>(r[j]);
+          }
+        }
+        // Walk the tile's document ends in order; every thread emits for every end.
+        int c = h0;  // next unprocessed column of this half
+        for (int sgi = 0; sgi <= nseg; ++sgi) {
+          const int e = sgi < nseg ? meta->seg_end[sgi] : h1;
+          const int a = c, bnd = min(e, h1);
+          if (bnd > a) {
+            if (a == h0 && bnd == h0 + 64) {
+              if (kTokenScale) {
+                float m = run;
+#pragma unroll
+                for (int j = 0; j < 64; j += 2) m = fmax3(m, v[j], v[j + 1]);
+                run = m;
+              } else {
+                int32_t m = run_i;
+#pragma unroll
+                for (int j = 0; j < 64; j += 2) m = __vimax3_s32(m, vi[j], vi[j + 1]);
+                run_i = m;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 64; ++j) {
+                const bool in = h0 + j >= a && h0 + j < bnd;
+                if (kTokenScale) run = in ? fmaxf(run, v[j]) : run;
+                else run_i = in ? max(run_i, vi[j]) : run_i;
               }
             }
+            c = bnd;
+          }
+          if (sgi < nseg) {
+            if (e > c) c = e;
+            emit(meta->seg_doc[sgi]);
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&acc_empty[acc]);
-          mbar_arrive(&empty[stage]);
+          mbar_arrive(&acc_empty[acc.idx]);
+          mbar_arrive(&empty[stg.idx]);
         }
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1;
-        }
-        if (++acc == kAccBufs) {
-          acc = 0;
-          acc_phase ^= 1;
-        }
+        stg.next<kStages>();
+        acc.next<kAccBufs>();
       }
       // flush the unit's remaining finished documents
       named_bar(1, kEpiWarps * 32);
-      for (int x = row; x < pending * n_queries; x += kEpiWarps * 32) {
+      for (int x = etid; x < pending * n_queries; x += kEpiWarps * 32) {
         const int g = x / n_queries, qq = x % n_queries;
         float sacc = 0.0F;
-        for (int k = 0; k < Q; ++k) sacc = __fadd_rn(sacc, rowval[g * 128 + qq * Q + k]);
+        for (int k = 0; k < Q; ++k) {
+          const int rr = qq * Q + k;
+          sacc = __fadd_rn(sacc, fmaxf(rowval[(g * 2) * 128 + rr], rowval[(g * 2 + 1) * 128 + rr]));
+        }
         p.out[static_cast<int64_t>(unit.qtile * p.qpt + qq) * p.num_docs + group_doc[g]] = __fmul_rn(sacc, p.scale);
       }
       named_bar(1, kEpiWarps * 32);
     }
   }
 done:
-  // Drain: the MMA warp waits (bounded) until its last commit has landed so
-  // no tensor-core operation still targets TMEM when it is released.
-  if (warp == kMmaWarp && *abort_flag) {
-    // on abort, outstanding MMAs finish on their own; give them time to land
+  // On abort, outstanding MMAs and bulk copies finish on their own; give them
+  // time to land before TMEM is released and the CTA exits.
+  if ((warp == kMmaWarp || warp == kLoadWarp) && *abort_flag) {
     const uint64_t t0 = global_ns();
-    while (global_ns() - t0 < 1000000ull) {
+    while (global_ns() - t0 < 2000000ull) {
     }
   }
   tc_fence_before();
@@ -596,6 +685,7 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
       const int64_t* it = std::lower_bound(off + lo + 1, off + d.num_docs + 1, target);
       int64_t hi = static_cast<int64_t>(it - off);
       if (hi > d.num_docs) hi = d.num_docs;
+      if (hi - lo > tc::kMaxRangeDocs) hi = lo + tc::kMaxRangeDocs;  // unit offsets live in shared memory
       if (hi <= lo) hi = lo + 1;
       if (off[hi] > off[lo])
         for (int t = 0; t < pl.n_qtiles; ++t) units.push_back(tc::Unit{lo, hi, off[lo], off[hi], t, 0});
