@@ -119,9 +119,9 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)  // suspend up to ~1 ms per try
       : "memory");
   return ok != 0;
 }
@@ -137,7 +137,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   const uint64_t t0 = global_ns();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try(bar, parity)) return true;
-    if ((it & 63u) == 63u) {
+    if ((it & 7u) == 7u) {
       if (*abort_flag) return false;
       if (global_ns() - t0 > kTimeoutNs) {
         *abort_flag = 1;
@@ -215,6 +215,19 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Fill 32 consecutive TMEM columns of this warp's 32 lanes with one value.
+__device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+      "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};"
+      ::"r"(taddr), "r"(v)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// Accumulators start from the bit pattern of 1.5 * 2^23: after the integer MMA
+// adds dot (|dot| < 2^22), the word read as a float is exactly 1.5 * 2^23 + dot.
+constexpr uint32_t kAccBias = 0x4B400000u;
+constexpr float kAccBiasF = 12582912.0F;
 
 // ---------------------------------------------------------------------------
 // The kernel
@@ -288,6 +301,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (warp < 4) {
+    // epilogue quarter warps pre-load every accumulator with the float bias
+    const uint32_t lb = static_cast<uint32_t>(warp * 32) << 16;
+    for (uint32_t c = 0; c < kTmemCols; c += 32) tmem_fill32(tmem_base + lb + c, kAccBias);
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
 
   if (warp == kLoadWarp) {
     // =================== loader: bulk copies run ahead of the expanders ===================
@@ -368,9 +390,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
             uint32_t o[8];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const uint32_t x = w[i] ^ 0x88888888u;  // two's-complement nibble -> code + 8
-              o[2 * i] = x & 0x0F0F0F0Fu;             // even dims (low nibbles)
-              o[2 * i + 1] = (x >> 4) & 0x0F0F0F0Fu;  // odd dims (high nibbles)
+              // Sign-extend 4-bit two's complement to 8 bits in every byte lane:
+              // (n + 0x78) ^ 0x78 maps 0..7 -> 0..7 and 8..15 -> 0xF8..0xFF (no carries).
+              o[2 * i] = ((w[i] & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x78787878u;          // even dims
+              o[2 * i + 1] = (((w[i] >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x78787878u;  // odd dims
             }
             *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
@@ -441,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = umma_desc(a_addr + 256u * k, 128u, 1024u);
             const uint64_t bd = umma_desc(b_addr + 256u * k, 128u, 1024u);
-            mma_i8(d_tmem, ad, bd, idesc, k > 0 ? 1u : 0u);
+            mma_i8(d_tmem, ad, bd, idesc, 1u);  // D = bias + A * B (bias pre-loaded by the epilogue)
           }
           mma_commit(&empty[stg.idx]);
           mma_commit(&acc_full[acc.idx]);
@@ -466,17 +489,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       const int b = unit.qtile * p.qpt + qi;
       const bool row_valid = row < p.qpt * Q && b < p.batch;
       const int64_t grow = static_cast<int64_t>(b) * Q + row % Q;
-      // acc + bias reinterpreted as float is 1.5 * 2^23 + dot exactly (|dot| < 2^22).
-      const int32_t bias = row_valid ? 0x4B400000 - 8 * __ldg(p.qsum + grow) : 0x4B400000;
       const float qs = row_valid ? __ldg(p.qscale + grow) : 0.0F;
       const int n_queries = min(p.qpt, p.batch - unit.qtile * p.qpt);
       float run = kLowest;        // running maximum of the open document over this half's columns
-      int32_t run_i = INT32_MIN;  // tensor-scale variant: integer maximum of acc
+      int32_t run_i = INT32_MIN;  // tensor-scale variant: maximum of the biased accumulator bits
       int pending = 0;
       auto emit = [&](int32_t doc) {
         float best;
         if (kTokenScale) best = run;
-        else best = run_i == INT32_MIN ? kLowest : __fadd_rn(__int_as_float(run_i + bias), -12582912.0F);
+        else best = run_i == INT32_MIN ? kLowest : __fadd_rn(__int_as_float(run_i), -kAccBiasF);
         // fl(max(a, b) * qs) == max(fl(a * qs), fl(b * qs)) for qs > 0, so halves are scaled first.
         rowval[(pending * 2 + half) * 128 + row] = row_valid ? __fmul_rn(best, qs) : 0.0F;
         if (etid == 0) group_doc[pending] = doc;
@@ -506,66 +527,77 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
         const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + kOffMeta + stg.idx * kMetaBytes);
         const int valid = meta->valid;
         const int nseg = meta->nseg;
-        const int h0 = 64 * half;
-        const int h1 = min(h0 + 64, valid);
-        float v[64];
-        int32_t vi[64];
-        if (h1 > h0) {
-          uint32_t r[64];
-          const uint32_t taddr = tmem_base + lane_base + static_cast<uint32_t>(acc.idx * kTileN + h0);
-          tmem_ld32_nowait(taddr, r);
-          tmem_ld32_nowait(taddr + 32, r + 32);
+        const uint32_t tbase = tmem_base + lane_base + static_cast<uint32_t>(acc.idx * kTileN);
+        int sgi = 0;
+        int next_end = nseg > 0 ? meta->seg_end[0] : (1 << 30);
+        // Two 32-column chunks per thread: columns [64*half + 32*ch, +32).
+#pragma unroll 1
+        for (int ch = 0; ch < 2; ++ch) {
+          const int c0 = 64 * half + 32 * ch;
+          // Documents ending before this chunk (they had no columns in it for this thread).
+          while (sgi < nseg && next_end <= c0) {
+            emit(meta->seg_doc[sgi]);
+            ++sgi;
+            next_end = sgi < nseg ? meta->seg_end[sgi] : (1 << 30);
+          }
+          if (c0 >= valid) continue;
+          const int cend = min(c0 + 32, valid);
+          uint32_t r[32];
+          tmem_ld32_nowait(tbase + static_cast<uint32_t>(c0), r);
           tmem_wait_ld();
+          float v[32];
           if (kTokenScale) {
-            const float4* sc4 = reinterpret_cast<const float4*>(meta->scale + h0);
+            const float4* sc4 = reinterpret_cast<const float4*>(meta->scale + c0);
 #pragma unroll
-            for (int j4 = 0; j4 < 16; ++j4) {
+            for (int j4 = 0; j4 < 8; ++j4) {
               const float4 s4 = sc4[j4];
               const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const int j = 4 * j4 + e;
-                v[j] = __fmul_rn(__fadd_rn(__int_as_float(static_cast<int32_t>(r[j]) + bias), -12582912.0F), sv[e]);
+                v[j] = __fmul_rn(__fadd_rn(__uint_as_float(r[j]), -kAccBiasF), sv[e]);
               }
+            }
+          }
+          if (next_end > c0 + 32 && cend == c0 + 32) {
+            // fast path: the whole chunk belongs to the open document
+            if (kTokenScale) {
+              float m = run;
+#pragma unroll
+              for (int j = 0; j < 32; j += 2) m = fmax3(m, v[j], v[j + 1]);
+              run = m;
+            } else {
+              int32_t m = run_i;
+#pragma unroll
+              for (int j = 0; j < 32; j += 2)
+                m = __vimax3_s32(m, static_cast<int32_t>(r[j]), static_cast<int32_t>(r[j + 1]));
+              run_i = m;
             }
           } else {
 #pragma unroll
-            for (int j = 0; j < 64; ++j) vi[j] = static_cast<int32_t>(r[j]);
-          }
-        }
-        // Walk the tile's document ends in order; every thread emits for every end.
-        int c = h0;  // next unprocessed column of this half
-        for (int sgi = 0; sgi <= nseg; ++sgi) {
-          const int e = sgi < nseg ? meta->seg_end[sgi] : h1;
-          const int a = c, bnd = min(e, h1);
-          if (bnd > a) {
-            if (a == h0 && bnd == h0 + 64) {
-              if (kTokenScale) {
-                float m = run;
-#pragma unroll
-                for (int j = 0; j < 64; j += 2) m = fmax3(m, v[j], v[j + 1]);
-                run = m;
-              } else {
-                int32_t m = run_i;
-#pragma unroll
-                for (int j = 0; j < 64; j += 2) m = __vimax3_s32(m, vi[j], vi[j + 1]);
-                run_i = m;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 64; ++j) {
-                const bool in = h0 + j >= a && h0 + j < bnd;
-                if (kTokenScale) run = in ? fmaxf(run, v[j]) : run;
-                else run_i = in ? max(run_i, vi[j]) : run_i;
+            for (int j = 0; j < 32; ++j) {
+              const int col = c0 + j;
+              if (col < cend) {
+                if (kTokenScale) run = fmaxf(run, v[j]);
+                else run_i = max(run_i, static_cast<int32_t>(r[j]));
+                if (col + 1 == next_end) {
+                  emit(meta->seg_doc[sgi]);
+                  ++sgi;
+                  next_end = sgi < nseg ? meta->seg_end[sgi] : (1 << 30);
+                }
               }
             }
-            c = bnd;
-          }
-          if (sgi < nseg) {
-            if (e > c) c = e;
-            emit(meta->seg_doc[sgi]);
           }
         }
+        // documents ending beyond this thread's columns (in the other half or at the tile end)
+        while (sgi < nseg) {
+          emit(meta->seg_doc[sgi]);
+          ++sgi;
+        }
+        // hand the accumulator back re-biased for its next tile
+        tmem_fill32(tbase + static_cast<uint32_t>(64 * half), kAccBias);
+        tmem_fill32(tbase + static_cast<uint32_t>(64 * half + 32), kAccBias);
+        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
