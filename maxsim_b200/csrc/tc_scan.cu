@@ -14,18 +14,23 @@
 //   * A work unit is (query tile, contiguous document range of ~W tokens);
 //     units are ordered range-major so the CTAs working on the query tiles of
 //     one range run together and share its codes through L2.
-//   * Persistent CTAs; each owns TMEM for two accumulators of TILE_N columns.
-//   * Warp roles: warps 0-3 epilogue (warp w reads TMEM lanes 32w..32w+31),
-//     warp 4 TMEM allocation + MMA issue (one thread), warps 5-8 producers.
-//   * Producers load 64-byte int4 rows with 16-byte vector loads, expand each
-//     nibble to a signed byte holding (code + 8) in [1, 15] (one LOP3 per 4
-//     values), and store the tile in the no-swizzle K-major UMMA layout
-//     (8x16-byte core matrices).  The +8 offset is removed exactly in the
-//     epilogue: dot(q, code) = acc - 8 * sum(q).
-//   * The epilogue converts acc to float with an exact integer-bias trick
-//     (|dot| < 2^22), multiplies by the token scale, and reduces with
-//     three-input max.  Document ends inside a tile come from a per-tile
-//     segment list the producers write next to the tile.
+//   * Persistent CTAs (one per SM), 14 warps: warps 0-7 epilogue (TMEM lane
+//     quarter = warp % 4, column half = warp / 4), warp 8 TMEM allocation and
+//     MMA issue (one thread), warps 9-12 expanders, warp 13 loader.
+//   * The loader streams each tile's 64-byte int4 rows (and token scales)
+//     into a 6-deep shared-memory ring with 1D bulk copies (TMA engine);
+//     expander warps turn each nibble into a byte holding (code + 8) in
+//     [1, 15] (one XOR and two masks per 8 values) and store the tile in the
+//     128-byte-swizzled K-major UMMA layout.  Tile metadata (token scales,
+//     document ends) goes through its own ring, released by the epilogue, so
+//     a B stage is free as soon as its MMAs complete.
+//   * Four TMEM accumulators of 128 columns.  The first K step overwrites,
+//     the other three accumulate, so a finished accumulator holds
+//     dot + 8 * sum(q) as an int32 below 2^24: conversion to float is exact,
+//     subtracting the per-row constant 8 * sum(q) recovers dot exactly, one
+//     FMUL applies the token scale and three-input max reduces.  Document ends
+//     inside a tile come from a per-tile segment list built from the unit's
+//     offsets.
 // Every mbarrier wait is bounded (%globaltimer); on timeout the kernel raises
 // an error flag, drains, frees its TMEM and returns.
 #include <algorithm>
@@ -38,18 +43,19 @@ namespace msb {
 namespace tc {
 
 constexpr int kTileN = 128;       // tokens per tile (MMA N)
-constexpr int kStages = 4;        // expanded-tile ring (B operand + tile metadata)
+constexpr int kStages = 4;        // expanded-tile ring (B operand), released by the MMA commit
+constexpr int kMeta = 8;          // tile metadata ring (scales, document ends), released by the epilogue
 constexpr int kRaw = 6;           // raw-code ring filled by bulk copies
-constexpr int kAccBufs = 2;       // TMEM accumulators
+constexpr int kAccBufs = 4;       // TMEM accumulators (4 x 128 columns = all 512)
 constexpr int kEpiWarps = 8;      // two per TMEM lane quarter, each owning 64 of a tile's columns
-constexpr int kXWarps = 4;        // expanders
+constexpr int kXWarps = 4;        // expanders (two tokens per thread per tile)
 constexpr int kMmaWarp = kEpiWarps;            // warp 8
 constexpr int kXWarp0 = kMmaWarp + 1;          // warps 9..12
 constexpr int kLoadWarp = kXWarp0 + kXWarps;   // warp 13
-constexpr int kThreads = (kLoadWarp + 1) * 32; // 448
+constexpr int kThreads = (kLoadWarp + 1) * 32; // 448 = 14 warps (128 registers each)
 constexpr int kSegGroup = 8;      // finished documents per epilogue flush
 constexpr int kMaxRangeDocs = 1024;
-constexpr uint32_t kTmemCols = kAccBufs * kTileN;             // 256
+constexpr uint32_t kTmemCols = kAccBufs * kTileN;             // 512
 constexpr uint64_t kTimeoutNs = 4000000000ull;                // 4 s per wait
 
 struct Unit {
@@ -96,11 +102,11 @@ constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + 2 * kATileBytes;
 constexpr int kOffRaw = kOffB + kStages * kBTileBytes;
 constexpr int kOffMeta = kOffRaw + kRaw * kRawBytes;
-constexpr int kOffUoff = kOffMeta + kStages * kMetaBytes;
+constexpr int kOffUoff = kOffMeta + kMeta * kMetaBytes;
 constexpr int kOffRow = kOffUoff + 2 * kUoffEntries * 8;
 constexpr int kRowBytes = kSegGroup * 2 * 128 * 4;     // [group][half][row]
 constexpr int kOffBar = kOffRow + kRowBytes + 128;     // + per-group doc ids
-constexpr int kNumBars = 2 * kStages + 2 * kRaw + 2 * kAccBufs + 4 + 4;
+constexpr int kNumBars = 2 * kStages + 2 * kMeta + 2 * kRaw + 2 * kAccBufs + 4 + 4;
 constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 64 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
@@ -135,8 +141,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
                                           int code) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = global_ns();
+  // Roles other than the epilogue (codes < 30 or >= 40) back off so their
+  // waiting does not take issue slots from the epilogue warps.
+  const bool backoff = code < 30 || code >= 40;
+  uint32_t sleep_ns = 32;
   for (uint32_t it = 0;; ++it) {
     if (mbar_try(bar, parity)) return true;
+    if (backoff) {
+      __nanosleep(sleep_ns);
+      if (sleep_ns < 256) sleep_ns <<= 1;
+    }
     if ((it & 7u) == 7u) {
       if (*abort_flag) return false;
       if (global_ns() - t0 > kTimeoutNs) {
@@ -157,7 +171,7 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
   // K-major, no swizzle: 8-row x 16-byte core matrices; LBO between core
   // matrices along K, SBO between 8-row groups; version 1 (bits 46-47).
   return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
-         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);  // SWIZZLE_128B
 }
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
@@ -190,7 +204,8 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 
 // Byte offset of (row, 16-byte K chunk) in a no-swizzle K-major tile of 128-byte rows.
 __device__ __forceinline__ uint32_t tile_off(int row, int kchunk) {
-  return static_cast<uint32_t>((row >> 3) * 1024 + kchunk * 128 + (row & 7) * 16);
+  // 128-byte swizzle: 8-row x 128-byte atoms, 16-byte chunk index XOR (row % 8)
+  return static_cast<uint32_t>((row >> 3) * 1024 + (row & 7) * 128 + ((kchunk ^ (row & 7)) << 4));
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -215,19 +230,6 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-// Fill 32 consecutive TMEM columns of this warp's 32 lanes with one value.
-__device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-      "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};"
-      ::"r"(taddr), "r"(v)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-// Accumulators start from the bit pattern of 1.5 * 2^23: after the integer MMA
-// adds dot (|dot| < 2^22), the word read as a float is exactly 1.5 * 2^23 + dot.
-constexpr uint32_t kAccBias = 0x4B400000u;
-constexpr float kAccBiasF = 12582912.0F;
 
 // ---------------------------------------------------------------------------
 // The kernel
@@ -252,7 +254,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* full = bars;                         // [kStages]  expanders -> MMA (and epilogue metadata)
   uint64_t* empty = full + kStages;              // [kStages]  MMA commit + epilogue -> expanders
-  uint64_t* raw_full = empty + kStages;          // [kRaw]     bulk copies -> expanders
+  uint64_t* m_full = empty + kStages;            // [kMeta]    expanders -> epilogue
+  uint64_t* m_empty = m_full + kMeta;            // [kMeta]    epilogue -> expanders
+  uint64_t* raw_full = m_empty + kMeta;          // [kRaw]     bulk copies -> expanders
   uint64_t* raw_empty = raw_full + kRaw;         // [kRaw]     expanders -> loader
   uint64_t* acc_full = raw_empty + kRaw;         // [kAccBufs] MMA -> epilogue
   uint64_t* acc_empty = acc_full + kAccBufs;     // [kAccBufs] epilogue -> MMA
@@ -272,7 +276,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], kXWarps);
-      mbar_init(&empty[s], 1 + kEpiWarps);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < kMeta; ++s) {
+      mbar_init(&m_full[s], kXWarps);
+      mbar_init(&m_empty[s], kEpiWarps);
     }
     for (int s = 0; s < kRaw; ++s) {
       mbar_init(&raw_full[s], 1);
@@ -301,16 +309,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  if (warp < 4) {
-    // epilogue quarter warps pre-load every accumulator with the float bias
-    const uint32_t lb = static_cast<uint32_t>(warp * 32) << 16;
-    for (uint32_t c = 0; c < kTmemCols; c += 32) tmem_fill32(tmem_base + lb + c, kAccBias);
-    tmem_wait_st();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-
   if (warp == kLoadWarp) {
     // =================== loader: bulk copies run ahead of the expanders ===================
     if (lane == 0) {
@@ -347,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
     // =================== expanders: int4 -> (code + 8) bytes, UMMA layout ===================
     const int xtid = threadIdx.x - kXWarp0 * 32;  // 0..127
     const int xwarp = warp - kXWarp0;
-    Ring raw, stg;
+    Ring raw, stg, mst;
     int iter = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
       const Unit unit = p.units[u];
@@ -355,14 +353,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       if (iter >= 2 && !mbar_wait(&a_empty[abuf], ((iter >> 1) - 1) & 1, abort_flag, p.error, 11)) goto done;
       {
         unsigned char* A = smem + kOffA + abuf * kATileBytes;
-        const int row = xtid;  // one query row per expander thread
-        const int b = unit.qtile * p.qpt + row / Q;
-        const bool valid = row < p.qpt * Q && b < p.batch;
-        const int4* src = reinterpret_cast<const int4*>(p.qwords + (static_cast<int64_t>(b) * Q + row % Q) * 32);
+        for (int row = xtid; row < 128; row += kXWarps * 32) {  // query rows of the tile
+          const int b = unit.qtile * p.qpt + row / Q;
+          const bool valid = row < p.qpt * Q && b < p.batch;
+          const int4* src = reinterpret_cast<const int4*>(p.qwords + (static_cast<int64_t>(b) * Q + row % Q) * 32);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          int4 v = valid ? __ldg(src + c) : make_int4(0, 0, 0, 0);
-          *reinterpret_cast<int4*>(A + tile_off(row, c)) = v;
+          for (int c = 0; c < 8; ++c) {
+            int4 v = valid ? __ldg(src + c) : make_int4(0, 0, 0, 0);
+            *reinterpret_cast<int4*>(A + tile_off(row, c)) = v;
+          }
         }
         fence_proxy_async();
         __syncwarp();
@@ -376,12 +375,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
         if (!mbar_wait(&raw_full[raw.idx], raw.phase, abort_flag, p.error, 14)) goto done;
         if (!mbar_wait(&empty[stg.idx], stg.phase ^ 1, abort_flag, p.error, 12)) goto done;
+        if (!mbar_wait(&m_empty[mst.idx], mst.phase ^ 1, abort_flag, p.error, 15)) goto done;
         const unsigned char* rb = smem + kOffRaw + raw.idx * kRawBytes;
         unsigned char* Bt = smem + kOffB + stg.idx * kBTileBytes;
-        StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kOffMeta + stg.idx * kMetaBytes);
+        StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kOffMeta + mst.idx * kMetaBytes);
         const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
-        const int r = xtid;  // one token per expander thread
-        if (r < valid) {
+#pragma unroll 1
+        for (int r = xtid; r < valid; r += kXWarps * 32) {  // tokens of the tile
 #pragma unroll
           for (int step = 0; step < 4; ++step) {
             const int c = (step + (r >> 1)) & 3;  // rotated chunk order: conflict-free shared loads
@@ -390,10 +390,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
             uint32_t o[8];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              // Sign-extend 4-bit two's complement to 8 bits in every byte lane:
-              // (n + 0x78) ^ 0x78 maps 0..7 -> 0..7 and 8..15 -> 0xF8..0xFF (no carries).
-              o[2 * i] = ((w[i] & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x78787878u;          // even dims
-              o[2 * i + 1] = (((w[i] >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x78787878u;  // odd dims
+              const uint32_t x = w[i] ^ 0x88888888u;  // two's-complement nibble -> code + 8 in [1, 15]
+              o[2 * i] = x & 0x0F0F0F0Fu;             // even dims (low nibbles)
+              o[2 * i + 1] = (x >> 4) & 0x0F0F0F0Fu;  // odd dims (high nibbles)
             }
             *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
@@ -435,10 +434,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&full[stg.idx]);
+          mbar_arrive(&m_full[mst.idx]);
           mbar_arrive(&raw_empty[raw.idx]);
         }
         raw.next<kRaw>();
         stg.next<kStages>();
+        mst.next<kMeta>();
       }
       if (xwarp == 0 && lane == 0) mbar_arrive(&u_empty[ub]);
     }
@@ -462,9 +463,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc.idx * kTileN);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = umma_desc(a_addr + 256u * k, 128u, 1024u);
-            const uint64_t bd = umma_desc(b_addr + 256u * k, 128u, 1024u);
-            mma_i8(d_tmem, ad, bd, idesc, 1u);  // D = bias + A * B (bias pre-loaded by the epilogue)
+            const uint64_t ad = umma_desc(a_addr + 32u * k, 16u, 1024u);
+            const uint64_t bd = umma_desc(b_addr + 32u * k, 16u, 1024u);
+            mma_i8(d_tmem, ad, bd, idesc, k > 0 ? 1u : 0u);
           }
           mma_commit(&empty[stg.idx]);
           mma_commit(&acc_full[acc.idx]);
@@ -481,6 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
     const int row = threadIdx.x & 127;            // TMEM lane = query-tile row
     const int half = threadIdx.x >> 7;            // columns [64*half, 64*half + 64) of every tile
     const int etid = threadIdx.x;                 // 0..255
+    const int h0 = 64 * half;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     Ring stg, acc;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
@@ -490,135 +492,115 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       const bool row_valid = row < p.qpt * Q && b < p.batch;
       const int64_t grow = static_cast<int64_t>(b) * Q + row % Q;
       const float qs = row_valid ? __ldg(p.qscale + grow) : 0.0F;
+      // The accumulator holds A.(code + 8) = dot + 8*sum(q), integers below 2^24 in magnitude:
+      // converting to float and subtracting this per-row constant recovers dot exactly.
+      const float neg_bias = -(8.0F * static_cast<float>(row_valid ? __ldg(p.qsum + grow) : 0));
       const int n_queries = min(p.qpt, p.batch - unit.qtile * p.qpt);
       float run = kLowest;        // running maximum of the open document over this half's columns
-      int32_t run_i = INT32_MIN;  // tensor-scale variant: maximum of the biased accumulator bits
+      int32_t run_i = INT32_MIN;  // tensor-scale variant: integer maximum of dot + 8 sum q
       int pending = 0;
-      auto emit = [&](int32_t doc) {
-        float best;
-        if (kTokenScale) best = run;
-        else best = run_i == INT32_MIN ? kLowest : __fadd_rn(__int_as_float(run_i), -kAccBiasF);
-        // fl(max(a, b) * qs) == max(fl(a * qs), fl(b * qs)) for qs > 0, so halves are scaled first.
-        rowval[(pending * 2 + half) * 128 + row] = row_valid ? __fmul_rn(best, qs) : 0.0F;
-        if (etid == 0) group_doc[pending] = doc;
-        run = kLowest;
-        run_i = INT32_MIN;
-        if (++pending == kSegGroup) {
-          named_bar(1, kEpiWarps * 32);
-          for (int x = etid; x < pending * n_queries; x += kEpiWarps * 32) {
-            const int g = x / n_queries, qq = x % n_queries;
-            float sacc = 0.0F;
-            for (int k = 0; k < Q; ++k) {
-              const int rr = qq * Q + k;
-              sacc = __fadd_rn(sacc, fmaxf(rowval[(g * 2) * 128 + rr], rowval[(g * 2 + 1) * 128 + rr]));
-            }
-            p.out[static_cast<int64_t>(unit.qtile * p.qpt + qq) * p.num_docs + group_doc[g]] = __fmul_rn(sacc, p.scale);
-          }
-          named_bar(1, kEpiWarps * 32);
-          pending = 0;
-        }
-      };
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
         if (!mbar_wait(&acc_full[acc.idx], acc.phase, abort_flag, p.error, 31)) goto done;
-        // The stage's expander phase is complete and cannot advance before this
-        // warp releases the stage; waiting on it acquires the metadata writes.
-        if (!mbar_wait(&full[stg.idx], stg.phase, abort_flag, p.error, 32)) goto done;
+        // Acquire the expanders' metadata writes for this tile (meta ring slot).
+        if (!mbar_wait(&m_full[stg.idx], stg.phase, abort_flag, p.error, 32)) goto done;
         tc_fence_after();
         const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + kOffMeta + stg.idx * kMetaBytes);
         const int valid = meta->valid;
         const int nseg = meta->nseg;
-        const uint32_t tbase = tmem_base + lane_base + static_cast<uint32_t>(acc.idx * kTileN);
-        int sgi = 0;
-        int next_end = nseg > 0 ? meta->seg_end[0] : (1 << 30);
-        // Two 32-column chunks per thread: columns [64*half + 32*ch, +32).
-#pragma unroll 1
-        for (int ch = 0; ch < 2; ++ch) {
-          const int c0 = 64 * half + 32 * ch;
-          // Documents ending before this chunk (they had no columns in it for this thread).
-          while (sgi < nseg && next_end <= c0) {
-            emit(meta->seg_doc[sgi]);
-            ++sgi;
-            next_end = sgi < nseg ? meta->seg_end[sgi] : (1 << 30);
+        const int h1 = min(h0 + 64, valid);  // this half's valid columns [h0, h1)
+        const uint32_t taddr = tmem_base + lane_base + static_cast<uint32_t>(acc.idx * kTileN + h0);
+        uint32_t r[64];
+        tmem_ld32_nowait(taddr, r);
+        tmem_ld32_nowait(taddr + 32, r + 32);
+        tmem_wait_ld();
+        if (kTokenScale) {
+          // exact: float(dot + 8 sum q) - 8 sum q = dot (integers below 2^24), then fl(dot * s_t)
+          const float4* sc4 = reinterpret_cast<const float4*>(meta->scale + h0);
+#pragma unroll
+          for (int j4 = 0; j4 < 16; ++j4) {
+            const float4 s4 = sc4[j4];
+            r[4 * j4 + 0] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 0])), neg_bias), s4.x));
+            r[4 * j4 + 1] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 1])), neg_bias), s4.y));
+            r[4 * j4 + 2] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 2])), neg_bias), s4.z));
+            r[4 * j4 + 3] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 3])), neg_bias), s4.w));
           }
-          if (c0 >= valid) continue;
-          const int cend = min(c0 + 32, valid);
-          uint32_t r[32];
-          tmem_ld32_nowait(tbase + static_cast<uint32_t>(c0), r);
-          tmem_wait_ld();
-          float v[32];
-          if (kTokenScale) {
-            const float4* sc4 = reinterpret_cast<const float4*>(meta->scale + c0);
+        }
+        // Walk the tile's document ends in order; every thread emits a partial for every end.
+        int a = h0;
+        for (int sgi = 0; sgi <= nseg; ++sgi) {
+          const int e = sgi < nseg ? meta->seg_end[sgi] : h1;
+          const int bnd = min(e, h1);
+          if (bnd > a) {
+            if (a == h0 && bnd == h0 + 64) {
+              // eight independent max chains (depth 4) instead of one chain of 32
+              if (kTokenScale) {
+                float m[8];
 #pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              const float4 s4 = sc4[j4];
-              const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+                for (int c = 0; c < 8; ++c) m[c] = fmaxf(__uint_as_float(r[2 * c]), __uint_as_float(r[2 * c + 1]));
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int j = 4 * j4 + e;
-                v[j] = __fmul_rn(__fadd_rn(__uint_as_float(r[j]), -kAccBiasF), sv[e]);
+                for (int j = 16; j < 64; j += 16)
+#pragma unroll
+                  for (int c = 0; c < 8; ++c) m[c] = fmax3(m[c], __uint_as_float(r[j + 2 * c]), __uint_as_float(r[j + 2 * c + 1]));
+                run = fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmax3(m[6], m[7], run));
+              } else {
+                int32_t m[8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) m[c] = max(static_cast<int32_t>(r[2 * c]), static_cast<int32_t>(r[2 * c + 1]));
+#pragma unroll
+                for (int j = 16; j < 64; j += 16)
+#pragma unroll
+                  for (int c = 0; c < 8; ++c)
+                    m[c] = __vimax3_s32(m[c], static_cast<int32_t>(r[j + 2 * c]), static_cast<int32_t>(r[j + 2 * c + 1]));
+                run_i = __vimax3_s32(__vimax3_s32(m[0], m[1], m[2]), __vimax3_s32(m[3], m[4], m[5]),
+                                     __vimax3_s32(m[6], m[7], run_i));
               }
-            }
-          }
-          if (next_end > c0 + 32 && cend == c0 + 32) {
-            // fast path: the whole chunk belongs to the open document
-            if (kTokenScale) {
-              float m = run;
-#pragma unroll
-              for (int j = 0; j < 32; j += 2) m = fmax3(m, v[j], v[j + 1]);
-              run = m;
             } else {
-              int32_t m = run_i;
+              const int la = a - h0, lb = bnd - h0;
 #pragma unroll
-              for (int j = 0; j < 32; j += 2)
-                m = __vimax3_s32(m, static_cast<int32_t>(r[j]), static_cast<int32_t>(r[j + 1]));
-              run_i = m;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int col = c0 + j;
-              if (col < cend) {
-                if (kTokenScale) run = fmaxf(run, v[j]);
-                else run_i = max(run_i, static_cast<int32_t>(r[j]));
-                if (col + 1 == next_end) {
-                  emit(meta->seg_doc[sgi]);
-                  ++sgi;
-                  next_end = sgi < nseg ? meta->seg_end[sgi] : (1 << 30);
-                }
+              for (int j = 0; j < 64; ++j) {
+                const bool in = j >= la && j < lb;
+                if (kTokenScale) run = in ? fmaxf(run, __uint_as_float(r[j])) : run;
+                else run_i = in ? max(run_i, static_cast<int32_t>(r[j])) : run_i;
               }
             }
+            a = bnd;
+          }
+          if (sgi == nseg) break;
+          if (e > a) a = e;
+          // document meta->seg_doc[sgi] ends: stage this half's partial, scaled by the row's query scale
+          float best;
+          if (kTokenScale) best = run;
+          else best = run_i == INT32_MIN ? kLowest : __fadd_rn(__int2float_rn(run_i), neg_bias);
+          // fl(max(x, y) * qs) == max(fl(x * qs), fl(y * qs)) for qs > 0, so halves are scaled first.
+          rowval[(pending * 2 + half) * 128 + row] = row_valid ? __fmul_rn(best, qs) : 0.0F;
+          if (etid == 0) group_doc[pending] = meta->seg_doc[sgi];
+          run = kLowest;
+          run_i = INT32_MIN;
+          if (++pending == kSegGroup || (sgi + 1 == nseg && t0 + kTileN >= unit.tok_hi)) {
+            named_bar(1, kEpiWarps * 32);
+            for (int x = etid; x < pending * n_queries; x += kEpiWarps * 32) {
+              const int g = x / n_queries, qq = x % n_queries;
+              float sacc = 0.0F;
+              for (int k = 0; k < Q; ++k) {
+                const int rr = qq * Q + k;
+                sacc = __fadd_rn(sacc, fmaxf(rowval[(g * 2) * 128 + rr], rowval[(g * 2 + 1) * 128 + rr]));
+              }
+              p.out[static_cast<int64_t>(unit.qtile * p.qpt + qq) * p.num_docs + group_doc[g]] =
+                  __fmul_rn(sacc, p.scale);
+            }
+            named_bar(1, kEpiWarps * 32);
+            pending = 0;
           }
         }
-        // documents ending beyond this thread's columns (in the other half or at the tile end)
-        while (sgi < nseg) {
-          emit(meta->seg_doc[sgi]);
-          ++sgi;
-        }
-        // hand the accumulator back re-biased for its next tile
-        tmem_fill32(tbase + static_cast<uint32_t>(64 * half), kAccBias);
-        tmem_fill32(tbase + static_cast<uint32_t>(64 * half + 32), kAccBias);
-        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&acc_empty[acc.idx]);
-          mbar_arrive(&empty[stg.idx]);
+          mbar_arrive(&m_empty[stg.idx]);
         }
-        stg.next<kStages>();
+        stg.next<kMeta>();
         acc.next<kAccBufs>();
       }
-      // flush the unit's remaining finished documents
-      named_bar(1, kEpiWarps * 32);
-      for (int x = etid; x < pending * n_queries; x += kEpiWarps * 32) {
-        const int g = x / n_queries, qq = x % n_queries;
-        float sacc = 0.0F;
-        for (int k = 0; k < Q; ++k) {
-          const int rr = qq * Q + k;
-          sacc = __fadd_rn(sacc, fmaxf(rowval[(g * 2) * 128 + rr], rowval[(g * 2 + 1) * 128 + rr]));
-        }
-        p.out[static_cast<int64_t>(unit.qtile * p.qpt + qq) * p.num_docs + group_doc[g]] = __fmul_rn(sacc, p.scale);
-      }
-      named_bar(1, kEpiWarps * 32);
     }
   }
 done:
