@@ -171,6 +171,30 @@ int msb_pack_int4_device(const float* x, int64_t n, int32_t dim, int32_t per_tok
                          float* token_scales, float* tensor_scale, void* stream);
 int msb_pack_signs_device(const float* x, int64_t n, int32_t dim, uint8_t* bits, float* mean_abs, void* stream);
 
+/* ---- allocation-free variant ------------------------------------------- */
+/* Bytes of the fixed device scratch used by msb_docs_topk_device_noalloc. */
+#define MSB_NOALLOC_SCRATCH_BYTES (16u << 20) /* 16 MiB */
+/* Full-scan top-k like msb_docs_topk_device (same arguments, options and
+ * results), for callers that cannot call cudaMalloc: code that runs while a
+ * framework's caching allocator owns all device memory, code inside a
+ * memory-budgeted serving loop, or code that must not add driver allocations
+ * (which synchronise the device) on a latency path.  It allocates nothing:
+ * its scratch -- the [batch, num_docs] fp32 score matrix plus, for int8
+ * queries, the quantised query rows -- lives in one fixed 16 MiB device
+ * array inside this library, which every GPU that loads the library holds
+ * until the process exits.  Calls whose scratch would exceed
+ * MSB_NOALLOC_SCRATCH_BYTES (about batch * num_docs * 4 bytes) fail with
+ * MSB_ERR_INVALID_ARGUMENT.  It always runs the CUDA-core scan engine.
+ *   - The first call on each device looks up the scratch's device address
+ *     (cudaGetSymbolAddress, which may load the library's device code on that
+ *     device); make that first call before any stream capture.
+ *   - All calls on a device share the one scratch array and it keeps the last
+ *     call's contents.  Calls that overlap on the GPU (two streams, or two
+ *     host threads) race on it: serialise them.
+ * This entry point has no counterpart in the reference. */
+int msb_docs_topk_device_noalloc(msb_docs* docs, const float* query, int32_t batch, int32_t query_tokens, int32_t k,
+                                 const msb_score_opts* opts, float* out_scores, int64_t* out_ids, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

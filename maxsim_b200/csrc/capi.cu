@@ -759,3 +759,89 @@ int msb_pack_signs_device(const float* x, int64_t n, int32_t dim, uint8_t* bits,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free full-scan top-k (msb_docs_topk_device_noalloc)
+// ---------------------------------------------------------------------------
+// Fixed scratch for callers that cannot allocate device memory: the score
+// matrix and the int8 query rows of one call.  Each device that loads the
+// library holds it until the process exits; all calls on a device share it.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MSB_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+// In host code `g_noalloc_scratch` names a host-side stand-in, not device
+// memory, so kernels are given the device address looked up here: once per
+// device, with that device current (the caller's DeviceGuard makes it so).
+unsigned char* noalloc_scratch_on_current_device() {
+  static std::mutex mu;
+  static std::vector<void*> addr;
+  int dev = 0;
+  check(cudaGetDevice(&dev), "get device");
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= static_cast<int>(addr.size())) addr.resize(static_cast<size_t>(dev) + 1, nullptr);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    check(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress of the no-alloc scratch");
+    addr[dev] = p;
+  }
+  return static_cast<unsigned char*>(addr[dev]);
+}
+
+constexpr size_t round256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
+
+}  // namespace
+
+extern "C" int msb_docs_topk_device_noalloc(msb_docs* h, const float* query, int32_t batch, int32_t qtok, int32_t k,
+                                            const msb_score_opts* opts, float* out_scores, int64_t* out_ids,
+                                            void* stream) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    if (k < 1 || k > h->num_docs) throw InvalidArgument("k must be between 1 and num_docs");
+    check_query(h, query, batch, qtok);
+    DeviceGuard g(h->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    Resolved r = resolve(h, opts, batch, qtok, opts ? opts->weights : nullptr, opts ? opts->doc_scale_override : nullptr);
+    if (batch == 0) return;
+    // Scratch layout: scores [batch, num_docs] fp32, then (int8 queries) codes,
+    // scan-order words, scales and code sums of the batch * qtok query rows.
+    constexpr size_t cap = MSB_NOALLOC_SCRATCH_BYTES;
+    const int64_t rows = static_cast<int64_t>(batch) * qtok;
+    const bool fits = h->num_docs <= static_cast<int64_t>(cap / sizeof(float) / static_cast<size_t>(batch)) &&
+                      rows <= static_cast<int64_t>(cap / static_cast<size_t>(h->dim));
+    size_t need = fits ? round256(sizeof(float) * static_cast<size_t>(batch) * h->num_docs) : cap + 1;
+    const size_t codes_at = need;
+    const size_t words_at = codes_at + round256(static_cast<size_t>(rows) * h->dim);
+    const size_t scales_at = words_at + round256(static_cast<size_t>(rows) * h->dim);
+    const size_t sums_at = scales_at + round256(static_cast<size_t>(rows) * sizeof(float));
+    if (fits && r.mode == kQueryI8) need = sums_at + round256(static_cast<size_t>(rows) * sizeof(int32_t));
+    if (need > cap)
+      throw InvalidArgument("msb_docs_topk_device_noalloc: batch " + std::to_string(batch) + " x " +
+                            std::to_string(h->num_docs) + " documents (" + std::to_string(qtok) +
+                            " query tokens) needs more than its fixed scratch of " + std::to_string(cap) +
+                            " bytes; use msb_docs_topk_device or a smaller batch");
+    unsigned char* base = noalloc_scratch_on_current_device();
+    float* scores = reinterpret_cast<float*>(base);
+    if (qtok == 0) {
+      check(cudaMemsetAsync(scores, 0, sizeof(float) * static_cast<size_t>(batch) * h->num_docs, s), "zero scores");
+    } else {
+      QueryView qv{};
+      qv.f32 = query;
+      qv.batch = batch;
+      qv.qtok = qtok;
+      qv.mode = r.mode;
+      if (r.mode == kQueryI8) {
+        qv.i8 = reinterpret_cast<const int8_t*>(base + codes_at);
+        qv.i8_words = reinterpret_cast<const int32_t*>(base + words_at);
+        qv.row_scale = reinterpret_cast<const float*>(base + scales_at);
+        qv.row_sum = reinterpret_cast<const int32_t*>(base + sums_at);
+        launch_quantize_rows(query, rows, h->dim, reinterpret_cast<int8_t*>(base + codes_at),
+                             reinterpret_cast<float*>(base + scales_at), reinterpret_cast<int32_t*>(base + sums_at),
+                             reinterpret_cast<int32_t*>(base + words_at), h->format == kFormatInt4, s);
+      }
+      // Every score is written by the scan, so nothing in the scratch needs clearing.
+      launch_simt_scan(r.docs, qv, r.red, TargetsView{}, r.residual, scores, s);
+    }
+    launch_topk_rows(scores, h->num_docs, batch, h->num_docs, k, nullptr, false, out_scores, out_ids, s);
+  });
+}
