@@ -29,6 +29,7 @@ size_t tc_scan_workspace_bytes(const DocsView&, const QueryView&, const TargetsV
 static std::atomic<int64_t> g_launches{0};
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 static std::atomic<int> g_engine{0};  // 0 auto, 1 SIMT, 2 tensor core
+static std::atomic<uint64_t> g_corpus_serial{0};
 }  // namespace msb
 
 using namespace msb;
@@ -125,6 +126,7 @@ struct msb_docs {
       w_override, w_fine, w_tc;
   std::vector<int64_t> host_offsets;
   bool tc_used = false;  // the tensor-core engine ran since the last error check
+  uint64_t serial = 0;   // unique corpus id for caches keyed on a corpus
 
   size_t bytes_per_token() const { return format == kFormatInt4 ? dim / 2 : dim / 8; }
   int64_t resident_bytes() const {
@@ -186,6 +188,7 @@ Resolved resolve(msb_docs* h, const msb_score_opts* o, int batch, int qtok, cons
   d.codes = h->codes.as<uint8_t>();
   d.offsets = h->offsets.as<int64_t>();
   d.host_offsets = h->host_offsets.data();
+  d.corpus_id = h->serial;
   d.num_docs = h->num_docs;
   d.num_tokens = h->num_tokens;
   d.dim = h->dim;
@@ -335,6 +338,7 @@ msb_docs* create_common(int32_t format, int32_t dim, int64_t num_tokens, const i
   if (num_docs > 0x7FFFFFFF) throw NotSupported("more than 2^31 - 1 documents per handle");
   validate_offsets(offsets_host, num_docs, num_tokens);
   auto* h = new msb_docs();
+  h->serial = g_corpus_serial.fetch_add(1) + 1;
   h->format = format;
   h->dim = dim;
   h->num_docs = num_docs;

@@ -49,6 +49,7 @@ struct DocsView {
   const int64_t* offsets;      // [D + 1]
   const float* doc_scale;      // [D] or nullptr (binary scale vector)
   const int64_t* host_offsets;  // host copy of offsets (work partitioning)
+  uint64_t corpus_id;          // unique per resident corpus (keys host-side caches)
   int64_t num_docs;
   int64_t num_tokens;
   int dim;

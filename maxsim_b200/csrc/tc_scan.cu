@@ -11,26 +11,29 @@
 // Layout of the work
 //   * A query tile is 128 TMEM lanes = floor(128 / Q) whole queries (Q rows
 //     each); query rows are int8, K permuted to the nibble order of the codes.
-//   * A work unit is (query tile, contiguous document range of ~W tokens);
-//     units are ordered range-major so the CTAs working on the query tiles of
-//     one range run together and share its codes through L2.
-//   * Persistent CTAs (one per SM), 14 warps: warps 0-7 epilogue (TMEM lane
-//     quarter = warp % 4, column half = warp / 4), warp 8 TMEM allocation and
-//     MMA issue (one thread), warps 9-12 expanders, warp 13 loader.
+//   * A work unit is (pair of query tiles, contiguous document range).  Each
+//     token tile is loaded and expanded once and multiplied against both
+//     query tiles, so loads, expansion and pipeline hand-offs are shared by
+//     two 128 x 128 products.  Document ranges are token quantiles of the
+//     corpus, 2 x SM-count of them, ordered range-major, so every CTA gets the
+//     same number of equal-sized units and the CTAs working on one range run
+//     together and share its codes through L2.
+//   * Persistent CTAs (one per SM), 14 warps: warps 0-7 epilogue (query tile
+//     warp / 4, TMEM lane quarter warp % 4), warp 8 TMEM allocation and MMA
+//     issue (one thread), warps 9-12 expanders, warp 13 loader.
 //   * The loader streams each tile's 64-byte int4 rows (and token scales)
 //     into a 6-deep shared-memory ring with 1D bulk copies (TMA engine);
 //     expander warps turn each nibble into a byte holding (code + 8) in
 //     [1, 15] (one XOR and two masks per 8 values) and store the tile in the
 //     128-byte-swizzled K-major UMMA layout.  Tile metadata (token scales,
-//     document ends) goes through its own ring, released by the epilogue, so
-//     a B stage is free as soon as its MMAs complete.
-//   * Four TMEM accumulators of 128 columns.  The first K step overwrites,
-//     the other three accumulate, so a finished accumulator holds
-//     dot + 8 * sum(q) as an int32 below 2^24: conversion to float is exact,
-//     subtracting the per-row constant 8 * sum(q) recovers dot exactly, one
-//     FMUL applies the token scale and three-input max reduces.  Document ends
-//     inside a tile come from a per-tile segment list built from the unit's
-//     offsets.
+//     document ends) goes through its own ring, released by the epilogue.
+//   * TMEM holds two token-tile buffers x two query tiles x 128 columns.  One
+//     commit per token tile both frees its shared-memory stage and hands the
+//     accumulators to the epilogue.  The first K step overwrites, the other
+//     three accumulate, so an accumulator holds dot + 8 * sum(q) as an int32
+//     below 2^24: conversion to float is exact, subtracting the per-row
+//     constant 8 * sum(q) recovers dot exactly, one FMUL applies the token
+//     scale and three-input max reduces.
 // Every mbarrier wait is bounded (%globaltimer); on timeout the kernel raises
 // an error flag, drains, frees its TMEM and returns.
 #include <algorithm>
@@ -43,25 +46,26 @@ namespace msb {
 namespace tc {
 
 constexpr int kTileN = 128;       // tokens per tile (MMA N)
+constexpr int kG = 2;             // query tiles per unit, sharing every expanded token tile
 constexpr int kStages = 4;        // expanded-tile ring (B operand), released by the MMA commit
 constexpr int kMeta = 8;          // tile metadata ring (scales, document ends), released by the epilogue
 constexpr int kRaw = 6;           // raw-code ring filled by bulk copies
-constexpr int kAccBufs = 4;       // TMEM accumulators (4 x 128 columns = all 512)
-constexpr int kEpiWarps = 8;      // two per TMEM lane quarter, each owning 64 of a tile's columns
-constexpr int kXWarps = 4;        // expanders (two tokens per thread per tile)
+constexpr int kAccBufs = 2;       // token-tile accumulator buffers (each kG x 128 TMEM columns)
+constexpr int kEpiWarps = 8;      // warp w: query tile w / 4 of the pair, TMEM lane quarter w % 4
+constexpr int kXWarps = 4;        // expanders (one token per thread per tile)
 constexpr int kMmaWarp = kEpiWarps;            // warp 8
 constexpr int kXWarp0 = kMmaWarp + 1;          // warps 9..12
 constexpr int kLoadWarp = kXWarp0 + kXWarps;   // warp 13
 constexpr int kThreads = (kLoadWarp + 1) * 32; // 448 = 14 warps (128 registers each)
 constexpr int kSegGroup = 8;      // finished documents per epilogue flush
-constexpr int kMaxRangeDocs = 1024;
-constexpr uint32_t kTmemCols = kAccBufs * kTileN;             // 512
+constexpr int kMaxRangeDocs = 512;
+constexpr uint32_t kTmemCols = kAccBufs * kG * kTileN;        // 512
 constexpr uint64_t kTimeoutNs = 4000000000ull;                // 4 s per wait
 
 struct Unit {
   int64_t d_lo, d_hi;    // documents [d_lo, d_hi), at most kMaxRangeDocs
   int64_t tok_lo, tok_hi;
-  int32_t qtile;
+  int32_t qpair;         // query tiles kG * qpair .. kG * qpair + kG - 1
   int32_t pad;
 };
 
@@ -98,17 +102,18 @@ struct StageMeta {
   int32_t valid;             // valid columns
 };
 constexpr int kMetaBytes = ((sizeof(StageMeta) + 127) / 128) * 128;
-constexpr int kOffA = 0;
-constexpr int kOffB = kOffA + 2 * kATileBytes;
+constexpr int kOffA = 0;                                         // [2 buffers][kG] query tiles
+constexpr int kOffB = kOffA + 2 * kG * kATileBytes;
 constexpr int kOffRaw = kOffB + kStages * kBTileBytes;
 constexpr int kOffMeta = kOffRaw + kRaw * kRawBytes;
 constexpr int kOffUoff = kOffMeta + kMeta * kMetaBytes;
 constexpr int kOffRow = kOffUoff + 2 * kUoffEntries * 8;
-constexpr int kRowBytes = kSegGroup * 2 * 128 * 4;     // [group][half][row]
+constexpr int kRowBytes = kSegGroup * kG * 128 * 4;    // [group][query tile][row]
 constexpr int kOffBar = kOffRow + kRowBytes + 128;     // + per-group doc ids
-constexpr int kNumBars = 2 * kStages + 2 * kMeta + 2 * kRaw + 2 * kAccBufs + 4 + 4;
+constexpr int kNumBars = 2 * kStages + 2 * kMeta + 2 * kRaw + kAccBufs + 8;
 constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 64 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+static_assert(kOffUoff % 16 == 0 && kOffRaw % 16 == 0 && kRawBytes % 16 == 0, "bulk-copy alignment");
 
 // ---------------------------------------------------------------------------
 // PTX wrappers
@@ -252,21 +257,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                          ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* full = bars;                         // [kStages]  expanders -> MMA (and epilogue metadata)
-  uint64_t* empty = full + kStages;              // [kStages]  MMA commit + epilogue -> expanders
-  uint64_t* m_full = empty + kStages;            // [kMeta]    expanders -> epilogue
+  uint64_t* full = bars;                         // [kStages]  expanders -> MMA
+  uint64_t* tile_done = full + kStages;          // [kStages]  MMA commit -> expanders (stage free), epilogue (acc full)
+  uint64_t* m_full = tile_done + kStages;        // [kMeta]    expanders -> epilogue
   uint64_t* m_empty = m_full + kMeta;            // [kMeta]    epilogue -> expanders
   uint64_t* raw_full = m_empty + kMeta;          // [kRaw]     bulk copies -> expanders
   uint64_t* raw_empty = raw_full + kRaw;         // [kRaw]     expanders -> loader
-  uint64_t* acc_full = raw_empty + kRaw;         // [kAccBufs] MMA -> epilogue
-  uint64_t* acc_empty = acc_full + kAccBufs;     // [kAccBufs] epilogue -> MMA
+  uint64_t* acc_empty = raw_empty + kRaw;        // [kAccBufs] epilogue -> MMA
   uint64_t* a_full = acc_empty + kAccBufs;       // [2]        expanders -> MMA
   uint64_t* a_empty = a_full + 2;                // [2]        MMA commit -> expanders
   uint64_t* u_full = a_empty + 2;                // [2]        unit offsets bulk copy -> segment warp
   uint64_t* u_empty = u_full + 2;                // [2]        segment warp -> loader
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* rowval = reinterpret_cast<float*>(smem + kOffRow);                      // [group][half][128]
+  float* rowval = reinterpret_cast<float*>(smem + kOffRow);                      // [group][kG][128]
   int32_t* group_doc = reinterpret_cast<int32_t*>(smem + kOffRow + kRowBytes);  // [kSegGroup]
 
   const int warp = threadIdx.x >> 5;
@@ -276,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], kXWarps);
-      mbar_init(&empty[s], 1);
+      mbar_init(&tile_done[s], 1);
     }
     for (int s = 0; s < kMeta; ++s) {
       mbar_init(&m_full[s], kXWarps);
@@ -286,10 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       mbar_init(&raw_full[s], 1);
       mbar_init(&raw_empty[s], kXWarps);
     }
-    for (int a = 0; a < kAccBufs; ++a) {
-      mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], kEpiWarps);
-    }
+    for (int a = 0; a < kAccBufs; ++a) mbar_init(&acc_empty[a], kEpiWarps);
     for (int a = 0; a < 2; ++a) {
       mbar_init(&a_full[a], kXWarps);
       mbar_init(&a_empty[a], 1);
@@ -309,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+
   if (warp == kLoadWarp) {
     // =================== loader: bulk copies run ahead of the expanders ===================
     if (lane == 0) {
@@ -352,9 +354,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       const int abuf = iter & 1;
       if (iter >= 2 && !mbar_wait(&a_empty[abuf], ((iter >> 1) - 1) & 1, abort_flag, p.error, 11)) goto done;
       {
-        unsigned char* A = smem + kOffA + abuf * kATileBytes;
-        for (int row = xtid; row < 128; row += kXWarps * 32) {  // query rows of the tile
-          const int b = unit.qtile * p.qpt + row / Q;
+        const int row = xtid;  // one query row of each tile of the pair per thread
+#pragma unroll
+        for (int g = 0; g < kG; ++g) {
+          unsigned char* A = smem + kOffA + (abuf * kG + g) * kATileBytes;
+          const int b = (unit.qpair * kG + g) * p.qpt + row / Q;
           const bool valid = row < p.qpt * Q && b < p.batch;
           const int4* src = reinterpret_cast<const int4*>(p.qwords + (static_cast<int64_t>(b) * Q + row % Q) * 32);
 #pragma unroll
@@ -374,14 +378,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       int64_t next_doc = unit.d_lo;  // first document whose end has not been passed
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
         if (!mbar_wait(&raw_full[raw.idx], raw.phase, abort_flag, p.error, 14)) goto done;
-        if (!mbar_wait(&empty[stg.idx], stg.phase ^ 1, abort_flag, p.error, 12)) goto done;
+        if (!mbar_wait(&tile_done[stg.idx], stg.phase ^ 1, abort_flag, p.error, 12)) goto done;
         if (!mbar_wait(&m_empty[mst.idx], mst.phase ^ 1, abort_flag, p.error, 15)) goto done;
         const unsigned char* rb = smem + kOffRaw + raw.idx * kRawBytes;
         unsigned char* Bt = smem + kOffB + stg.idx * kBTileBytes;
         StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kOffMeta + mst.idx * kMetaBytes);
         const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
-#pragma unroll 1
-        for (int r = xtid; r < valid; r += kXWarps * 32) {  // tokens of the tile
+        if (xtid < valid) {
+          const int r = xtid;  // one token per thread
 #pragma unroll
           for (int step = 0; step < 4; ++step) {
             const int c = (step + (r >> 1)) & 3;  // rotated chunk order: conflict-free shared loads
@@ -452,23 +456,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
       const Unit unit = p.units[u];
       const int abuf = iter & 1;
+      // query tiles of the pair that hold at least one query
+      const int n_tiles = min(kG, (p.batch - unit.qpair * kG * p.qpt + p.qpt - 1) / p.qpt);
       if (!mbar_wait(&a_full[abuf], (iter >> 1) & 1, abort_flag, p.error, 21)) goto done;
-      const uint32_t a_addr = smem_u32(smem + kOffA + abuf * kATileBytes);
+      const uint32_t a_addr = smem_u32(smem + kOffA + abuf * kG * kATileBytes);
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
         if (!mbar_wait(&full[stg.idx], stg.phase, abort_flag, p.error, 22)) goto done;
         if (!mbar_wait(&acc_empty[acc.idx], acc.phase ^ 1, abort_flag, p.error, 23)) goto done;
         tc_fence_after();
         if (lane == 0) {
           const uint32_t b_addr = smem_u32(smem + kOffB + stg.idx * kBTileBytes);
-          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc.idx * kTileN);
+          for (int g = 0; g < n_tiles; ++g) {
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((acc.idx * kG + g) * kTileN);
+            const uint32_t ag = a_addr + static_cast<uint32_t>(g * kATileBytes);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = umma_desc(a_addr + 32u * k, 16u, 1024u);
-            const uint64_t bd = umma_desc(b_addr + 32u * k, 16u, 1024u);
-            mma_i8(d_tmem, ad, bd, idesc, k > 0 ? 1u : 0u);
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t ad = umma_desc(ag + 32u * k, 16u, 1024u);
+              const uint64_t bd = umma_desc(b_addr + 32u * k, 16u, 1024u);
+              mma_i8(d_tmem, ad, bd, idesc, k > 0 ? 1u : 0u);
+            }
           }
-          mma_commit(&empty[stg.idx]);
-          mma_commit(&acc_full[acc.idx]);
+          mma_commit(&tile_done[stg.idx]);
         }
         __syncwarp();
         stg.next<kStages>();
@@ -478,128 +486,136 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       __syncwarp();
     }
   } else {
-    // =================== epilogue: warps 0-7; lane quarter = warp % 4, column half = warp / 4 ===========
+    // =================== epilogue: warps 0-7; query tile g = warp / 4, lane quarter = warp % 4 ===========
     const int row = threadIdx.x & 127;            // TMEM lane = query-tile row
-    const int half = threadIdx.x >> 7;            // columns [64*half, 64*half + 64) of every tile
+    const int g = threadIdx.x >> 7;               // query tile of the pair
     const int etid = threadIdx.x;                 // 0..255
-    const int h0 = 64 * half;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    Ring stg, acc;
+    Ring stg, acc, mst;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
       const Unit unit = p.units[u];
-      const int qi = row / Q;
-      const int b = unit.qtile * p.qpt + qi;
+      const int tile = unit.qpair * kG + g;
+      const int b = tile * p.qpt + row / Q;
       const bool row_valid = row < p.qpt * Q && b < p.batch;
+      const bool tile_live = tile * p.qpt < p.batch;
       const int64_t grow = static_cast<int64_t>(b) * Q + row % Q;
       const float qs = row_valid ? __ldg(p.qscale + grow) : 0.0F;
       // The accumulator holds A.(code + 8) = dot + 8*sum(q), integers below 2^24 in magnitude:
       // converting to float and subtracting this per-row constant recovers dot exactly.
       const float neg_bias = -(8.0F * static_cast<float>(row_valid ? __ldg(p.qsum + grow) : 0));
-      const int n_queries = min(p.qpt, p.batch - unit.qtile * p.qpt);
-      float run = kLowest;        // running maximum of the open document over this half's columns
+      const int nq0 = max(0, min(p.qpt, p.batch - (unit.qpair * kG) * p.qpt));
+      const int nq1 = max(0, min(p.qpt, p.batch - (unit.qpair * kG + 1) * p.qpt));
+      const int nq = nq0 + nq1;
+      float run = kLowest;        // running maximum of the open document
       int32_t run_i = INT32_MIN;  // tensor-scale variant: integer maximum of dot + 8 sum q
       int pending = 0;
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
-        if (!mbar_wait(&acc_full[acc.idx], acc.phase, abort_flag, p.error, 31)) goto done;
+        if (!mbar_wait(&tile_done[stg.idx], stg.phase, abort_flag, p.error, 31)) goto done;
         // Acquire the expanders' metadata writes for this tile (meta ring slot).
-        if (!mbar_wait(&m_full[stg.idx], stg.phase, abort_flag, p.error, 32)) goto done;
+        if (!mbar_wait(&m_full[mst.idx], mst.phase, abort_flag, p.error, 32)) goto done;
         tc_fence_after();
-        const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + kOffMeta + stg.idx * kMetaBytes);
+        const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + kOffMeta + mst.idx * kMetaBytes);
         const int valid = meta->valid;
         const int nseg = meta->nseg;
-        const int h1 = min(h0 + 64, valid);  // this half's valid columns [h0, h1)
-        const uint32_t taddr = tmem_base + lane_base + static_cast<uint32_t>(acc.idx * kTileN + h0);
-        uint32_t r[64];
-        tmem_ld32_nowait(taddr, r);
-        tmem_ld32_nowait(taddr + 32, r + 32);
-        tmem_wait_ld();
-        if (kTokenScale) {
-          // exact: float(dot + 8 sum q) - 8 sum q = dot (integers below 2^24), then fl(dot * s_t)
-          const float4* sc4 = reinterpret_cast<const float4*>(meta->scale + h0);
+        const uint32_t tbase = tmem_base + lane_base + static_cast<uint32_t>((acc.idx * kG + g) * kTileN);
+        int sgi = 0;
+        for (int h0 = 0; h0 < valid; h0 += 64) {
+          const int h1 = min(h0 + 64, valid);  // this chunk's valid columns [h0, h1)
+          uint32_t r[64];
+          if (tile_live) {
+            tmem_ld32_nowait(tbase + h0, r);
+            tmem_ld32_nowait(tbase + h0 + 32, r + 32);
+            tmem_wait_ld();
+            if (kTokenScale) {
+              // exact: float(dot + 8 sum q) - 8 sum q = dot (integers below 2^24), then fl(dot * s_t)
+              const float4* sc4 = reinterpret_cast<const float4*>(meta->scale + h0);
 #pragma unroll
-          for (int j4 = 0; j4 < 16; ++j4) {
-            const float4 s4 = sc4[j4];
-            r[4 * j4 + 0] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 0])), neg_bias), s4.x));
-            r[4 * j4 + 1] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 1])), neg_bias), s4.y));
-            r[4 * j4 + 2] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 2])), neg_bias), s4.z));
-            r[4 * j4 + 3] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 3])), neg_bias), s4.w));
+              for (int j4 = 0; j4 < 16; ++j4) {
+                const float4 s4 = sc4[j4];
+                r[4 * j4 + 0] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 0])), neg_bias), s4.x));
+                r[4 * j4 + 1] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 1])), neg_bias), s4.y));
+                r[4 * j4 + 2] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 2])), neg_bias), s4.z));
+                r[4 * j4 + 3] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 3])), neg_bias), s4.w));
+              }
+            }
           }
-        }
-        // Walk the tile's document ends in order; every thread emits a partial for every end.
-        int a = h0;
-        for (int sgi = 0; sgi <= nseg; ++sgi) {
-          const int e = sgi < nseg ? meta->seg_end[sgi] : h1;
-          const int bnd = min(e, h1);
-          if (bnd > a) {
-            if (a == h0 && bnd == h0 + 64) {
-              // eight independent max chains (depth 4) instead of one chain of 32
-              if (kTokenScale) {
-                float m[8];
+          // Walk the document ends inside this chunk in order.
+          int a = h0;
+          while (true) {
+            const int e = sgi < nseg ? meta->seg_end[sgi] : 0x7FFF;
+            const int bnd = min(e, h1);
+            if (bnd > a && tile_live) {
+              if (a == h0 && bnd == h0 + 64) {
+                // eight independent max chains (depth 4) instead of one chain of 32
+                if (kTokenScale) {
+                  float m[8];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) m[c] = fmaxf(__uint_as_float(r[2 * c]), __uint_as_float(r[2 * c + 1]));
+                  for (int c = 0; c < 8; ++c) m[c] = fmaxf(__uint_as_float(r[2 * c]), __uint_as_float(r[2 * c + 1]));
 #pragma unroll
-                for (int j = 16; j < 64; j += 16)
+                  for (int j = 16; j < 64; j += 16)
 #pragma unroll
-                  for (int c = 0; c < 8; ++c) m[c] = fmax3(m[c], __uint_as_float(r[j + 2 * c]), __uint_as_float(r[j + 2 * c + 1]));
-                run = fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmax3(m[6], m[7], run));
+                    for (int c = 0; c < 8; ++c)
+                      m[c] = fmax3(m[c], __uint_as_float(r[j + 2 * c]), __uint_as_float(r[j + 2 * c + 1]));
+                  run = fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmax3(m[6], m[7], run));
+                } else {
+                  int32_t m[8];
+#pragma unroll
+                  for (int c = 0; c < 8; ++c) m[c] = max(static_cast<int32_t>(r[2 * c]), static_cast<int32_t>(r[2 * c + 1]));
+#pragma unroll
+                  for (int j = 16; j < 64; j += 16)
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                      m[c] = __vimax3_s32(m[c], static_cast<int32_t>(r[j + 2 * c]), static_cast<int32_t>(r[j + 2 * c + 1]));
+                  run_i = __vimax3_s32(__vimax3_s32(m[0], m[1], m[2]), __vimax3_s32(m[3], m[4], m[5]),
+                                       __vimax3_s32(m[6], m[7], run_i));
+                }
               } else {
-                int32_t m[8];
+                const int la = a - h0, lb = bnd - h0;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) m[c] = max(static_cast<int32_t>(r[2 * c]), static_cast<int32_t>(r[2 * c + 1]));
-#pragma unroll
-                for (int j = 16; j < 64; j += 16)
-#pragma unroll
-                  for (int c = 0; c < 8; ++c)
-                    m[c] = __vimax3_s32(m[c], static_cast<int32_t>(r[j + 2 * c]), static_cast<int32_t>(r[j + 2 * c + 1]));
-                run_i = __vimax3_s32(__vimax3_s32(m[0], m[1], m[2]), __vimax3_s32(m[3], m[4], m[5]),
-                                     __vimax3_s32(m[6], m[7], run_i));
-              }
-            } else {
-              const int la = a - h0, lb = bnd - h0;
-#pragma unroll
-              for (int j = 0; j < 64; ++j) {
-                const bool in = j >= la && j < lb;
-                if (kTokenScale) run = in ? fmaxf(run, __uint_as_float(r[j])) : run;
-                else run_i = in ? max(run_i, static_cast<int32_t>(r[j])) : run_i;
+                for (int j = 0; j < 64; ++j) {
+                  const bool in = j >= la && j < lb;
+                  if (kTokenScale) run = in ? fmaxf(run, __uint_as_float(r[j])) : run;
+                  else run_i = in ? max(run_i, static_cast<int32_t>(r[j])) : run_i;
+                }
               }
             }
-            a = bnd;
-          }
-          if (sgi == nseg) break;
-          if (e > a) a = e;
-          // document meta->seg_doc[sgi] ends: stage this half's partial, scaled by the row's query scale
-          float best;
-          if (kTokenScale) best = run;
-          else best = run_i == INT32_MIN ? kLowest : __fadd_rn(__int2float_rn(run_i), neg_bias);
-          // fl(max(x, y) * qs) == max(fl(x * qs), fl(y * qs)) for qs > 0, so halves are scaled first.
-          rowval[(pending * 2 + half) * 128 + row] = row_valid ? __fmul_rn(best, qs) : 0.0F;
-          if (etid == 0) group_doc[pending] = meta->seg_doc[sgi];
-          run = kLowest;
-          run_i = INT32_MIN;
-          if (++pending == kSegGroup || (sgi + 1 == nseg && t0 + kTileN >= unit.tok_hi)) {
-            named_bar(1, kEpiWarps * 32);
-            for (int x = etid; x < pending * n_queries; x += kEpiWarps * 32) {
-              const int g = x / n_queries, qq = x % n_queries;
-              float sacc = 0.0F;
-              for (int k = 0; k < Q; ++k) {
-                const int rr = qq * Q + k;
-                sacc = __fadd_rn(sacc, fmaxf(rowval[(g * 2) * 128 + rr], rowval[(g * 2 + 1) * 128 + rr]));
+            if (bnd > a) a = bnd;
+            if (sgi >= nseg || e > h1) break;
+            // document meta->seg_doc[sgi] ends at column e: stage this row's value, scaled by the query scale
+            float best;
+            if (kTokenScale) best = run;
+            else best = run_i == INT32_MIN ? kLowest : __fadd_rn(__int2float_rn(run_i), neg_bias);
+            rowval[(pending * kG + g) * 128 + row] = row_valid ? __fmul_rn(best, qs) : 0.0F;
+            if (etid == 0) group_doc[pending] = meta->seg_doc[sgi];
+            run = kLowest;
+            run_i = INT32_MIN;
+            ++sgi;
+            if (++pending == kSegGroup || (sgi == nseg && t0 + kTileN >= unit.tok_hi)) {
+              named_bar(1, kEpiWarps * 32);
+              for (int x = etid; x < pending * nq; x += kEpiWarps * 32) {
+                const int gd = x / nq, qx = x % nq;
+                const int gq = qx < nq0 ? 0 : 1;
+                const int qq = qx < nq0 ? qx : qx - nq0;
+                const float* rv = rowval + (gd * kG + gq) * 128 + qq * Q;
+                float sacc = 0.0F;
+                for (int k = 0; k < Q; ++k) sacc = __fadd_rn(sacc, rv[k]);
+                p.out[static_cast<int64_t>((unit.qpair * kG + gq) * p.qpt + qq) * p.num_docs + group_doc[gd]] =
+                    __fmul_rn(sacc, p.scale);
               }
-              p.out[static_cast<int64_t>(unit.qtile * p.qpt + qq) * p.num_docs + group_doc[g]] =
-                  __fmul_rn(sacc, p.scale);
+              named_bar(1, kEpiWarps * 32);
+              pending = 0;
             }
-            named_bar(1, kEpiWarps * 32);
-            pending = 0;
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&acc_empty[acc.idx]);
-          mbar_arrive(&m_empty[stg.idx]);
+          mbar_arrive(&m_empty[mst.idx]);
         }
-        stg.next<kMeta>();
+        stg.next<kStages>();
         acc.next<kAccBufs>();
+        mst.next<kMeta>();
       }
     }
   }
@@ -630,18 +646,25 @@ namespace {
 struct TcPlan {
   int qpt;
   int n_qtiles;
-  int64_t range_tokens;
+  int n_pairs;
+  int64_t n_ranges;  // token-quantile document ranges before the per-range document cap
 };
 
-TcPlan plan_for(const DocsView& d, const QueryView& q) {
+int sm_count() {
+  int dev = 0, sms = 0;
+  check(cudaGetDevice(&dev), "get device");
+  check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "query SM count");
+  return sms;
+}
+
+TcPlan plan_for(const DocsView& d, const QueryView& q, int sms) {
   TcPlan pl{};
   pl.qpt = 128 / q.qtok;
   pl.n_qtiles = (q.batch + pl.qpt - 1) / pl.qpt;
-  // ~4 units per CTA slot, at least 8 tiles per range.
-  const int64_t slots = 148LL * 4;
-  int64_t w = (d.num_tokens * pl.n_qtiles + slots - 1) / slots;
-  w = std::max<int64_t>(w, 8 * tc::kTileN);
-  pl.range_tokens = ((w + tc::kTileN - 1) / tc::kTileN) * tc::kTileN;
+  pl.n_pairs = (pl.n_qtiles + tc::kG - 1) / tc::kG;
+  // 2 x SM-count ranges: every CTA gets 2 * n_pairs equal units; ranges of
+  // fewer than 8 tiles only for small corpora.
+  pl.n_ranges = std::max<int64_t>(1, std::min<int64_t>(2LL * sms, d.num_tokens / (8 * tc::kTileN)));
   return pl;
 }
 
@@ -655,19 +678,18 @@ bool tc_scan_supported(const DocsView& d, const QueryView& q, const ReduceView& 
 }
 
 size_t tc_scan_workspace_bytes(const DocsView& d, const QueryView& q, const TargetsView&) {
-  const TcPlan pl = plan_for(d, q);
-  const int64_t max_ranges = d.num_docs + (d.num_tokens / pl.range_tokens) + 2;
-  return 256 + sizeof(tc::Unit) * static_cast<size_t>(max_ranges) * pl.n_qtiles;
+  const TcPlan pl = plan_for(d, q, sm_count());
+  const int64_t max_ranges = pl.n_ranges + d.num_docs / tc::kMaxRangeDocs + 2;
+  return 256 + sizeof(tc::Unit) * static_cast<size_t>(max_ranges) * pl.n_pairs;
 }
 
 struct UnitCacheKey {
   const void* ws;
-  const int64_t* offsets;
-  int64_t num_docs, num_tokens, range_tokens;
-  int n_qtiles;
+  uint64_t corpus_id;
+  int64_t n_ranges;
+  int n_pairs;
   bool operator==(const UnitCacheKey& o) const {
-    return ws == o.ws && offsets == o.offsets && num_docs == o.num_docs && num_tokens == o.num_tokens &&
-           range_tokens == o.range_tokens && n_qtiles == o.n_qtiles;
+    return ws == o.ws && corpus_id == o.corpus_id && n_ranges == o.n_ranges && n_pairs == o.n_pairs;
   }
 };
 
@@ -677,8 +699,9 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   // built once per (workspace, corpus, tiling) and kept in the workspace.
   static std::mutex cache_mu;
   static std::vector<std::pair<UnitCacheKey, int>> cache;  // key -> number of units
-  const TcPlan pl = plan_for(d, q);
-  const UnitCacheKey key{ws, d.offsets, d.num_docs, d.num_tokens, pl.range_tokens, pl.n_qtiles};
+  const int sms = sm_count();
+  const TcPlan pl = plan_for(d, q, sms);
+  const UnitCacheKey key{ws, d.corpus_id, pl.n_ranges, pl.n_pairs};
   int* err = static_cast<int*>(ws);
   tc::Unit* d_units = reinterpret_cast<tc::Unit*>(static_cast<unsigned char*>(ws) + 256);
   int num_units = -1;
@@ -690,20 +713,25 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   // Empty documents never appear in a tile; their score is 0.
   check(cudaMemsetAsync(out, 0, sizeof(float) * static_cast<size_t>(q.batch) * d.num_docs, stream), "zero scores");
   if (num_units < 0) {
-    // Document ranges of ~range_tokens tokens (host offsets), range-major units.
+    // Document ranges cut at the token quantiles r * N / n_ranges, each split
+    // further to at most kMaxRangeDocs documents; range-major units.
     std::vector<tc::Unit> units;
     const int64_t* off = d.host_offsets;
+    const int64_t D = d.num_docs, N = d.num_tokens;
     int64_t lo = 0;
-    while (lo < d.num_docs) {
-      const int64_t target = off[lo] + pl.range_tokens;
-      const int64_t* it = std::lower_bound(off + lo + 1, off + d.num_docs + 1, target);
-      int64_t hi = static_cast<int64_t>(it - off);
-      if (hi > d.num_docs) hi = d.num_docs;
-      if (hi - lo > tc::kMaxRangeDocs) hi = lo + tc::kMaxRangeDocs;  // unit offsets live in shared memory
-      if (hi <= lo) hi = lo + 1;
-      if (off[hi] > off[lo])
-        for (int t = 0; t < pl.n_qtiles; ++t) units.push_back(tc::Unit{lo, hi, off[lo], off[hi], t, 0});
-      lo = hi;
+    for (int64_t r = 1; r <= pl.n_ranges && lo < D; ++r) {
+      int64_t hi = D;
+      if (r < pl.n_ranges) {
+        const int64_t target = static_cast<int64_t>((static_cast<__int128>(N) * r) / pl.n_ranges);
+        hi = static_cast<int64_t>(std::lower_bound(off + lo, off + D + 1, target) - off);
+        if (hi > D) hi = D;
+      }
+      while (lo < hi) {
+        const int64_t h2 = std::min<int64_t>(hi, lo + tc::kMaxRangeDocs);  // unit offsets live in shared memory
+        if (off[h2] > off[lo])
+          for (int t = 0; t < pl.n_pairs; ++t) units.push_back(tc::Unit{lo, h2, off[lo], off[h2], t, 0});
+        lo = h2;
+      }
     }
     const size_t need = 256 + sizeof(tc::Unit) * units.size();
     if (need > ws_bytes) throw CudaFailure("tensor-core scan workspace too small");
@@ -736,9 +764,6 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   prm.num_docs = d.num_docs;
   prm.out = out;
   prm.error = err;
-  int dev = 0, sms = 0;
-  check(cudaGetDevice(&dev), "get device");
-  check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "query SM count");
   const int grid = std::min<int>(sms, prm.num_units);
   if (d.token_scale) {
     check(cudaFuncSetAttribute(tc::tc_scan_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes),
