@@ -23,17 +23,22 @@
 //     issue (one thread), warps 9-12 expanders, warp 13 loader.
 //   * The loader streams each tile's 64-byte int4 rows (and token scales)
 //     into a 6-deep shared-memory ring with 1D bulk copies (TMA engine);
-//     expander warps turn each nibble into a byte holding (code + 8) in
-//     [1, 15] (one XOR and two masks per 8 values) and store the tile in the
-//     128-byte-swizzled K-major UMMA layout.  Tile metadata (token scales,
-//     document ends) goes through its own ring, released by the epilogue.
+//     expander warps sign-extend each two's-complement nibble to an int8
+//     byte (two masks and one multiply-add per 4 values) and store the tile
+//     in the 128-byte-swizzled K-major UMMA layout, in a chunk order that
+//     keeps both their shared loads and stores free of bank conflicts.  Tile
+//     metadata (token scales, document ends) goes through its own ring,
+//     released by the epilogue.
 //   * TMEM holds two token-tile buffers x two query tiles x 128 columns.  One
 //     commit per token tile both frees its shared-memory stage and hands the
-//     accumulators to the epilogue.  The first K step overwrites, the other
-//     three accumulate, so an accumulator holds dot + 8 * sum(q) as an int32
-//     below 2^24: conversion to float is exact, subtracting the per-row
-//     constant 8 * sum(q) recovers dot exactly, one FMUL applies the token
-//     scale and three-input max reduces.
+//     accumulators to the epilogue, which returns them as soon as the tile's
+//     last columns are in registers.  The first K step overwrites, the other
+//     three accumulate, so an accumulator holds the exact int32 dot (below
+//     2^24: conversion to float is exact); one FMUL applies the token scale
+//     and three-input max reduces.  The epilogue reads TMEM with 16x256b
+//     loads, so each thread holds two rows x 16 columns per 64-column chunk
+//     and needs 16 token scales instead of 64; a row's maximum is completed
+//     with two butterfly shuffles when a document ends.
 // Every mbarrier wait is bounded (%globaltimer); on timeout the kernel raises
 // an error flag, drains, frees its TMEM and returns.
 #include <algorithm>
@@ -75,7 +80,6 @@ struct Params {
   const int64_t* offsets;
   const int32_t* qwords;      // [B*Q, 32] nibble-order int8 words
   const float* qscale;        // [B*Q]
-  const int32_t* qsum;        // [B*Q]
   const Unit* units;
   int num_units;
   int batch;
@@ -234,6 +238,18 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 16 TMEM lanes x 64 columns: thread t receives, for j = 0..7, columns 8j + 2(t % 4) + {0, 1} of lane
+// (t / 4) in r[4j], r[4j + 1] and of lane (t / 4 + 8) in r[4j + 2], r[4j + 3].
+__device__ __forceinline__ void tmem_ld16x256b_x8(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
@@ -344,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       }
     }
   } else if (warp >= kXWarp0) {
-    // =================== expanders: int4 -> (code + 8) bytes, UMMA layout ===================
+    // =================== expanders: int4 -> int8 bytes, UMMA layout ===================
     const int xtid = threadIdx.x - kXWarp0 * 32;  // 0..127
     const int xwarp = warp - kXWarp0;
     Ring raw, stg, mst;
@@ -386,17 +402,24 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
         const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
         if (xtid < valid) {
           const int r = xtid;  // one token per thread
+          // Chunk order c = M(a) ^ step with a = (r / 2) % 4 and M multiplication by a generator of GF(4)
+          // ({0, 2, 3, 1}): both c and c ^ a run over all four values within each 8-token quarter warp,
+          // so the raw loads (bank slot 4(r % 2) + c) and the swizzled stores (slot 2(c ^ a) + r % 2) are
+          // conflict-free.
+          const int qa = (r >> 1) & 3;
+          const int qm = ((qa << 1) & 3) ^ ((qa >> 1) * 3);
 #pragma unroll
           for (int step = 0; step < 4; ++step) {
-            const int c = (step + (r >> 1)) & 3;  // rotated chunk order: conflict-free shared loads
+            const int c = qm ^ step;
             const uint4 v = *reinterpret_cast<const uint4*>(rb + r * 64 + c * 16);
             const uint32_t w[4] = {v.x, v.y, v.z, v.w};
             uint32_t o[8];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const uint32_t x = w[i] ^ 0x88888888u;  // two's-complement nibble -> code + 8 in [1, 15]
-              o[2 * i] = x & 0x0F0F0F0Fu;             // even dims (low nibbles)
-              o[2 * i + 1] = (x >> 4) & 0x0F0F0F0Fu;  // odd dims (high nibbles)
+              // sign-extend each two's-complement nibble to a byte: n | (n & 8) * 0x1E, no carries between bytes
+              const uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = (w[i] >> 4) & 0x0F0F0F0Fu;
+              o[2 * i] = lo + (lo & 0x08080808u) * 30u;      // even dims (low nibbles)
+              o[2 * i + 1] = hi + (hi & 0x08080808u) * 30u;  // odd dims (high nibbles)
             }
             *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
@@ -486,28 +509,31 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       __syncwarp();
     }
   } else {
-    // =================== epilogue: warps 0-7; query tile g = warp / 4, lane quarter = warp % 4 ===========
-    const int row = threadIdx.x & 127;            // TMEM lane = query-tile row
-    const int g = threadIdx.x >> 7;               // query tile of the pair
+    // =================== epilogue: warps 0-7; query tile g = warp / 4, TMEM lane quarter warp % 4 ===========
+    // 16x256b TMEM loads: thread t holds rows R(i) = 32 (warp % 4) + 16 (i / 2) + 8 (i % 2) + t / 4,
+    // i = 0..3, and per 64-column chunk the 16 columns 8j + 2(t % 4) + {0, 1}, so it needs 16 token
+    // scales per chunk instead of 64.  A row's maximum is completed across the four threads
+    // t % 4 = 0..3 with two butterfly shuffles when a document ends.
+    const int q4 = warp & 3;
+    const int g = warp >> 2;                      // query tile of the pair
     const int etid = threadIdx.x;                 // 0..255
-    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int tq = lane >> 2, tc = lane & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
     Ring stg, acc, mst;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
       const Unit unit = p.units[u];
       const int tile = unit.qpair * kG + g;
-      const int b = tile * p.qpt + row / Q;
-      const bool row_valid = row < p.qpt * Q && b < p.batch;
       const bool tile_live = tile * p.qpt < p.batch;
-      const int64_t grow = static_cast<int64_t>(b) * Q + row % Q;
-      const float qs = row_valid ? __ldg(p.qscale + grow) : 0.0F;
-      // The accumulator holds A.(code + 8) = dot + 8*sum(q), integers below 2^24 in magnitude:
-      // converting to float and subtracting this per-row constant recovers dot exactly.
-      const float neg_bias = -(8.0F * static_cast<float>(row_valid ? __ldg(p.qsum + grow) : 0));
+      // the row this thread stores when a document ends: i = t % 4
+      const int wrow = q4 * 32 + 16 * (tc >> 1) + 8 * (tc & 1) + tq;
+      const int wb = tile * p.qpt + wrow / Q;
+      const bool w_valid = wrow < p.qpt * Q && wb < p.batch;
+      const float qs = w_valid ? __ldg(p.qscale + static_cast<int64_t>(wb) * Q + wrow % Q) : 0.0F;
       const int nq0 = max(0, min(p.qpt, p.batch - (unit.qpair * kG) * p.qpt));
       const int nq1 = max(0, min(p.qpt, p.batch - (unit.qpair * kG + 1) * p.qpt));
       const int nq = nq0 + nq1;
-      float run = kLowest;        // running maximum of the open document
-      int32_t run_i = INT32_MIN;  // tensor-scale variant: integer maximum of dot + 8 sum q
+      float run[4] = {kLowest, kLowest, kLowest, kLowest};                // open document, per row
+      int32_t run_i[4] = {INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN};    // tensor-scale variant
       int pending = 0;
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
         if (!mbar_wait(&tile_done[stg.idx], stg.phase, abort_flag, p.error, 31)) goto done;
@@ -517,80 +543,133 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
         const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + kOffMeta + mst.idx * kMetaBytes);
         const int valid = meta->valid;
         const int nseg = meta->nseg;
+        const bool last_tile = t0 + kTileN >= unit.tok_hi;
         const uint32_t tbase = tmem_base + lane_base + static_cast<uint32_t>((acc.idx * kG + g) * kTileN);
         int sgi = 0;
-        for (int h0 = 0; h0 < valid; h0 += 64) {
-          const int h1 = min(h0 + 64, valid);  // this chunk's valid columns [h0, h1)
-          uint32_t r[64];
+        bool released = false;
+        for (int c0 = 0; c0 < valid; c0 += 64) {
+          const int c1 = min(c0 + 64, valid);  // this chunk's valid columns [c0, c1)
+          uint32_t ra[32], rb[32];              // lanes +0..15 (rows i = 0, 1) and +16..31 (rows i = 2, 3)
           if (tile_live) {
-            tmem_ld32_nowait(tbase + h0, r);
-            tmem_ld32_nowait(tbase + h0 + 32, r + 32);
-            tmem_wait_ld();
+            float2 sc[8];
             if (kTokenScale) {
-              // exact: float(dot + 8 sum q) - 8 sum q = dot (integers below 2^24), then fl(dot * s_t)
-              const float4* sc4 = reinterpret_cast<const float4*>(meta->scale + h0);
 #pragma unroll
-              for (int j4 = 0; j4 < 16; ++j4) {
-                const float4 s4 = sc4[j4];
-                r[4 * j4 + 0] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 0])), neg_bias), s4.x));
-                r[4 * j4 + 1] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 1])), neg_bias), s4.y));
-                r[4 * j4 + 2] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 2])), neg_bias), s4.z));
-                r[4 * j4 + 3] = __float_as_uint(__fmul_rn(__fadd_rn(__int2float_rn(static_cast<int32_t>(r[4 * j4 + 3])), neg_bias), s4.w));
+              for (int j = 0; j < 8; ++j) sc[j] = *reinterpret_cast<const float2*>(meta->scale + c0 + 8 * j + 2 * tc);
+            }
+            tmem_ld16x256b_x8(tbase + c0, ra);
+            tmem_ld16x256b_x8(tbase + (16u << 16) + c0, rb);
+            tmem_wait_ld();
+            if (c0 + 64 >= valid) {
+              // last chunk of the tile is in registers: hand the accumulators back to the MMA now
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&acc_empty[acc.idx]);
+              released = true;
+            }
+            if (kTokenScale) {
+              // exact int32 dot -> float, then fl(dot * s_t)
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                ra[4 * j + 0] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(ra[4 * j + 0])), sc[j].x));
+                ra[4 * j + 1] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(ra[4 * j + 1])), sc[j].y));
+                ra[4 * j + 2] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(ra[4 * j + 2])), sc[j].x));
+                ra[4 * j + 3] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(ra[4 * j + 3])), sc[j].y));
+                rb[4 * j + 0] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(rb[4 * j + 0])), sc[j].x));
+                rb[4 * j + 1] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(rb[4 * j + 1])), sc[j].y));
+                rb[4 * j + 2] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(rb[4 * j + 2])), sc[j].x));
+                rb[4 * j + 3] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(rb[4 * j + 3])), sc[j].y));
               }
             }
           }
-          // Walk the document ends inside this chunk in order.
-          int a = h0;
+          int a = c0;
           while (true) {
             const int e = sgi < nseg ? meta->seg_end[sgi] : 0x7FFF;
-            const int bnd = min(e, h1);
+            const int bnd = min(e, c1);
             if (bnd > a && tile_live) {
-              if (a == h0 && bnd == h0 + 64) {
-                // eight independent max chains (depth 4) instead of one chain of 32
+              if (a == c0 && bnd == c0 + 64) {
+                // whole chunk inside one document: two independent chains per row
                 if (kTokenScale) {
-                  float m[8];
-#pragma unroll
-                  for (int c = 0; c < 8; ++c) m[c] = fmaxf(__uint_as_float(r[2 * c]), __uint_as_float(r[2 * c + 1]));
-#pragma unroll
-                  for (int j = 16; j < 64; j += 16)
-#pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                      m[c] = fmax3(m[c], __uint_as_float(r[j + 2 * c]), __uint_as_float(r[j + 2 * c + 1]));
-                  run = fmax3(fmax3(m[0], m[1], m[2]), fmax3(m[3], m[4], m[5]), fmax3(m[6], m[7], run));
+#define MSB_ROWMAX(X, s, R)                                                                                \
+  {                                                                                                        \
+    float m0 = fmaxf(__uint_as_float(X[2 * s]), __uint_as_float(X[2 * s + 1]));                            \
+    float m1 = fmaxf(__uint_as_float(X[4 + 2 * s]), __uint_as_float(X[4 + 2 * s + 1]));                    \
+    _Pragma("unroll") for (int j = 2; j < 8; j += 2) {                                                     \
+      m0 = fmax3(m0, __uint_as_float(X[4 * j + 2 * s]), __uint_as_float(X[4 * j + 2 * s + 1]));            \
+      m1 = fmax3(m1, __uint_as_float(X[4 * j + 4 + 2 * s]), __uint_as_float(X[4 * j + 4 + 2 * s + 1]));    \
+    }                                                                                                      \
+    R = fmax3(R, m0, m1);                                                                                  \
+  }
+                  MSB_ROWMAX(ra, 0, run[0]) MSB_ROWMAX(ra, 1, run[1]) MSB_ROWMAX(rb, 0, run[2]) MSB_ROWMAX(rb, 1, run[3])
+#undef MSB_ROWMAX
                 } else {
-                  int32_t m[8];
-#pragma unroll
-                  for (int c = 0; c < 8; ++c) m[c] = max(static_cast<int32_t>(r[2 * c]), static_cast<int32_t>(r[2 * c + 1]));
-#pragma unroll
-                  for (int j = 16; j < 64; j += 16)
-#pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                      m[c] = __vimax3_s32(m[c], static_cast<int32_t>(r[j + 2 * c]), static_cast<int32_t>(r[j + 2 * c + 1]));
-                  run_i = __vimax3_s32(__vimax3_s32(m[0], m[1], m[2]), __vimax3_s32(m[3], m[4], m[5]),
-                                       __vimax3_s32(m[6], m[7], run_i));
+#define MSB_ROWMAXI(X, s, R)                                                                               \
+  {                                                                                                        \
+    int32_t m0 = max(static_cast<int32_t>(X[2 * s]), static_cast<int32_t>(X[2 * s + 1]));                  \
+    int32_t m1 = max(static_cast<int32_t>(X[4 + 2 * s]), static_cast<int32_t>(X[4 + 2 * s + 1]));          \
+    _Pragma("unroll") for (int j = 2; j < 8; j += 2) {                                                     \
+      m0 = __vimax3_s32(m0, static_cast<int32_t>(X[4 * j + 2 * s]), static_cast<int32_t>(X[4 * j + 2 * s + 1])); \
+      m1 = __vimax3_s32(m1, static_cast<int32_t>(X[4 * j + 4 + 2 * s]),                                   \
+                        static_cast<int32_t>(X[4 * j + 4 + 2 * s + 1]));                                   \
+    }                                                                                                      \
+    R = __vimax3_s32(R, m0, m1);                                                                           \
+  }
+                  MSB_ROWMAXI(ra, 0, run_i[0]) MSB_ROWMAXI(ra, 1, run_i[1]) MSB_ROWMAXI(rb, 0, run_i[2])
+                  MSB_ROWMAXI(rb, 1, run_i[3])
+#undef MSB_ROWMAXI
                 }
               } else {
-                const int la = a - h0, lb = bnd - h0;
+                const int la = a - c0 - 2 * tc, lb = bnd - c0 - 2 * tc;  // element (j, b) is column 8j + b here
 #pragma unroll
-                for (int j = 0; j < 64; ++j) {
-                  const bool in = j >= la && j < lb;
-                  if (kTokenScale) run = in ? fmaxf(run, __uint_as_float(r[j])) : run;
-                  else run_i = in ? max(run_i, static_cast<int32_t>(r[j])) : run_i;
+                for (int j = 0; j < 8; ++j) {
+#pragma unroll
+                  for (int b2 = 0; b2 < 2; ++b2) {
+                    const int cc = 8 * j + b2;
+                    const bool in = cc >= la && cc < lb;
+                    if (kTokenScale) {
+                      run[0] = in ? fmaxf(run[0], __uint_as_float(ra[4 * j + b2])) : run[0];
+                      run[1] = in ? fmaxf(run[1], __uint_as_float(ra[4 * j + 2 + b2])) : run[1];
+                      run[2] = in ? fmaxf(run[2], __uint_as_float(rb[4 * j + b2])) : run[2];
+                      run[3] = in ? fmaxf(run[3], __uint_as_float(rb[4 * j + 2 + b2])) : run[3];
+                    } else {
+                      run_i[0] = in ? max(run_i[0], static_cast<int32_t>(ra[4 * j + b2])) : run_i[0];
+                      run_i[1] = in ? max(run_i[1], static_cast<int32_t>(ra[4 * j + 2 + b2])) : run_i[1];
+                      run_i[2] = in ? max(run_i[2], static_cast<int32_t>(rb[4 * j + b2])) : run_i[2];
+                      run_i[3] = in ? max(run_i[3], static_cast<int32_t>(rb[4 * j + 2 + b2])) : run_i[3];
+                    }
+                  }
                 }
               }
             }
             if (bnd > a) a = bnd;
-            if (sgi >= nseg || e > h1) break;
-            // document meta->seg_doc[sgi] ends at column e: stage this row's value, scaled by the query scale
+            if (e > c1) break;  // the open document continues past this chunk (or no ends are left)
+            // document meta->seg_doc[sgi] ends: complete each row's maximum across the four threads
+            // holding it, stage the row value scaled by the query scale, flush finished documents.
             float best;
-            if (kTokenScale) best = run;
-            else best = run_i == INT32_MIN ? kLowest : __fadd_rn(__int2float_rn(run_i), neg_bias);
-            rowval[(pending * kG + g) * 128 + row] = row_valid ? __fmul_rn(best, qs) : 0.0F;
+            if (kTokenScale) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                run[i] = fmaxf(run[i], __shfl_xor_sync(0xFFFFFFFFu, run[i], 1));
+                run[i] = fmaxf(run[i], __shfl_xor_sync(0xFFFFFFFFu, run[i], 2));
+              }
+              best = tc == 0 ? run[0] : tc == 1 ? run[1] : tc == 2 ? run[2] : run[3];
+            } else {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                run_i[i] = max(run_i[i], __shfl_xor_sync(0xFFFFFFFFu, run_i[i], 1));
+                run_i[i] = max(run_i[i], __shfl_xor_sync(0xFFFFFFFFu, run_i[i], 2));
+              }
+              const int32_t bi = tc == 0 ? run_i[0] : tc == 1 ? run_i[1] : tc == 2 ? run_i[2] : run_i[3];
+              best = bi == INT32_MIN ? kLowest : __int2float_rn(bi);
+            }
+            rowval[(pending * kG + g) * 128 + wrow] = w_valid ? __fmul_rn(best, qs) : 0.0F;
             if (etid == 0) group_doc[pending] = meta->seg_doc[sgi];
-            run = kLowest;
-            run_i = INT32_MIN;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              run[i] = kLowest;
+              run_i[i] = INT32_MIN;
+            }
             ++sgi;
-            if (++pending == kSegGroup || (sgi == nseg && t0 + kTileN >= unit.tok_hi)) {
+            if (++pending == kSegGroup || (sgi == nseg && last_tile)) {
               named_bar(1, kEpiWarps * 32);
               for (int x = etid; x < pending * nq; x += kEpiWarps * 32) {
                 const int gd = x / nq, qx = x % nq;
@@ -610,7 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&acc_empty[acc.idx]);
+          if (!released) mbar_arrive(&acc_empty[acc.idx]);
           mbar_arrive(&m_empty[mst.idx]);
         }
         stg.next<kStages>();
@@ -754,7 +833,6 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   prm.offsets = d.offsets;
   prm.qwords = q.i8_words;
   prm.qscale = q.row_scale;
-  prm.qsum = q.row_sum;
   prm.units = d_units;
   prm.num_units = num_units;
   prm.batch = q.batch;
