@@ -227,7 +227,10 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--engine", type=int, default=0, help="0 auto, 1 SIMT, 2 tensor core")
+    ap.add_argument("--pages", type=int, default=NUM_PAGES,
+                    help="corpus pages (default: the C4 workload; smaller values are for profiling captures)")
     args = ap.parse_args()
+    globals()["NUM_PAGES"] = args.pages
     if args.warmup < 3:
         args.warmup = 3
 
@@ -410,7 +413,7 @@ def main() -> None:
         "vs_baseline": None,
         "dtype": "int8 x int4 (int32 accumulate, fp32 epilogue)",
         "data": "synthetic (seeded per-page centroid + noise, generated and packed on the GPU)",
-        "config": {"workload": WORKLOAD, "num_docs": NUM_PAGES, "num_tokens": NUM_PAGES * PAGE_TOKENS,
+        "config": {"workload": WORKLOAD if NUM_PAGES == 100_000 else f"profiling case: {NUM_PAGES} pages of the C4 distribution", "num_docs": NUM_PAGES, "num_tokens": NUM_PAGES * PAGE_TOKENS,
                    "batch": BATCH, "query_tokens": QUERY_TOKENS, "k": TOP_K,
                    "parallelism": f"document shards x{world} + NCCL all-gather merge",
                    "l2": "corpus 7.0 GB >> 126 MB L2; no flush between steps",

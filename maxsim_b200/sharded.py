@@ -106,11 +106,23 @@ class ShardedReranker:
         k_local = min(int(k), local_docs)
         if int(k) > self.info.num_docs_total:
             raise ValueError("k cannot exceed the number of documents")
-        buf = self._buffers(batch, k_local, query.device)
+        # Every rank contributes exactly k entries so the all-gather shapes agree; a shard with fewer
+        # than k documents pads with (-inf, INT64_MAX), which the merge order never selects while
+        # k <= the total number of documents.
         stream = t.cuda.current_stream(query.device).cuda_stream
-        self.local.topk_batch_device(query, k_local, buf["loc_s"], buf["loc_i"], int8_query=self.int8_query,
-                                     stream=stream)
-        buf["loc_i"].add_(self.info.doc_lo)
+        buf = self._buffers(batch, int(k), query.device)
+        if k_local == int(k):
+            self.local.topk_batch_device(query, k_local, buf["loc_s"], buf["loc_i"], int8_query=self.int8_query,
+                                         stream=stream)
+            buf["loc_i"].add_(self.info.doc_lo)
+        else:
+            part = self._buffers(batch, k_local, query.device)
+            self.local.topk_batch_device(query, k_local, part["loc_s"], part["loc_i"], int8_query=self.int8_query,
+                                         stream=stream)
+            buf["loc_s"].fill_(float("-inf"))
+            buf["loc_i"].fill_(np.iinfo(np.int64).max)
+            buf["loc_s"][:, :k_local].copy_(part["loc_s"])
+            buf["loc_i"][:, :k_local].copy_(part["loc_i"]).add_(self.info.doc_lo)
         if self.info.world_size == 1:
             buf["out_s"].copy_(buf["loc_s"])
             buf["out_i"].copy_(buf["loc_i"])
