@@ -50,9 +50,9 @@ SEED = 20260713
 CHUNK_PAGES = 2_000
 # DRAM bytes (read + write) of one tc_scan_kernel launch per corpus page, from one ncu capture of a
 # 2,000-page case of the same workload (profiles/tc_scan_kernel_2000pages_full.txt: 140.43 MB read +
-# 3.74 MB written).  The corpus is streamed once per launch and the score matrix grows with the pages,
+# 4.13 MB written).  The corpus is streamed once per launch and the score matrix grows with the pages,
 # so traffic scales with the pages a rank holds.
-TC_DRAM_BYTES_PER_PAGE = (140.430080e6 + 3.742208e6) / 2000
+TC_DRAM_BYTES_PER_PAGE = (140.431104e6 + 4.134400e6) / 2000
 WORKLOAD = ("C4: 100,000 pages x 1,030 tokens (dim 128) per-token int4 (6.59 GB codes + 0.41 GB scales); "
             "1,024 queries x 24 tokens int8, batch 64, full-scan top-10")
 
@@ -416,7 +416,7 @@ def main() -> None:
         "config": {"workload": WORKLOAD if NUM_PAGES == 100_000 else f"profiling case: {NUM_PAGES} pages of the C4 distribution", "num_docs": NUM_PAGES, "num_tokens": NUM_PAGES * PAGE_TOKENS,
                    "batch": BATCH, "query_tokens": QUERY_TOKENS, "k": TOP_K,
                    "parallelism": f"document shards x{world} + NCCL all-gather merge",
-                   "l2": "corpus 7.0 GB >> 126 MB L2; no flush between steps",
+                   "l2": f"corpus {NUM_PAGES * PAGE_TOKENS * (DIM // 2 + 4) / 1e9:.2f} GB vs 126 MB L2; no flush between steps",
                    "engine": ["auto", "simt", "tensor"][args.engine],
                    "step_ms_min": min(step_ms), "step_ms_max": max(step_ms)},
         "gpu_launches": int(launches),
