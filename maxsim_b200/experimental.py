@@ -2,9 +2,12 @@
 
 Public surface of the reference's int4 part of ``src/maxsim/experimental.py``
 (``Int4PackedDocs``, ``pack_int4_symmetric``, ``int4_to_device``,
-``int4_maxsim``, ``int4_maxsim_int8q``, ``topk_int4_maxsim``).  The
-centroid (``binary_q40``) and ternary experiments of that module are not part
-of this package.
+``int4_maxsim``, ``int4_maxsim_int8q``, ``topk_int4_maxsim``) and of its
+dimension-centroid binary format behind the ``binary_q40`` corpus mode
+(``DimCentroidCalibration``, ``fit_dim_centroid_calibration``,
+``pack_dim_centroid_signs``, ``transform_query_dim_centroids``,
+``dim_centroid_maxsim``, ``topk_dim_centroid_maxsim``).  The ternary
+experiments of that module are not part of this package.
 """
 
 from __future__ import annotations
@@ -250,3 +253,155 @@ def topk_int4_maxsim(query_tokens, packed: Int4PackedDocs, k: int, *, device="au
 
         scores, ids = _topk_with_options(handle, batches, int(k), reducer_value, weights, temperature_value)
     return (scores[0], ids[0]) if squeeze else (scores, ids)
+
+
+# ---------------------------------------------------------------------------
+# Dimension-centroid sign codes (corpus mode "binary_q40")
+# ---------------------------------------------------------------------------
+# A token's bit for dimension i says whether x_i >= t_i; the bit decodes to the
+# mean of the corpus values on its side of t_i (p_i above, n_i below).  With
+# s = 2 * bit - 1, decoded x_i = (p_i + n_i) / 2 + s * (p_i - n_i) / 2, so
+#   q . decoded(x) = 0.5 * sum_i q_i (p_i - n_i) s_i + 0.5 * sum_i q_i (p_i + n_i)
+# and MaxSim over documents needs only the sign scan of the query scaled by
+# (p - n); the second term is a per-query constant added after the scan
+# (reference ``src/maxsim/experimental.py:69-146``, ``:612-622``).
+
+@dataclass(frozen=True)
+class DimCentroidCalibration:
+    """Per-dimension threshold and the two decode values (fp32 ``[dim]`` each)."""
+
+    thresholds: np.ndarray
+    negative_centroids: np.ndarray
+    positive_centroids: np.ndarray
+
+    @property
+    def dim(self) -> int:
+        return int(self.thresholds.shape[0])
+
+    @property
+    def metadata_bytes(self) -> int:
+        return int(self.dim * 3 * 4)
+
+
+def _side_means(docs: np.ndarray, thresholds: np.ndarray):
+    """Mean (float64 accumulation, stored as fp32) of each column at/above and below its threshold;
+    an empty side decodes to the threshold itself."""
+    negative = np.empty(docs.shape[1], dtype=np.float32)
+    positive = np.empty(docs.shape[1], dtype=np.float32)
+    for i in range(docs.shape[1]):
+        col = docs[:, i]
+        above = col >= thresholds[i]
+        hi, lo = col[above], col[~above]
+        positive[i] = np.float32(np.mean(hi, dtype=np.float64)) if hi.size else np.float32(thresholds[i])
+        negative[i] = np.float32(np.mean(lo, dtype=np.float64)) if lo.size else np.float32(thresholds[i])
+    return negative, positive
+
+
+def _thresholds_for(thresholds, dim: int) -> np.ndarray:
+    if thresholds is None:
+        return np.zeros(dim, dtype=np.float32)
+    t = _as_numpy(thresholds).astype(np.float32, copy=False)
+    if t.ndim != 1 or t.shape[0] != dim:
+        raise ValueError("thresholds must have shape [dim]")
+    return np.ascontiguousarray(t, dtype=np.float32)
+
+
+def fit_dim_centroid_calibration(doc_embeddings, *, thresholds=None, lloyd_iterations: int = 0) -> DimCentroidCalibration:
+    """Fit the decode values for given thresholds (default 0), optionally refining the thresholds
+    to the midpoints of the decode values (Lloyd iterations, stopping when they move < 1e-6)."""
+    docs = _as_numpy(doc_embeddings).astype(np.float32, copy=False)
+    if docs.ndim != 2:
+        raise ValueError("doc_embeddings must have shape [num_doc_tokens, dim]")
+    if docs.shape[1] % 8 != 0:
+        raise ValueError("dim must be divisible by 8")
+    if lloyd_iterations < 0:
+        raise ValueError("lloyd_iterations must be >= 0")
+    t = _thresholds_for(thresholds, docs.shape[1])
+    negative, positive = _side_means(docs, t)
+    for _ in range(lloyd_iterations):
+        mid = ((negative + positive) * 0.5).astype(np.float32)
+        negative, positive = _side_means(docs, mid)
+        converged = np.allclose(mid, t, rtol=0.0, atol=1e-6)
+        t = mid
+        if converged:
+            break
+    return DimCentroidCalibration(thresholds=np.ascontiguousarray(t, dtype=np.float32),
+                                  negative_centroids=np.ascontiguousarray(negative, dtype=np.float32),
+                                  positive_centroids=np.ascontiguousarray(positive, dtype=np.float32))
+
+
+def _check_calibration(calibration, dim: int | None = None) -> None:
+    if not isinstance(calibration, DimCentroidCalibration):
+        raise TypeError("calibration must be a DimCentroidCalibration instance")
+    if calibration.thresholds.ndim != 1:
+        raise ValueError("calibration thresholds must be one-dimensional")
+    want = calibration.thresholds.shape[0] if dim is None else int(dim)
+    for name, values in (("negative_centroids", calibration.negative_centroids),
+                         ("positive_centroids", calibration.positive_centroids)):
+        if values.ndim != 1 or values.shape[0] != want:
+            raise ValueError(f"calibration {name} must have shape [dim]")
+    if calibration.thresholds.shape[0] != want:
+        raise ValueError("calibration thresholds must have shape [dim]")
+
+
+def pack_dim_centroid_signs(doc_embeddings, doc_offsets=None, *, calibration: DimCentroidCalibration | None = None,
+                            thresholds=None, lloyd_iterations: int = 0, device: str = "cpu"):
+    """Sign bits of ``x - thresholds`` plus the calibration used (fitted when not given)."""
+    from maxsim_b200._api import pack_signs
+
+    docs = _as_numpy(doc_embeddings).astype(np.float32, copy=False)
+    if calibration is None:
+        calibration = fit_dim_centroid_calibration(docs, thresholds=thresholds, lloyd_iterations=lloyd_iterations)
+    _check_calibration(calibration, docs.shape[1])
+    shifted = docs - calibration.thresholds[np.newaxis, :]
+    return pack_signs(shifted, doc_offsets, device=device), calibration
+
+
+def transform_query_dim_centroids(query_tokens, calibration: DimCentroidCalibration) -> np.ndarray:
+    """Query scaled per dimension by (positive - negative) decode values, fp32."""
+    _check_calibration(calibration)
+    q = _as_numpy(query_tokens).astype(np.float32, copy=False)
+    if q.ndim not in (2, 3):
+        raise ValueError("query_tokens must have shape [query_tokens, dim] or [batch, query_tokens, dim]")
+    if q.shape[-1] != calibration.dim:
+        raise ValueError(f"query dim={q.shape[-1]} does not match calibration dim={calibration.dim}")
+    return np.ascontiguousarray(q * (calibration.positive_centroids - calibration.negative_centroids),
+                                dtype=np.float32)
+
+
+def _restore_centroid_scores(scores, query_tokens, calibration: DimCentroidCalibration) -> np.ndarray:
+    """scan score * 0.5 + 0.5 * sum(q * (positive + negative)) per query (float64 sum, fp32 result)."""
+    s = _as_numpy(scores).astype(np.float32, copy=False)
+    q = _as_numpy(query_tokens).astype(np.float32, copy=False)
+    mid = calibration.positive_centroids + calibration.negative_centroids
+    if q.ndim == 2:
+        const = np.float32(0.5 * np.sum(q * mid[np.newaxis, :], dtype=np.float64))
+        return np.asarray(s * 0.5 + const, dtype=np.float32)
+    if q.ndim == 3:
+        const = 0.5 * np.sum(q * mid[np.newaxis, np.newaxis, :], axis=(1, 2), dtype=np.float64)
+        return np.asarray(s * 0.5 + const[:, np.newaxis].astype(np.float32), dtype=np.float32)
+    raise ValueError("query_tokens must have shape [query_tokens, dim] or [batch, query_tokens, dim]")
+
+
+def dim_centroid_maxsim(query_tokens, packed, calibration: DimCentroidCalibration, *, device="auto",
+                        restore_scores: bool = True, candidate_indices=None):
+    """MaxSim of every document (or of candidates) against dimension-centroid sign codes (GPU scan)."""
+    from maxsim_b200._api import maxsim
+
+    scores = maxsim(transform_query_dim_centroids(query_tokens, calibration), packed, device=device,
+                    candidate_indices=candidate_indices)
+    return _restore_centroid_scores(scores, query_tokens, calibration) if restore_scores else scores
+
+
+def topk_dim_centroid_maxsim(query_tokens, packed, calibration: DimCentroidCalibration, k: int, *, device="auto",
+                             restore_scores: bool = True):
+    """Top-k over dimension-centroid sign codes (scan + top-k on the GPU, ties to the lower id).
+
+    The restore is an increasing affine map per query, so the order of the scan scores is the
+    order of the restored scores."""
+    from maxsim_b200._api import topk_maxsim
+
+    scores, ids = topk_maxsim(transform_query_dim_centroids(query_tokens, calibration), packed, k, device=device)
+    if restore_scores:
+        scores = _restore_centroid_scores(scores, query_tokens, calibration)
+    return scores, ids

@@ -7,9 +7,10 @@ npz layout (schema 2, readable schema 1), ``memory_report``,
 ``rescore_candidates`` for ``int4_residual``) and ``rerank``.
 
 All scoring runs on the GPU through ``libmaxsim_b200.so``; ``device="cpu"``
-raises ``NotImplementedError``.  ``pooled_binary`` corpora (built by Ward
-pooling) and ``binary_q40`` corpora are loadable/searchable as written by the
-reference only where noted below.
+raises ``NotImplementedError``.  ``pooled_binary`` corpora are built by Ward
+pooling of each document's tokens; ``binary_q40`` corpora carry a
+dimension-centroid calibration (40th-percentile thresholds) and are scored by
+the sign scan on the calibrated query.
 """
 
 from __future__ import annotations
@@ -32,7 +33,12 @@ from maxsim_b200.cascade import (
     residual_score,
 )
 from maxsim_b200.experimental import (
+    DimCentroidCalibration,
     Int4PackedDocs,
+    dim_centroid_maxsim,
+    fit_dim_centroid_calibration,
+    pack_dim_centroid_signs,
+    topk_dim_centroid_maxsim,
     _validate_int4_data_matches_values,
     _validate_int4_packed,
     int4_maxsim,
@@ -83,25 +89,35 @@ class SearchResult:
 
 
 def _pool_doc_tokens(docs: np.ndarray, offsets: np.ndarray, pool_factor: int):
-    """Ward-pool each document's tokens into ceil(n / pool_factor) cluster means."""
+    """Pool each document's tokens into ceil(n / pool_factor) clusters (reference
+    src/maxsim/pooling.py:18-62): Ward linkage on the L2-normalised tokens, at most that
+    many clusters, each replaced by the float64-accumulated mean of its raw tokens, in
+    cluster-label order.  Documents already at or below the target keep their tokens."""
+    if pool_factor < 1:
+        raise ValueError("factor must be >= 1")
+    if pool_factor == 1:
+        return docs.copy(), offsets.copy()
     from scipy.cluster.hierarchy import fcluster, linkage
 
-    pooled, lengths = [], []
+    pieces, lengths = [], []
     for d in range(offsets.shape[0] - 1):
-        s, e = int(offsets[d]), int(offsets[d + 1])
-        tokens = docs[s:e]
+        tokens = docs[int(offsets[d]):int(offsets[d + 1])]
         n = tokens.shape[0]
-        target = max(1, -(-n // pool_factor)) if n else 0
-        if n <= 1 or target >= n:
-            pooled.append(tokens)
+        target = max(1, -(-n // pool_factor))
+        if n == 0 or n <= target:
+            pieces.append(tokens.astype(np.float32, copy=True))
             lengths.append(n)
             continue
-        labels = fcluster(linkage(tokens.astype(np.float64), method="ward"), t=target, criterion="maxclust")
-        groups = [tokens[labels == c].mean(axis=0) for c in np.unique(labels)]
-        pooled.append(np.stack(groups).astype(np.float32))
-        lengths.append(len(groups))
+        unit = tokens / np.maximum(np.linalg.norm(tokens, axis=1, keepdims=True), 1e-12)
+        labels = fcluster(linkage(unit, method="ward"), t=target, criterion="maxclust")
+        count = int(labels.max())
+        means = np.empty((count, tokens.shape[1]), dtype=np.float32)
+        for c in range(count):
+            means[c] = tokens[labels == c + 1].mean(axis=0, dtype=np.float64)
+        pieces.append(means)
+        lengths.append(count)
     out_offsets = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
-    out = np.concatenate(pooled, axis=0) if pooled else np.zeros((0, docs.shape[1]), np.float32)
+    out = np.concatenate(pieces, axis=0) if pieces else np.zeros((0, docs.shape[1]), np.float32)
     return np.ascontiguousarray(out, dtype=np.float32), out_offsets
 
 
@@ -141,7 +157,11 @@ class Corpus:
                     "binary_token_scale_u4": "mean_abs_u4"}[mode]
             return cls(doc_ids=ids, mode=mode, packed=pack_signs(docs, offs, token_scale=kind), metadata=meta)
         if mode == "binary_q40":
-            raise NotImplementedError("binary_q40 (dimension-centroid calibration) is not part of maxsim_b200")
+            # per-dimension 40th-percentile thresholds of the corpus (reference src/maxsim/sdk.py:164-174)
+            thresholds = np.percentile(docs, 40.0, axis=0).astype(np.float32)
+            calibration = fit_dim_centroid_calibration(docs, thresholds=thresholds)
+            packed, calibration = pack_dim_centroid_signs(docs, offs, calibration=calibration)
+            return cls(doc_ids=ids, mode=mode, packed=packed, calibration=calibration, metadata=meta)
         if mode == "int4":
             return cls(doc_ids=ids, mode=mode, int4_packed=pack_int4_symmetric(docs, offs), metadata=meta)
         if mode == "int4_per_token":
@@ -188,6 +208,12 @@ class Corpus:
                     arrays["token_scale_u4_count"] = np.array(len(codes), dtype=np.int64)
                 else:
                     arrays["token_scale_fp16"] = np.ascontiguousarray(ts, dtype=np.float16)
+            if self.calibration is not None:
+                arrays.update({
+                    "centroid_thresholds": np.ascontiguousarray(self.calibration.thresholds, dtype=np.float32),
+                    "centroid_negative": np.ascontiguousarray(self.calibration.negative_centroids, dtype=np.float32),
+                    "centroid_positive": np.ascontiguousarray(self.calibration.positive_centroids, dtype=np.float32),
+                })
         elif self.int4_packed is not None and self.mode == "int4_residual":
             p = self.int4_packed
             if p.device != "cpu":
@@ -236,8 +262,12 @@ class Corpus:
                 raise ValueError("serialized doc_offsets must contain integers")
             offsets = np.ascontiguousarray(raw_offsets, dtype=np.int64)
             dim = int(np.asarray(data["dim"]).item())
+            calibration = None
             if mode == "binary_q40":
-                raise NotImplementedError("binary_q40 (dimension-centroid calibration) is not part of maxsim_b200")
+                calibration = DimCentroidCalibration(
+                    thresholds=np.ascontiguousarray(data["centroid_thresholds"], dtype=np.float32),
+                    negative_centroids=np.ascontiguousarray(data["centroid_negative"], dtype=np.float32),
+                    positive_centroids=np.ascontiguousarray(data["centroid_positive"], dtype=np.float32))
             if mode in _BINARY_MODES:
                 token_scale = None
                 if "token_scale_fp16" in data:
@@ -255,7 +285,8 @@ class Corpus:
                 corpus = cls(doc_ids=ids, mode=mode, packed=PackedDocs(
                     data=_load_u8(data, "packed_data"), doc_offsets=offsets, dim=dim, num_docs=len(ids),
                     scale=_decode_scale(str(np.asarray(data["scale_kind"]).item()), np.asarray(data["scale_values"])),
-                    device="cpu", token_scale=token_scale), metadata=metadata, _source_path=source)
+                    device="cpu", token_scale=token_scale), calibration=calibration, metadata=metadata,
+                    _source_path=source)
                 _validate_corpus(corpus)
                 return corpus
             if mode == "int4_residual":
@@ -301,7 +332,7 @@ class Corpus:
     @property
     def encoded_bytes(self) -> int:
         if self.packed is not None:
-            extra = 0
+            extra = 0 if self.calibration is None else int(self.calibration.metadata_bytes)
             if isinstance(self.packed.scale, np.ndarray):
                 extra += int(self.packed.scale.astype(np.float32, copy=False).nbytes)
             elif self.packed.scale is not None:
@@ -372,6 +403,10 @@ class Reranker:
         if rescore_candidates is not None and mode != "int4_residual":
             raise ValueError("rescore_candidates requires corpus mode='int4_residual'")
         kw = dict(reducer=reducer, query_weights=query_weights, temperature=temperature)
+        if mode == "binary_q40":
+            _require_maxsim_reducer(mode, reducer, query_weights, temperature)
+            return topk_dim_centroid_maxsim(query_embeddings, self.corpus.packed, self.corpus.calibration, k,
+                                            device="auto")
         if mode in _BINARY_MODES:
             return topk_maxsim(query_embeddings, self.corpus.packed, k, device="auto", **kw)
         if mode == "int4_residual":
@@ -405,6 +440,10 @@ class Reranker:
         kw = dict(device="auto", reducer=reducer, query_weights=query_weights, temperature=temperature,
                   candidate_indices=candidate_indices)
         mode = self.corpus.mode
+        if mode == "binary_q40":
+            _require_maxsim_reducer(mode, reducer, query_weights, temperature)
+            return dim_centroid_maxsim(query_embeddings, self.corpus.packed, self.corpus.calibration, device="auto",
+                                       candidate_indices=candidate_indices)
         if mode in _BINARY_MODES:
             return maxsim(query_embeddings, self.corpus.packed, **kw)
         if mode in _INT4_MODES:
@@ -536,7 +575,17 @@ def _validate_corpus(corpus: Corpus) -> None:
         if needs != (p.token_scale is not None):
             raise ValueError(f"mode {corpus.mode!r} {'requires' if needs else 'does not accept'} binary token scales")
         _validate_token_scale(p.token_scale, num_tokens, "packed.token_scale")
+        if corpus.mode == "binary_q40":
+            if corpus.calibration is None:
+                raise ValueError("binary_q40 mode requires centroid calibration")
+            _validate_calibration_values(corpus.calibration, p.dim)
+        elif corpus.calibration is not None:
+            raise ValueError("centroid calibration is only valid for binary_q40 mode")
         return
+    if corpus.calibration is not None and corpus.mode in _INT4_MODES:
+        raise ValueError("centroid calibration is not valid for int4 modes")
+    if corpus.calibration is not None and corpus.mode == "int4_residual":
+        raise ValueError("centroid calibration is not valid for int4_residual")
     if corpus.mode in _INT4_MODES:
         p = corpus.int4_packed
         if p is None or corpus.packed is not None:
@@ -560,6 +609,30 @@ def _validate_corpus(corpus: Corpus) -> None:
             raise ValueError("residual int4 num_docs must match corpus.doc_ids")
         return
     raise ValueError(f"unsupported corpus mode: {corpus.mode}")
+
+
+def _validate_calibration_values(calibration, dim: int) -> None:
+    """Shape and finiteness of a binary_q40 calibration (reference src/maxsim/sdk.py:897-903)."""
+    for name in ("thresholds", "negative_centroids", "positive_centroids"):
+        values = getattr(calibration, name, None)
+        if not isinstance(values, np.ndarray) or values.ndim != 1 or values.shape[0] != dim:
+            raise ValueError(f"calibration.{name} must have shape [dim]")
+        if not np.all(np.isfinite(values)):
+            raise ValueError(f"calibration.{name} must contain finite values")
+
+
+def _require_maxsim_reducer(mode: str, reducer, query_weights, temperature) -> None:
+    """Corpus modes scored by a transformed query support plain MaxSim only (reference sdk.py:1103-1113)."""
+    if reducer != "maxsim":
+        raise ValueError(f"corpus mode '{mode}' currently supports only reducer='maxsim'")
+    if query_weights is not None:
+        raise ValueError("query_weights is only supported with reducer='weighted_maxsim'")
+    try:
+        t = float(temperature)
+    except (TypeError, ValueError) as exc:
+        raise ValueError("temperature must be a finite value greater than 0") from exc
+    if not np.isfinite(t) or t <= 0.0:
+        raise ValueError("temperature must be a finite value greater than 0")
 
 
 def _validate_serialized_offsets(offsets, num_docs, data, dim, *, bytes_per_token):
@@ -589,6 +662,11 @@ def _host_array_bytes(corpus: Corpus) -> int:
     if corpus.packed is not None:
         p = corpus.packed
         for a in (p.data, p.doc_offsets, p.scale, p.token_scale):
+            if isinstance(a, np.ndarray):
+                arrays.append(a)
+    if corpus.calibration is not None:
+        for name in ("thresholds", "negative_centroids", "positive_centroids"):
+            a = getattr(corpus.calibration, name, None)
             if isinstance(a, np.ndarray):
                 arrays.append(a)
     if corpus.int4_packed is not None:

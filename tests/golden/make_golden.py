@@ -19,6 +19,7 @@ It imports the reference's Python package from ``<reference>/src`` (with the
 * ``index_<mode>.npz`` -- ``Index.save`` files written by the reference for
                        every corpus mode (npz layout golden)
 * ``sdk_search.json`` -- ``Reranker(device="cpu").search`` results
+* ``sdk_rerank.json`` -- ``Reranker(device="cpu").rerank`` results on a candidate list
 
 The fixtures are committed; the GPU box never needs the reference.
 """
@@ -179,12 +180,18 @@ def main() -> None:
     ids = [f"doc-{i}" for i in range(6)]
     search = {}
     iq = np.random.default_rng(18).standard_normal((2, 3, 128)).astype(np.float32)
+    rerank = {}
     for mode in ("binary", "binary_token_scale", "binary_token_scale_u8", "binary_token_scale_u4", "int4",
-                 "int4_per_token", "int4_residual", "max_speed", "balanced", "compact", "max_quality", "auto"):
+                 "int4_per_token", "int4_residual", "max_speed", "balanced", "compact", "max_quality", "auto",
+                 "binary_q40", "pooled_binary", "max_compression"):
         idx = ms.Index.from_embeddings(ids, i_docs, i_off, mode=mode, metadata={"seed": 17})
         idx.save(HERE / f"index_{mode}.npz")
-        res = ms.Reranker(idx, device="cpu").search(iq, k=3)
+        reranker = ms.Reranker(idx, device="cpu")
+        res = reranker.search(iq, k=3)
         search[mode] = [[(r.doc_id, float(r.score), r.rank) for r in row] for row in res]
+        rr = reranker.rerank(iq, ["doc-4", "doc-1", "doc-5", "doc-1"], k=2)
+        rerank[mode] = [[(r.doc_id, float(r.score), r.rank) for r in row] for row in rr]
+    (HERE / "sdk_rerank.json").write_text(json.dumps(rerank, indent=1, sort_keys=True))
     np.savez_compressed(HERE / "index_inputs.npz", docs=i_docs, offsets=i_off, query=iq)
     (HERE / "sdk_search.json").write_text(json.dumps(search, indent=1, sort_keys=True))
     print("golden fixtures written to", HERE)

@@ -198,6 +198,21 @@ def test_sdk_search_matches_reference_golden(engine):
             assert [r.rank for r in grow] == [1, 2, 3]
 
 
+def test_sdk_rerank_matches_reference_golden(engine):
+    """Reranker.rerank on a candidate list with a duplicate id, every corpus mode."""
+    import maxsim_b200 as m
+
+    want = json.loads((GOLDEN / "sdk_rerank.json").read_text())
+    inputs = np.load(GOLDEN / "index_inputs.npz")
+    for mode, rows in want.items():
+        reranker = m.Reranker.load(GOLDEN / f"index_{mode}.npz", device="cuda")
+        got = reranker.rerank(inputs["query"], ["doc-4", "doc-1", "doc-5", "doc-1"], k=2)
+        for grow, wrow in zip(got, rows):
+            assert [r.doc_id for r in grow] == [w[0] for w in wrow], mode
+            np.testing.assert_allclose([r.score for r in grow], [w[1] for w in wrow], rtol=RTOL, atol=ATOL)
+            assert [r.rank for r in grow] == [w[2] for w in wrow], mode
+
+
 def test_sdk_int8_query_search_and_rerank(engine):
     import maxsim_b200 as m
 

@@ -184,3 +184,27 @@ def test_index_files_have_reference_layout():
         assert int(z["schema_version"]) == 2
         assert str(z["format"]) == "maxsim_corpus"
         assert z["int4_data"].dtype == np.uint8 and z["int4_token_scale"].dtype == np.float32
+
+
+@pytest.mark.parametrize("mode", ["binary", "binary_token_scale", "binary_token_scale_u8", "binary_token_scale_u4",
+                                  "int4", "int4_per_token", "int4_residual", "binary_q40", "pooled_binary",
+                                  "max_compression", "max_speed", "balanced", "compact", "max_quality", "auto"])
+def test_index_from_embeddings_writes_the_reference_arrays(tmp_path, mode):
+    """Index.from_embeddings + save (host packing, calibration, pooling) reproduces the
+    npz arrays the reference wrote for the same inputs, key for key."""
+    from pathlib import Path
+
+    import maxsim_b200 as m
+
+    gdir = Path(__file__).parent / "golden"
+    inp = np.load(gdir / "index_inputs.npz")
+    ids = [f"doc-{i}" for i in range(len(inp["offsets"]) - 1)]
+    idx = m.Index.from_embeddings(ids, inp["docs"], inp["offsets"], mode=mode, metadata={"seed": 17})
+    idx.save(tmp_path / "out.npz")
+    with np.load(gdir / f"index_{mode}.npz") as want, np.load(tmp_path / "out.npz") as got:
+        assert set(got.keys()) == set(want.keys()), mode
+        for k in want.keys():
+            if k == "metadata_json":
+                assert json.loads(str(got[k])) == json.loads(str(want[k])), mode
+            else:
+                np.testing.assert_array_equal(got[k], want[k], err_msg=f"{mode}:{k}")
