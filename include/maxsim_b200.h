@@ -65,7 +65,7 @@ typedef struct msb_score_opts {
   const float* weights;       /* weighted MaxSim: [weight_rows, query_tokens] */
   int32_t weight_rows;        /* 1 (shared) or batch */
   float temperature;          /* SmoothSim temperature, > 0 */
-  int32_t use_residual;       /* int4 handles: fused two-stream residual similarity */
+  int32_t use_residual;       /* handles with a residual stream: fused two-stream residual similarity */
   int32_t use_token_scale;    /* binary handles: apply the resident per-token scales */
   int32_t use_doc_scale;      /* binary handles: apply the resident per-document scales */
   float scale;                /* binary handles: scalar document scale (ignored with doc scales) */
@@ -120,7 +120,10 @@ int msb_docs_clear_token_scales(msb_docs* docs);
 /* set_scale_vector / clear_scale_vector (reference :1943-1956). */
 int msb_docs_set_doc_scales(msb_docs* docs, const float* scales, int64_t count);
 int msb_docs_clear_doc_scales(msb_docs* docs);
-/* set_residual_int4 / clear_residual_int4 (reference :2777-2833). */
+/* set_residual_int4 / clear_residual_int4 (reference :2777-2833).  codes are int4 [num_tokens, dim/2]
+ * for both formats.  On a binary handle the residual completes a sign-bit prefix whose per-token
+ * reconstruction scale is the handle's token scale vector (scale must be 1); that two-stream format has
+ * no counterpart in the reference, whose residual cascade uses an int4 prefix. */
 int msb_docs_set_residual(msb_docs* docs, const uint8_t* codes, int64_t num_tokens, float scale,
                           const float* token_scales);
 int msb_docs_clear_residual(msb_docs* docs);
@@ -140,7 +143,9 @@ int msb_docs_topk(msb_docs* docs, const float* query, int32_t batch, int32_t que
                   const msb_score_opts* opts, float* out_scores, int64_t* out_ids);
 /* Residual cascade (reference src/maxsim/cascade.py:294-417) entirely on the
  * device: prefix scan, per-row top-M, fused residual rescoring of each row's
- * candidates, final top-k with ties broken by candidate document id. */
+ * candidates, final top-k with ties broken by candidate document id.  On a
+ * binary handle with a residual stream the prefix is the sign scan scaled by the
+ * per-token reconstruction scale. */
 int msb_docs_cascade_topk(msb_docs* docs, const float* query, int32_t batch, int32_t query_tokens, int32_t k,
                           int32_t candidates, const msb_score_opts* opts, float* out_scores, int64_t* out_ids);
 

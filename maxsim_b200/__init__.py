@@ -5,7 +5,7 @@ Drop-in for the reference ``maxsim`` package's GPU path: the same public names
 ``to_device``, ``score``, ``maxsim``, ``topk_maxsim``, the residual cascade
 API) over ``libmaxsim_b200.so``.  ``maxsim_b200._maxsim_cuda`` reproduces the
 reference's native extension module and can be installed as
-``maxsim._maxsim_cuda`` (see INTEGRATION.md).
+``maxsim._maxsim_cuda``.
 
 Importing the package loads the CUDA library; it fails loudly when the library
 has not been built -- there is no CPU fallback.
@@ -13,7 +13,13 @@ has not been built -- there is no CPU fallback.
 
 from maxsim_b200._api import PackedDocs, maxsim, pack_signs, score, to_device, topk_maxsim
 from maxsim_b200.cascade import (
+    BinaryResidualPackedDocs,
     ResidualInt4PackedDocs,
+    binary_cascade_topk,
+    binary_prefix_score,
+    binary_residual_score,
+    binary_residual_to_device,
+    pack_binary_residual_int4,
     cascade_topk,
     pack_residual_int4,
     prefix_score,
@@ -22,7 +28,13 @@ from maxsim_b200.cascade import (
     residual_score,
 )
 from maxsim_b200.experimental import (
+    DimCentroidCalibration,
     Int4PackedDocs,
+    dim_centroid_maxsim,
+    fit_dim_centroid_calibration,
+    pack_dim_centroid_signs,
+    topk_dim_centroid_maxsim,
+    transform_query_dim_centroids,
     int4_maxsim,
     int4_maxsim_int8q,
     int4_to_device,
@@ -57,4 +69,16 @@ __all__ = [
     "prefix_topk",
     "residual_score",
     "cascade_topk",
+    "DimCentroidCalibration",
+    "fit_dim_centroid_calibration",
+    "pack_dim_centroid_signs",
+    "transform_query_dim_centroids",
+    "dim_centroid_maxsim",
+    "topk_dim_centroid_maxsim",
+    "BinaryResidualPackedDocs",
+    "pack_binary_residual_int4",
+    "binary_residual_to_device",
+    "binary_prefix_score",
+    "binary_residual_score",
+    "binary_cascade_topk",
 ]

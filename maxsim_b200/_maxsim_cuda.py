@@ -379,6 +379,56 @@ class CudaPackedDocs(_Handle):
         return self._topk(q, k, self._binary_opts(scale, use_scale_vector, use_token_scale, query_mode=_lib.QUERY_I8))
 
 
+    # -- sign-bit prefix + int4 residual (two-stream format with no counterpart in the reference) --
+    @property
+    def has_residual_int4(self):
+        return bool(self._info().has_residual)
+
+    def set_residual_int4(self, packed, token_scales):
+        """Per-token int4 residual [num_doc_tokens, dim / 2] completing the sign prefix, whose per-token
+        reconstruction scale is this handle's token scale vector."""
+        p = _u8(packed)
+        if p.ndim != 2 or p.shape[0] != self.num_tokens or p.shape[1] != self._dim // 2:
+            raise ValueError("residual packed data must have shape [num_doc_tokens, dim / 2]")
+        ts = _f32(token_scales)
+        if ts.ndim != 1 or ts.shape[0] != self.num_tokens:
+            raise ValueError("residual token scale vector must have shape [num_doc_tokens]")
+        check(lib.msb_docs_set_residual(self._h, _vp(p), p.shape[0], ctypes.c_float(1.0), _vp(ts)))
+
+    def clear_residual_int4(self):
+        check(lib.msb_docs_clear_residual(self._h))
+
+    def _residual(self, query, candidates, reducer, query_weights, temperature):
+        q = _check_query3(query, self._dim)
+        rid, w, rows, temp = _reducer_opts(reducer, query_weights, temperature, q.shape[0], q.shape[1])
+        if not self.has_residual_int4 and q.shape[0] and q.shape[1]:
+            raise ValueError("residual int4 data was requested but is not loaded on this CUDA handle")
+        return self._score(q, _opts(reducer=rid, weights=w, weight_rows=rows, temperature=temp, use_residual=True),
+                           candidates)
+
+    def score_residual_batch(self, query, reducer="maxsim", query_weights=None, temperature=1.0):
+        return self._residual(query, None, reducer, query_weights, temperature)
+
+    def score_residual_candidates_batch(self, query, candidate_indices, reducer="maxsim", query_weights=None,
+                                        temperature=1.0):
+        cands = _i64(candidate_indices)
+        if cands.ndim != 1:
+            raise ValueError("candidate_indices must be a 1-D array")
+        return self._residual(query, cands, reducer, query_weights, temperature)
+
+    def cascade_topk_batch(self, query, k, candidates, reducer="maxsim", query_weights=None, temperature=1.0):
+        """Sign-prefix scan -> per-row top-M -> fused residual rescoring -> top-k, on the device."""
+        q = _check_query3(query, self._dim)
+        rid, w, rows, temp = _reducer_opts(reducer, query_weights, temperature, q.shape[0], q.shape[1])
+        k, m = int(k), int(candidates)
+        scores = np.empty((q.shape[0], k), dtype=np.float32)
+        ids = np.empty((q.shape[0], k), dtype=np.int64)
+        opts = _opts(reducer=rid, weights=w, weight_rows=rows, temperature=temp)
+        check(lib.msb_docs_cascade_topk(self._h, _vp(q), q.shape[0], q.shape[1], k, m, ctypes.byref(opts),
+                                        _vp(scores), _vp(ids)))
+        return scores, ids
+
+
 class CudaInt4PackedDocs(_Handle):
     """int4 (tensor or per-token scale, optional residual stream) corpus on the GPU
     (reference ``CudaInt4PackedDocs``)."""

@@ -259,3 +259,123 @@ def cascade_topk(query_tokens, packed: ResidualInt4PackedDocs, k: int, *, candid
     scores, ids = resident.prefix_data.cascade_topk_batch(batches, int(k), int(candidates), reducer, weights,
                                                           temperature_value)
     return (scores[0], ids[0]) if squeeze else (scores, ids)
+
+
+# ---------------------------------------------------------------------------
+# Binary-prefix cascade: sign bits scaled by a per-token reconstruction scale,
+# plus a per-token int4 residual.  The reference's residual cascade uses an int4
+# prefix only; this two-stream format is the benchmark's binary-prefix variant
+# (16 B + 4 B per token for the prefix scan, 32 B + 4 B more for rescoring).
+# ---------------------------------------------------------------------------
+
+@dataclass(frozen=True)
+class BinaryResidualPackedDocs:
+    prefix_data: object                 # sign bits uint8 [N, dim/8] (bit i of byte i/8, x >= 0 -> 1) or a handle
+    prefix_token_scale: np.ndarray      # per-token mean |x|: the sign reconstruction scale
+    residual_data: object | None        # int4 [N, dim/2] of x - mean|x| * sign(x)
+    residual_values: np.ndarray | None
+    residual_token_scale: np.ndarray
+    doc_offsets: np.ndarray
+    dim: int
+    num_docs: int
+    device: str = "cpu"
+
+    @property
+    def num_tokens(self) -> int:
+        return int(self.doc_offsets[-1])
+
+    @property
+    def storage_bytes(self) -> int:
+        n = self.num_tokens
+        return int(n * self.dim // 8 + n * self.dim // 2 + self.prefix_token_scale.nbytes +
+                   self.residual_token_scale.nbytes)
+
+
+def pack_binary_residual_int4(doc_embeddings, doc_offsets=None) -> BinaryResidualPackedDocs:
+    """Sign bits with per-token mean |x| reconstruction scale, and the per-token int4 residual."""
+    from maxsim_b200._api import _mean_abs, _normalize_offsets, _sign_bits
+
+    x = _as_numpy(doc_embeddings).astype(np.float32, copy=False)
+    if x.ndim != 2:
+        raise ValueError("doc_embeddings must have shape [num_doc_tokens, dim]")
+    if x.shape[1] % 8 != 0:
+        raise ValueError("dim must be divisible by 8")
+    offsets = _normalize_offsets(doc_offsets, x.shape[0])
+    ps = _mean_abs(x)
+    signs = np.where(x >= 0, np.float32(1.0), np.float32(-1.0))
+    residual = (x - ps[:, np.newaxis] * signs).astype(np.float32)
+    rpk = pack_int4_symmetric(residual, offsets, scale_granularity="token")
+    return BinaryResidualPackedDocs(prefix_data=_sign_bits(x), prefix_token_scale=ps, residual_data=rpk.data,
+                                    residual_values=rpk.values, residual_token_scale=rpk.token_scale,
+                                    doc_offsets=offsets, dim=int(x.shape[1]), num_docs=int(offsets.shape[0] - 1))
+
+
+def binary_residual_to_device(packed: BinaryResidualPackedDocs, device: str = "cuda") -> BinaryResidualPackedDocs:
+    """Upload both streams to one resident binary handle."""
+    if device != "cuda":
+        raise ValueError("device must be 'cuda'")
+    if packed.device == "cuda":
+        return packed
+    from maxsim_b200 import _maxsim_cuda
+
+    handle = _maxsim_cuda.CudaPackedDocs(np.ascontiguousarray(packed.prefix_data, dtype=np.uint8),
+                                         np.ascontiguousarray(packed.doc_offsets, dtype=np.int64), packed.dim)
+    handle.set_token_scale_vector(np.ascontiguousarray(packed.prefix_token_scale, dtype=np.float32))
+    handle.set_residual_int4(np.ascontiguousarray(packed.residual_data, dtype=np.uint8),
+                             np.ascontiguousarray(packed.residual_token_scale, dtype=np.float32))
+    return BinaryResidualPackedDocs(prefix_data=handle, prefix_token_scale=packed.prefix_token_scale,
+                                    residual_data=None, residual_values=None,
+                                    residual_token_scale=packed.residual_token_scale,
+                                    doc_offsets=packed.doc_offsets.copy(), dim=packed.dim, num_docs=packed.num_docs,
+                                    device="cuda")
+
+
+def _binary_resident(packed: BinaryResidualPackedDocs, device) -> BinaryResidualPackedDocs:
+    if not isinstance(packed, BinaryResidualPackedDocs):
+        raise TypeError("packed must be a BinaryResidualPackedDocs instance")
+    _effective_device(device, packed)
+    return packed if packed.device == "cuda" else binary_residual_to_device(packed)
+
+
+def binary_prefix_score(query_tokens, packed: BinaryResidualPackedDocs, *, device: str = "auto",
+                        reducer: str = "maxsim", query_weights=None, temperature: float = 1.0,
+                        candidate_indices=None) -> np.ndarray:
+    """Scores of the sign prefix alone (sign dot times the per-token reconstruction scale)."""
+    resident = _binary_resident(packed, device)
+    q, squeeze = _normalize_query(query_tokens, packed.dim)
+    rv, w, t = _normalize_reducer_options(reducer, query_weights, temperature, batch=q.shape[0],
+                                          query_tokens=q.shape[1])
+    cands = _normalize_candidate_indices(candidate_indices, packed.num_docs)
+    h = resident.prefix_data
+    out = (h.score_batch(q, rv, w, t, 1.0, False, True) if cands is None
+           else h.score_candidates_batch(q, cands, rv, w, t, 1.0, False, True))
+    return out[0] if squeeze else out
+
+
+def binary_residual_score(query_tokens, packed: BinaryResidualPackedDocs, *, device: str = "auto",
+                          reducer: str = "maxsim", query_weights=None, temperature: float = 1.0,
+                          candidate_indices=None) -> np.ndarray:
+    """Fused two-stream scores: (sign . q) * prefix scale + (residual . q) * residual scale, then the reducer."""
+    resident = _binary_resident(packed, device)
+    q, squeeze = _normalize_query(query_tokens, packed.dim)
+    rv, w, t = _normalize_reducer_options(reducer, query_weights, temperature, batch=q.shape[0],
+                                          query_tokens=q.shape[1])
+    cands = _normalize_candidate_indices(candidate_indices, packed.num_docs)
+    h = resident.prefix_data
+    out = (h.score_residual_batch(q, rv, w, t) if cands is None
+           else h.score_residual_candidates_batch(q, cands, rv, w, t))
+    return out[0] if squeeze else out
+
+
+def binary_cascade_topk(query_tokens, packed: BinaryResidualPackedDocs, k: int, *, candidates: int,
+                        device: str = "auto", reducer: str = "maxsim", query_weights=None,
+                        temperature: float = 1.0):
+    """Sign-prefix scan -> per-query top-M -> fused residual rescoring -> top-k, in one device call."""
+    resident = _binary_resident(packed, device)
+    q, squeeze = _normalize_query(query_tokens, packed.dim)
+    if not 1 <= int(k) <= int(candidates) <= packed.num_docs:
+        raise ValueError("cascade sizes must satisfy 1 <= k <= candidates <= num_docs")
+    rv, w, t = _normalize_reducer_options(reducer, query_weights, temperature, batch=q.shape[0],
+                                          query_tokens=q.shape[1])
+    s, i = resident.prefix_data.cascade_topk_batch(q, int(k), int(candidates), rv, w, t)
+    return (s[0], i[0]) if squeeze else (s, i)

@@ -205,8 +205,21 @@ Resolved resolve(msb_docs* h, const msb_score_opts* o, int batch, int qtok, cons
       d.token_scale2 = h->residual_token_scale.as<float>();
       d.scale2 = h->residual_scale;
     }
+  } else if (r.residual) {
+    // sign-bit prefix scaled by its per-token reconstruction scale + per-token int4 residual
+    if (!h->has_residual)
+      throw InvalidArgument("residual int4 data was requested but is not loaded on this CUDA handle");
+    if (!h->has_token_scale)
+      throw InvalidArgument("residual scoring on a binary handle needs the prefix token scale vector");
+    if (o->query_mode != kQueryF32) throw InvalidArgument("residual scoring takes fp32 queries");
+    if (o->use_doc_scale || d_override)
+      throw InvalidArgument("document scales do not apply to residual scoring");
+    d.token_scale = h->token_scale.as<float>();
+    d.codes2 = h->residual_codes.as<uint8_t>();
+    d.token_scale2 = h->residual_token_scale.as<float>();
+    d.scale2 = h->residual_scale;
+    d.scale = 1.0F;
   } else {
-    if (r.residual) throw InvalidArgument("residual scoring requires an int4 handle");
     if (o->use_token_scale) {
       if (!h->has_token_scale)
         throw InvalidArgument("token scale vector was requested but is not loaded on this CUDA handle");
@@ -530,15 +543,16 @@ int msb_docs_set_residual(msb_docs* h, const uint8_t* codes, int64_t num_tokens,
                           const float* token_scales) {
   return guarded([&] {
     if (!h) throw InvalidArgument("handle is NULL");
-    if (h->format != kFormatInt4) throw InvalidArgument("residual int4 data requires an int4 handle");
     if (num_tokens != h->num_tokens)
       throw InvalidArgument("residual packed data must have shape [num_doc_tokens, dim / 2]");
+    if (h->format == kFormatBinary && scale != 1.0F)
+      throw InvalidArgument("a binary handle's residual stream uses per-token scales only (scale must be 1)");
     if (!(scale > 0.0F) || !std::isfinite(scale)) throw InvalidArgument("residual scale must be finite and > 0");
     for (int64_t i = 0; i < num_tokens; ++i)
       if (!(token_scales[i] > 0.0F) || !std::isfinite(token_scales[i]))
         throw InvalidArgument("residual token scales must be finite and > 0");
     DeviceGuard g(h->device);
-    const size_t cbytes = h->bytes_per_token() * static_cast<size_t>(num_tokens);
+    const size_t cbytes = static_cast<size_t>(h->dim / 2) * static_cast<size_t>(num_tokens);  // int4 residual
     const size_t sbytes = sizeof(float) * static_cast<size_t>(num_tokens);
     h->residual_codes.ensure(cbytes > 0 ? cbytes : 4, "cudaMalloc resident int4 residual data");
     h->residual_token_scale.ensure(sbytes > 0 ? sbytes : 4, "cudaMalloc resident int4 residual token scales");
@@ -639,6 +653,13 @@ int msb_docs_cascade_topk(msb_docs* h, const float* query, int32_t batch, int32_
     msb_score_opts prefix_opts = *opts;
     prefix_opts.use_residual = 0;
     prefix_opts.query_mode = kQueryF32;
+    if (h->format == kFormatBinary) {
+      // binary prefix: sign scan scaled by the per-token reconstruction scale
+      prefix_opts.use_token_scale = 1;
+      prefix_opts.use_doc_scale = 0;
+      prefix_opts.scale = 1.0F;
+      prefix_opts.doc_scale_override = nullptr;
+    }
     Resolved rp = resolve(h, &prefix_opts, batch, qtok, d_w, d_ov);
     msb_score_opts fine_opts = prefix_opts;
     fine_opts.use_residual = 1;

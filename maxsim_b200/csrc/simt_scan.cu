@@ -213,7 +213,9 @@ __device__ __forceinline__ int dot_bin_i8(const int32_t* __restrict__ qw, int32_
 }
 
 // Format selector for the kernel template.
-enum ScanKind : int { kKindInt4 = 0, kKindBinary = 1, kKindResidual = 2 };
+// kKindResidual: int4 prefix + int4 residual; kKindResidualBinary: sign-bit prefix (scaled by its per-token
+// reconstruction scale) + int4 residual.
+enum ScanKind : int { kKindInt4 = 0, kKindBinary = 1, kKindResidual = 2, kKindResidualBinary = 3 };
 
 template <int Kind, int Mode, int R>
 __global__ void __launch_bounds__(128) simt_scan_kernel(DocsView docs, QueryView qv, ReduceView red,
@@ -237,7 +239,7 @@ __global__ void __launch_bounds__(128) simt_scan_kernel(DocsView docs, QueryView
   if (Kind == kKindInt4) doc_scale = docs.scale;
   if (Kind == kKindBinary) doc_scale = docs.doc_scale ? docs.doc_scale[d] : docs.scale;
 
-  const int bytes_per_token = (Kind == kKindBinary) ? dim / 8 : dim / 2;
+  const int bytes_per_token = (Kind == kKindBinary || Kind == kKindResidualBinary) ? dim / 8 : dim / 2;
   for (int r = warp; r < Q; r += 4) {
     const int64_t row = static_cast<int64_t>(b) * Q + r;
     typename P::S st = P::init();
@@ -250,6 +252,11 @@ __global__ void __launch_bounds__(128) simt_scan_kernel(DocsView docs, QueryView
         float d2 = dot_int4_f32(qf, docs.codes2 + t * bytes_per_token, dim);
         float s1 = docs.token_scale ? docs.token_scale[t] : 1.0F;
         sim = d1 * docs.scale * s1 + d2 * docs.scale2 * docs.token_scale2[t];
+      } else if (Kind == kKindResidualBinary) {
+        const float* qf = qv.f32 + row * dim;
+        const float d1 = dot_bin_f32(qf, code, dim);                                     // sum of +-q
+        const float d2 = dot_int4_f32(qf, docs.codes2 + t * static_cast<int64_t>(dim / 2), dim);
+        sim = d1 * docs.token_scale[t] + d2 * docs.scale2 * docs.token_scale2[t];
       } else {
         if (Mode == kQueryI8) {
           const int32_t* qw = qv.i8_words + row * (dim / 4);
@@ -280,7 +287,7 @@ __global__ void __launch_bounds__(128) simt_scan_kernel(DocsView docs, QueryView
   if (threadIdx.x == 0) {
     float acc = 0.0F;
     for (int r = 0; r < Q; ++r) acc += row_value[r];
-    if (!P::kScaleFirst && Kind != kKindResidual) acc *= doc_scale;
+    if (!P::kScaleFirst && Kind != kKindResidual && Kind != kKindResidualBinary) acc *= doc_scale;
     out[static_cast<int64_t>(b) * T + j] = acc;
   }
 }
@@ -311,7 +318,8 @@ void launch_simt_scan(const DocsView& docs, const QueryView& qv, const ReduceVie
                       bool residual, float* out, cudaStream_t stream) {
   if (residual) {
     if (qv.mode != kQueryF32) throw InvalidArgument("residual scoring takes fp32 queries");
-    launch_kind_mode<kKindResidual, kQueryF32>(docs, qv, red, tg, out, stream);
+    if (docs.format == kFormatBinary) launch_kind_mode<kKindResidualBinary, kQueryF32>(docs, qv, red, tg, out, stream);
+    else launch_kind_mode<kKindResidual, kQueryF32>(docs, qv, red, tg, out, stream);
     return;
   }
   if (qv.mode == kQueryI8 && red.reducer != kMaxSim)

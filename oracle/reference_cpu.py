@@ -429,6 +429,59 @@ def cascade_topk(query, res: dict, offsets, k: int, candidates: int, *, reducer=
 
 
 # ---------------------------------------------------------------------------
+# Binary-prefix residual cascade (parity unpinned: the reference has no such
+# format; this follows the benchmark description of the binary-prefix cascade,
+# with the per-token mean |x| of ``src/maxsim/_api.py:84-85`` as the sign
+# reconstruction scale and the per-token int4 of ``experimental.py:240-246``
+# for the residual, fused like ``cascade.py:469-480``)
+# ---------------------------------------------------------------------------
+
+def pack_binary_residual(docs: np.ndarray) -> dict:
+    """Sign bits + per-token mean |x|; residual x - mean|x| * sign(x) as per-token int4."""
+    x = np.asarray(docs, dtype=np.float32)
+    ps = mean_abs_token_scale(x)
+    signs = np.where(x >= 0, np.float32(1.0), np.float32(-1.0))
+    residual = (x - ps[:, None] * signs).astype(np.float32)
+    rdata, rvals, _, rts = pack_int4(residual, "token")
+    return dict(bits=pack_signs(x), prefix_token_scale=ps, residual_data=rdata, residual_values=rvals,
+                residual_token_scale=rts)
+
+
+def score_binary_residual(query, res: dict, offsets, **kw):
+    """Fused similarity sign(x).q * ps + r.q * rts, then the reducer (float64 reference)."""
+    dim = res["bits"].shape[1] * 8
+    p = unpack_signs(res["bits"], dim).astype(np.float64) * res["prefix_token_scale"].astype(np.float64)[:, None]
+    r = res["residual_values"].astype(np.float64) * res["residual_token_scale"].astype(np.float64)[:, None]
+    return score_dense(query, p + r, offsets, **kw)
+
+
+def binary_cascade_topk(query, res: dict, offsets, k: int, candidates: int, *, reducer="maxsim", weights=None,
+                        temperature=1.0):
+    """Sign-prefix scan (scaled by ps) -> stable top-M -> fused rescoring -> top-k (ties by candidate id)."""
+    batches, squeeze = _as_batches(query)
+    n_docs = int(len(offsets) - 1)
+    dim = res["bits"].shape[1] * 8
+    out_s, out_i = [], []
+    for b, qm in enumerate(batches):
+        wb = None if weights is None else _weights_for(weights, b, qm.shape[0])
+        kw = dict(reducer=reducer, weights=wb, temperature=temperature)
+        if candidates == n_docs:
+            fine = score_binary_residual(qm, res, offsets, **kw)
+            idx = topk_indices(fine, k)
+            out_s.append(fine[idx])
+            out_i.append(idx)
+            continue
+        coarse = score_binary_fp32(qm, res["bits"], dim, offsets, token_scale=res["prefix_token_scale"], **kw)
+        cand = topk_indices(coarse, candidates)
+        fine = score_binary_residual(qm, res, offsets, candidates=cand, **kw)
+        order = topk_indices(fine, k, tie_ids=cand)
+        out_s.append(fine[order])
+        out_i.append(cand[order])
+    s, i = np.stack(out_s), np.stack(out_i)
+    return (s[0], i[0]) if squeeze else (s, i)
+
+
+# ---------------------------------------------------------------------------
 # Synthetic corpora shaped like the benchmark configurations
 # ---------------------------------------------------------------------------
 

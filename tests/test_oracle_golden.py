@@ -208,3 +208,22 @@ def test_index_from_embeddings_writes_the_reference_arrays(tmp_path, mode):
                 assert json.loads(str(got[k])) == json.loads(str(want[k])), mode
             else:
                 np.testing.assert_array_equal(got[k], want[k], err_msg=f"{mode}:{k}")
+
+
+def test_binary_residual_host_pack_matches_oracle():
+    """Host packing of the binary-prefix residual format equals the oracle restatement
+    (parity unpinned: the reference has no such format)."""
+    import maxsim_b200 as m
+
+    docs, off = ref.clustered_corpus(40, 0, 50, seed=5)
+    docs[3] = 0.0  # an all-zero token: mean |x| = 0, residual int4 scale falls back to 1
+    want = ref.pack_binary_residual(docs)
+    got = m.pack_binary_residual_int4(docs, off)
+    np.testing.assert_array_equal(got.prefix_data, want["bits"])
+    np.testing.assert_array_equal(got.prefix_token_scale, want["prefix_token_scale"])
+    np.testing.assert_array_equal(got.residual_data, want["residual_data"])
+    np.testing.assert_array_equal(got.residual_token_scale, want["residual_token_scale"])
+    # the fused reconstruction is closer to x than the sign prefix alone
+    p = ref.unpack_signs(want["bits"], 128) * want["prefix_token_scale"][:, None]
+    r = want["residual_values"] * want["residual_token_scale"][:, None]
+    assert np.abs(docs - (p + r)).mean() < 0.25 * np.abs(docs - p).mean()
