@@ -18,9 +18,11 @@
 //     corpus, 2 x SM-count of them, ordered range-major, so every CTA gets the
 //     same number of equal-sized units and the CTAs working on one range run
 //     together and share its codes through L2.
-//   * Persistent CTAs (one per SM), 14 warps: warps 0-7 epilogue (query tile
+//   * Persistent CTAs (one per SM), 12 warps: warps 0-7 epilogue (query tile
 //     warp / 4, TMEM lane quarter warp % 4), warp 8 TMEM allocation and MMA
-//     issue (one thread), warps 9-12 expanders, warp 13 loader.
+//     issue (one thread), warps 9-10 expanders, warp 11 loader.  Fewer
+//     producer warps leave more issue slots to the epilogue and allow up to
+//     168 registers per thread.
 //   * The loader streams each tile's 64-byte int4 rows (and token scales)
 //     into a 6-deep shared-memory ring with 1D bulk copies (TMA engine);
 //     expander warps sign-extend each two's-complement nibble to an int8
@@ -57,11 +59,11 @@ constexpr int kMeta = 8;          // tile metadata ring (scales, document ends),
 constexpr int kRaw = 6;           // raw-code ring filled by bulk copies
 constexpr int kAccBufs = 2;       // token-tile accumulator buffers (each kG x 128 TMEM columns)
 constexpr int kEpiWarps = 8;      // warp w: query tile w / 4 of the pair, TMEM lane quarter w % 4
-constexpr int kXWarps = 4;        // expanders (one token per thread per tile)
+constexpr int kXWarps = 2;        // expanders (two tokens per thread per tile)
 constexpr int kMmaWarp = kEpiWarps;            // warp 8
-constexpr int kXWarp0 = kMmaWarp + 1;          // warps 9..12
-constexpr int kLoadWarp = kXWarp0 + kXWarps;   // warp 13
-constexpr int kThreads = (kLoadWarp + 1) * 32; // 448 = 14 warps (128 registers each)
+constexpr int kXWarp0 = kMmaWarp + 1;          // warps 9..10
+constexpr int kLoadWarp = kXWarp0 + kXWarps;   // warp 11
+constexpr int kThreads = (kLoadWarp + 1) * 32; // 384 = 12 warps
 constexpr int kSegGroup = 8;      // finished documents per epilogue flush
 constexpr int kMaxRangeDocs = 512;
 constexpr uint32_t kTmemCols = kAccBufs * kG * kTileN;        // 512
@@ -361,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
     }
   } else if (warp >= kXWarp0) {
     // =================== expanders: int4 -> int8 bytes, UMMA layout ===================
-    const int xtid = threadIdx.x - kXWarp0 * 32;  // 0..127
+    const int xtid = threadIdx.x - kXWarp0 * 32;  // 0..63
     const int xwarp = warp - kXWarp0;
     Ring raw, stg, mst;
     int iter = 0;
@@ -369,8 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       const Unit unit = p.units[u];
       const int abuf = iter & 1;
       if (iter >= 2 && !mbar_wait(&a_empty[abuf], ((iter >> 1) - 1) & 1, abort_flag, p.error, 11)) goto done;
-      {
-        const int row = xtid;  // one query row of each tile of the pair per thread
+#pragma unroll 1
+      for (int row = xtid; row < 128; row += kXWarps * 32) {  // query rows of each tile of the pair
 #pragma unroll
         for (int g = 0; g < kG; ++g) {
           unsigned char* A = smem + kOffA + (abuf * kG + g) * kATileBytes;
@@ -383,6 +385,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
             *reinterpret_cast<int4*>(A + tile_off(row, c)) = v;
           }
         }
+      }
+      {
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[abuf]);
@@ -400,8 +404,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
         unsigned char* Bt = smem + kOffB + stg.idx * kBTileBytes;
         StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kOffMeta + mst.idx * kMetaBytes);
         const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
-        if (xtid < valid) {
-          const int r = xtid;  // one token per thread
+#pragma unroll 1
+        for (int r = xtid; r < valid; r += kXWarps * 32) {  // tokens of the tile
           // Chunk order c = M(a) ^ step with a = (r / 2) % 4 and M multiplication by a generator of GF(4)
           // ({0, 2, 3, 1}): both c and c ^ a run over all four values within each 8-token quarter warp,
           // so the raw loads (bank slot 4(r % 2) + c) and the swizzled stores (slot 2(c ^ a) + r % 2) are
