@@ -49,10 +49,10 @@ NOISE = 0.3
 SEED = 20260713
 CHUNK_PAGES = 2_000
 # DRAM bytes (read + write) of one tc_scan_kernel launch per corpus page, from one ncu capture of a
-# 2,000-page case of the same workload (profiles/tc_scan_kernel_2000pages_full.txt: 140.43 MB read +
-# 4.13 MB written).  The corpus is streamed once per launch and the score matrix grows with the pages,
+# 2,000-page case of the same workload (profiles/tc_scan_kernel_2000pages_full.txt: 140.49 MB read +
+# 4.19 MB written).  The corpus is streamed once per launch and the score matrix grows with the pages,
 # so traffic scales with the pages a rank holds.
-TC_DRAM_BYTES_PER_PAGE = (140.431104e6 + 4.134400e6) / 2000
+TC_DRAM_BYTES_PER_PAGE = (140.493568e6 + 4.193280e6) / 2000
 WORKLOAD = ("C4: 100,000 pages x 1,030 tokens (dim 128) per-token int4 (6.59 GB codes + 0.41 GB scales); "
             "1,024 queries x 24 tokens int8, batch 64, full-scan top-10")
 
