@@ -94,7 +94,11 @@ int msb_version(void);
 /* Kernels launched by this library since load (bench.py reports the delta). */
 int64_t msb_launch_count(void);
 /* Runtime knobs.  "engine": 0 auto, 1 SIMT only, 2 tensor-core only (errors
- * where unsupported).  Unknown names return MSB_ERR_INVALID_ARGUMENT. */
+ * where unsupported).  "tc_int8_cache": 1 (default) lets the tensor-core engine
+ * keep a resident int8 copy of an int4 corpus (128 B per token, built on first
+ * use and counted in resident_bytes) and stream operand tiles from it with
+ * TMA; 0 expands int4 rows per tile instead.  Unknown names return
+ * MSB_ERR_INVALID_ARGUMENT. */
 int msb_set_option(const char* name, int64_t value);
 int msb_get_option(const char* name, int64_t* value);
 

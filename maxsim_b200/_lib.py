@@ -152,3 +152,14 @@ def get_engine() -> int:
     out = ctypes.c_int64()
     check(lib.msb_get_option(b"engine", ctypes.byref(out)))
     return int(out.value)
+
+
+def set_option(name: str, value: int) -> None:
+    """Set a runtime knob of the library ("engine", "tc_int8_cache")."""
+    check(lib.msb_set_option(name.encode(), int(value)))
+
+
+def get_option(name: str) -> int:
+    out = ctypes.c_int64()
+    check(lib.msb_get_option(name.encode(), ctypes.byref(out)))
+    return int(out.value)

@@ -25,10 +25,13 @@ bool tc_scan_supported(const DocsView&, const QueryView&, const ReduceView&, con
 void launch_tc_scan(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, float*, void* ws,
                     size_t ws_bytes, cudaStream_t);
 size_t tc_scan_workspace_bytes(const DocsView&, const QueryView&, const TargetsView&);
+bool tc_int8_cache_supported(const DocsView&);
+void launch_expand_codes8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t);
 
 static std::atomic<int64_t> g_launches{0};
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 static std::atomic<int> g_engine{0};  // 0 auto, 1 SIMT, 2 tensor core
+static std::atomic<int> g_tc_int8_cache{1};  // keep an int8-expanded copy of int4 corpora for the tc engine
 static std::atomic<uint64_t> g_corpus_serial{0};
 }  // namespace msb
 
@@ -127,10 +130,14 @@ struct msb_docs {
   std::vector<int64_t> host_offsets;
   bool tc_used = false;  // the tensor-core engine ran since the last error check
   uint64_t serial = 0;   // unique corpus id for caches keyed on a corpus
+  // int4 codes expanded once to int8 in the tensor-core scan's K order ([N, 128] bytes), so the scan
+  // streams ready operand tiles with tiled TMA instead of expanding every tile for every query batch.
+  DeviceBuf codes8;
+  bool codes8_failed = false;  // allocation failed once: keep using the expanding scan
 
   size_t bytes_per_token() const { return format == kFormatInt4 ? dim / 2 : dim / 8; }
   int64_t resident_bytes() const {
-    return static_cast<int64_t>(codes.cap + offsets.cap + token_scale.cap + doc_scale.cap + residual_codes.cap +
+    return static_cast<int64_t>(codes.cap + codes8.cap + offsets.cap + token_scale.cap + doc_scale.cap + residual_codes.cap +
                                 residual_token_scale.cap);
   }
   int64_t workspace_bytes() const {
@@ -146,7 +153,7 @@ struct msb_docs {
     DeviceBuf* all[] = {&codes,   &offsets,  &token_scale, &doc_scale, &residual_codes, &residual_token_scale,
                         &w_query, &w_qcodes, &w_qwords,    &w_qscale,  &w_qsum,         &w_scores,
                         &w_cands, &w_weights, &w_top_s,    &w_top_i,   &w_override,     &w_fine,
-                        &w_tc};
+                        &w_tc,    &codes8};
     for (DeviceBuf* b : all) b->release();
     if (stream) cudaStreamDestroy(stream);
     if (prev >= 0) cudaSetDevice(prev);
@@ -277,7 +284,23 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
   if (tc_ok && engine != 1) {
     const size_t ws = tc_scan_workspace_bytes(r.docs, qv, tg);
     h->w_tc.ensure(ws > 0 ? ws : 16, "cudaMalloc tensor-core scan workspace");
-    launch_tc_scan(r.docs, qv, r.red, tg, d_out, h->w_tc.ptr, h->w_tc.cap, stream);
+    DocsView dv = r.docs;
+    if (g_tc_int8_cache.load() && !h->codes8_failed && tc_int8_cache_supported(dv)) {
+      if (!h->codes8.ptr) {
+        const size_t bytes = static_cast<size_t>(h->num_tokens) * 128;
+        void* p = nullptr;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) {
+          (void)cudaGetLastError();  // not enough memory for the copy: keep expanding per tile
+          h->codes8_failed = true;
+        } else {
+          h->codes8.ptr = p;
+          h->codes8.cap = bytes;
+          launch_expand_codes8(h->codes.as<uint8_t>(), h->num_tokens, h->codes8.as<uint8_t>(), stream);
+        }
+      }
+      if (h->codes8.ptr) dv.codes8 = h->codes8.as<uint8_t>();
+    }
+    launch_tc_scan(dv, qv, r.red, tg, d_out, h->w_tc.ptr, h->w_tc.cap, stream);
     h->tc_used = true;
     return;
   }
@@ -378,6 +401,11 @@ int msb_set_option(const char* name, int64_t value) {
       g_engine.store(static_cast<int>(value));
       return;
     }
+    if (std::strcmp(name, "tc_int8_cache") == 0) {
+      if (value != 0 && value != 1) throw InvalidArgument("tc_int8_cache must be 0 or 1");
+      g_tc_int8_cache.store(static_cast<int>(value));
+      return;
+    }
     throw InvalidArgument(std::string("unknown option: ") + name);
   });
 }
@@ -387,6 +415,10 @@ int msb_get_option(const char* name, int64_t* value) {
     if (!name || !value) throw InvalidArgument("NULL argument");
     if (std::strcmp(name, "engine") == 0) {
       *value = g_engine.load();
+      return;
+    }
+    if (std::strcmp(name, "tc_int8_cache") == 0) {
+      *value = g_tc_int8_cache.load();
       return;
     }
     throw InvalidArgument(std::string("unknown option: ") + name);

@@ -50,6 +50,7 @@ struct DocsView {
   const float* doc_scale;      // [D] or nullptr (binary scale vector)
   const int64_t* host_offsets;  // host copy of offsets (work partitioning)
   uint64_t corpus_id;          // unique per resident corpus (keys host-side caches)
+  const uint8_t* codes8;       // int4 codes expanded to int8 in scan K order [N, 128], or nullptr
   int64_t num_docs;
   int64_t num_tokens;
   int dim;

@@ -23,14 +23,16 @@
 //     issue (one thread), warps 9-10 expanders, warp 11 loader.  Fewer
 //     producer warps leave more issue slots to the epilogue and allow up to
 //     168 registers per thread.
-//   * The loader streams each tile's 64-byte int4 rows (and token scales)
-//     into a 6-deep shared-memory ring with 1D bulk copies (TMA engine);
-//     expander warps sign-extend each two's-complement nibble to an int8
-//     byte (two masks and one multiply-add per 4 values) and store the tile
-//     in the 128-byte-swizzled K-major UMMA layout, in a chunk order that
-//     keeps both their shared loads and stores free of bank conflicts.  Tile
-//     metadata (token scales, document ends) goes through its own ring,
-//     released by the epilogue.
+//   * Operand tiles.  By default the int4 corpus is expanded once into a
+//     resident int8 copy in the scan's K order (128 B per token, built by
+//     expand_codes8_kernel on first use), and the loader fills each B stage
+//     with one tiled TMA load (cp.async.bulk.tensor.2d, 128 rows x 128 bytes,
+//     128-byte swizzle: the UMMA layout) while expander warps only stage the
+//     tile metadata (token scales, document ends).  Without the copy (option
+//     "tc_int8_cache" 0, or no memory for it) the loader copies raw int4 rows
+//     into a 6-deep ring and the expander warps sign-extend each nibble to an
+//     int8 byte in the swizzled layout, in a chunk order that keeps their
+//     shared loads and stores free of bank conflicts.
 //   * TMEM holds two token-tile buffers x two query tiles x 128 columns.  One
 //     commit per token tile both frees its shared-memory stage and hands the
 //     accumulators to the epilogue, which returns them as soon as the tile's
@@ -39,10 +41,13 @@
 //     2^24: conversion to float is exact); one FMUL applies the token scale
 //     and three-input max reduces.  The epilogue reads TMEM with 16x256b
 //     loads, so each thread holds two rows x 16 columns per 64-column chunk
-//     and needs 16 token scales instead of 64; a row's maximum is completed
-//     with two butterfly shuffles when a document ends.
+//     and reads its 16 token scales with four 16-byte loads from a permuted
+//     layout; a row's maximum is completed with two butterfly shuffles when a
+//     document ends, and tiles without document ends skip the walk.
 // Every mbarrier wait is bounded (%globaltimer); on timeout the kernel raises
 // an error flag, drains, frees its TMEM and returns.
+#include <cuda.h>  // CUtensorMap (the encoder is fetched through cudaGetDriverEntryPoint)
+
 #include <algorithm>
 #include <mutex>
 #include <vector>
@@ -100,8 +105,15 @@ constexpr int kRawCodeBytes = kTileN * 64;             // 8 KB
 constexpr int kRawScaleFloats = kTileN + 4;            // aligned superset of the tile's scales
 constexpr int kRawBytes = ((kRawCodeBytes + kRawScaleFloats * 4 + 127) / 128) * 128;
 constexpr int kUoffEntries = kMaxRangeDocs + 4;
+// Token scales in the order the epilogue threads consume them: column c = 64h + 8j + 2t + b is held by
+// threads with t % 4 = t at index h * 80 + t * 20 + 2j + b, so each thread reads its 16 scales of a
+// 64-column chunk with four conflict-free 16-byte loads (the 20-float stride spreads the four
+// threads' blocks over distinct banks).
+__host__ __device__ constexpr int scale_slot(int col) {
+  return (col >> 6) * 80 + ((col & 7) >> 1) * 20 + ((col & 63) >> 3) * 2 + (col & 1);
+}
 struct StageMeta {
-  float scale[kTileN];
+  float scale[160];
   int16_t seg_end[kTileN];   // exclusive end column of each document ending in the tile
   int32_t seg_doc[kTileN];
   int32_t nseg;
@@ -230,6 +242,14 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
 }
+// Tiled 2D TMA load of box {128 bytes, 128 rows} at (x bytes, y rows), completing tx bytes on `bar`.
+// x is 0 (16-byte aligned); no multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -269,8 +289,11 @@ struct Ring {
   }
 };
 
-template <bool kTokenScale>
-__global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
+// kPre: the int4 codes were expanded once into an int8 copy (same K order); each B stage is a tiled TMA
+// load of 128 rows from it, landing in the 128-byte-swizzled layout, and the expanders only stage the
+// tile metadata.  Otherwise the loader copies raw int4 rows and the expanders build the B stage.
+template <bool kTokenScale, bool kPre>
+__global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                          ~static_cast<uintptr_t>(1023));
@@ -297,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], kXWarps);
+      mbar_init(&full[s], kPre ? 1 : kXWarps);  // kPre: the loader's expect_tx + the TMA's bytes
       mbar_init(&tile_done[s], 1);
     }
     for (int s = 0; s < kMeta; ++s) {
@@ -332,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
   if (warp == kLoadWarp) {
     // =================== loader: bulk copies run ahead of the expanders ===================
     if (lane == 0) {
-      Ring raw;
+      Ring raw, stg;
       int iter = 0;
       for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
         const Unit unit = p.units[u];
@@ -347,15 +370,22 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
           bulk_g2s(smem + kOffUoff + ub * kUoffEntries * 8, p.offsets + first, bytes, &u_full[ub]);
         }
         for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
+          if (kPre) {
+            // B stage: wait until the MMAs that read it have completed, then one tiled TMA load
+            if (!mbar_wait(&tile_done[stg.idx], stg.phase ^ 1, abort_flag, p.error, 43)) goto done;
+            mbar_expect_tx(&full[stg.idx], static_cast<uint32_t>(kBTileBytes));
+            tma_load_2d(smem + kOffB + stg.idx * kBTileBytes, &tmap, 0, static_cast<int>(t0), &full[stg.idx]);
+            stg.next<kStages>();
+          }
           if (!mbar_wait(&raw_empty[raw.idx], raw.phase ^ 1, abort_flag, p.error, 42)) goto done;
           const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
           unsigned char* rb = smem + kOffRaw + raw.idx * kRawBytes;
-          const uint32_t code_bytes = static_cast<uint32_t>(valid) * 64u;
+          const uint32_t code_bytes = kPre ? 0u : static_cast<uint32_t>(valid) * 64u;
           uint32_t scale_bytes = 0;
           const int64_t s_first = t0 & ~3LL;
           if (kTokenScale) scale_bytes = static_cast<uint32_t>(((t0 + valid - s_first + 3) & ~3LL) * 4);
           mbar_expect_tx(&raw_full[raw.idx], code_bytes + scale_bytes);
-          bulk_g2s(rb, p.codes + t0 * 64, code_bytes, &raw_full[raw.idx]);
+          if (!kPre) bulk_g2s(rb, p.codes + t0 * 64, code_bytes, &raw_full[raw.idx]);
           if (kTokenScale) bulk_g2s(rb + kRawCodeBytes, p.token_scale + s_first, scale_bytes, &raw_full[raw.idx]);
           raw.next<kRaw>();
         }
@@ -398,14 +428,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
       int64_t next_doc = unit.d_lo;  // first document whose end has not been passed
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
         if (!mbar_wait(&raw_full[raw.idx], raw.phase, abort_flag, p.error, 14)) goto done;
-        if (!mbar_wait(&tile_done[stg.idx], stg.phase ^ 1, abort_flag, p.error, 12)) goto done;
+        if (!kPre && !mbar_wait(&tile_done[stg.idx], stg.phase ^ 1, abort_flag, p.error, 12)) goto done;
         if (!mbar_wait(&m_empty[mst.idx], mst.phase ^ 1, abort_flag, p.error, 15)) goto done;
         const unsigned char* rb = smem + kOffRaw + raw.idx * kRawBytes;
         unsigned char* Bt = smem + kOffB + stg.idx * kBTileBytes;
         StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kOffMeta + mst.idx * kMetaBytes);
         const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
+        if (kPre && kTokenScale) {
+          const float* rs = reinterpret_cast<const float*>(rb + kRawCodeBytes);
+          for (int r = xtid; r < valid; r += kXWarps * 32) meta->scale[scale_slot(r)] = rs[(t0 & 3) + r];
+        }
 #pragma unroll 1
-        for (int r = xtid; r < valid; r += kXWarps * 32) {  // tokens of the tile
+        for (int r = xtid; r < (kPre ? 0 : valid); r += kXWarps * 32) {  // tokens of the tile
           // Chunk order c = M(a) ^ step with a = (r / 2) % 4 and M multiplication by a generator of GF(4)
           // ({0, 2, 3, 1}): both c and c ^ a run over all four values within each 8-token quarter warp,
           // so the raw loads (bank slot 4(r % 2) + c) and the swizzled stores (slot 2(c ^ a) + r % 2) are
@@ -430,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
           }
           if (kTokenScale) {
             const float* rs = reinterpret_cast<const float*>(rb + kRawCodeBytes);
-            meta->scale[r] = rs[(t0 & 3) + r];
+            meta->scale[scale_slot(r)] = rs[(t0 & 3) + r];
           }
         }
         // Documents ending inside (t0, t0 + valid]: expander warp 0 walks the unit's offsets in smem.
@@ -464,7 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&full[stg.idx]);
+          if (!kPre) mbar_arrive(&full[stg.idx]);
           mbar_arrive(&m_full[mst.idx]);
           mbar_arrive(&raw_empty[raw.idx]);
         }
@@ -558,7 +592,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
             float2 sc[8];
             if (kTokenScale) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) sc[j] = *reinterpret_cast<const float2*>(meta->scale + c0 + 8 * j + 2 * tc);
+              for (int k4 = 0; k4 < 4; ++k4) {
+                const float4 x = *reinterpret_cast<const float4*>(meta->scale + (c0 >> 6) * 80 + tc * 20 + 4 * k4);
+                sc[2 * k4] = make_float2(x.x, x.y);
+                sc[2 * k4 + 1] = make_float2(x.z, x.w);
+              }
             }
             tmem_ld16x256b_x8(tbase + c0, ra);
             tmem_ld16x256b_x8(tbase + (16u << 16) + c0, rb);
@@ -587,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p) {
           }
           int a = c0;
           while (true) {
-            const int e = sgi < nseg ? meta->seg_end[sgi] : 0x7FFF;
+            const int e = nseg == 0 ? 0x7FFF : (sgi < nseg ? meta->seg_end[sgi] : 0x7FFF);
             const int bnd = min(e, c1);
             if (bnd > a && tile_live) {
               if (a == c0 && bnd == c0 + 64) {
@@ -753,6 +791,74 @@ TcPlan plan_for(const DocsView& d, const QueryView& q, int sms) {
 
 }  // namespace
 
+bool tc_int8_cache_supported(const DocsView& d) {
+  // TMA row coordinates are 32-bit
+  return d.format == kFormatInt4 && d.dim == 128 && d.num_tokens > 0 && d.num_tokens < 0x7FFFFF00LL;
+}
+
+namespace tc {
+// int4 rows [N, 64] -> int8 rows [N, 128] in the scan's K order (per 16-byte input chunk: low
+// nibbles of word 0, high nibbles of word 0, ..., of word 3), identical to the expander warps.
+__global__ void expand_codes8_kernel(const uint4* __restrict__ in, int64_t n_chunks, uint4* __restrict__ out) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_chunks;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint4 v = __ldg(in + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = (w[j] >> 4) & 0x0F0F0F0Fu;
+      o[2 * j] = lo + (lo & 0x08080808u) * 30u;
+      o[2 * j + 1] = hi + (hi & 0x08080808u) * 30u;
+    }
+    out[2 * i] = make_uint4(o[0], o[1], o[2], o[3]);
+    out[2 * i + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+}  // namespace tc
+
+void launch_expand_codes8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t stream) {
+  const int64_t chunks = num_tokens * 4;
+  if (chunks == 0) return;
+  const int blocks = static_cast<int>(std::min<int64_t>((chunks + 255) / 256, 148LL * 16));
+  tc::expand_codes8_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const uint4*>(codes), chunks,
+                                                       reinterpret_cast<uint4*>(out));
+  count_launch();
+  check(cudaGetLastError(), "launch int8 expansion kernel");
+}
+
+namespace {
+// 2D tensor map over the int8 copy: {128 bytes, N rows}, box {128, 128}, 128-byte swizzle, zero fill.
+CUtensorMap make_codes8_map(const uint8_t* codes8, int64_t num_tokens) {
+  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn encode = nullptr;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q{};
+      check(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q),
+            "look up cuTensorMapEncodeTiled");
+      if (!fn || q != cudaDriverEntryPointSuccess) throw CudaFailure("cuTensorMapEncodeTiled is not available");
+      encode = reinterpret_cast<EncodeFn>(fn);
+    }
+  }
+  CUtensorMap m{};
+  const cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(num_tokens)};
+  const cuuint64_t strides[1] = {128};
+  const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(tc::kTileN)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(codes8), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw CudaFailure("cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
+  return m;
+}
+}  // namespace
+
 bool tc_scan_supported(const DocsView& d, const QueryView& q, const ReduceView& r, const TargetsView& tg,
                        bool residual) {
   return !residual && d.format == kFormatInt4 && d.dim == 128 && q.mode == kQueryI8 && r.reducer == kMaxSim &&
@@ -847,14 +953,18 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   prm.out = out;
   prm.error = err;
   const int grid = std::min<int>(sms, prm.num_units);
+  const bool pre = d.codes8 != nullptr;
+  const CUtensorMap tmap = pre ? make_codes8_map(d.codes8, d.num_tokens) : CUtensorMap{};
+  auto go = [&](auto kernel) {
+    check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes), "set tc smem");
+    kernel<<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(prm, tmap);
+  };
   if (d.token_scale) {
-    check(cudaFuncSetAttribute(tc::tc_scan_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes),
-          "set tc smem");
-    tc::tc_scan_kernel<true><<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(prm);
+    if (pre) go(tc::tc_scan_kernel<true, true>);
+    else go(tc::tc_scan_kernel<true, false>);
   } else {
-    check(cudaFuncSetAttribute(tc::tc_scan_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes),
-          "set tc smem");
-    tc::tc_scan_kernel<false><<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(prm);
+    if (pre) go(tc::tc_scan_kernel<false, true>);
+    else go(tc::tc_scan_kernel<false, false>);
   }
   count_launch();
   check(cudaGetLastError(), "launch tensor-core scan kernel");

@@ -52,6 +52,19 @@ def _run(engine, fn):
         _lib.set_engine(prev)
 
 
+@pytest.fixture(params=[1, 0], ids=["int8_copy", "expanding"], autouse=True)
+def tc_operands(request):
+    """Run every test with both tensor-core producers: operand tiles streamed by TMA from the resident
+    int8 copy of the corpus, and raw int4 rows expanded in shared memory per tile.  Handles built in
+    a test start with the setting of that test."""
+    from maxsim_b200 import _lib
+
+    prev = _lib.get_option("tc_int8_cache")
+    _lib.set_option("tc_int8_cache", request.param)
+    yield request.param
+    _lib.set_option("tc_int8_cache", prev)
+
+
 @pytest.mark.parametrize("gran", ["token", "tensor"])
 @pytest.mark.parametrize("batch,qtok", [(1, 1), (3, 24), (11, 24), (4, 32), (2, 100), (2, 128), (7, 20)])
 def test_tc_int8_scores_exact(oracle_c, gran, batch, qtok):
