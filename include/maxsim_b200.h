@@ -132,6 +132,42 @@ int msb_docs_set_residual(msb_docs* docs, const uint8_t* codes, int64_t num_toke
                           const float* token_scales);
 int msb_docs_clear_residual(msb_docs* docs);
 
+/* ---- streaming upload (load-to-GPU path) -------------------------------- */
+/* Replaces the host side of Corpus.load + int4_to_device / residual_int4_to_device
+ * (reference src/maxsim/sdk.py:331-400, experimental.py:271-305, cuda_extension.cu:2679-2773,
+ * 2777-2831): the resident arrays are allocated at their final size and filled chunk by chunk
+ * from host memory with asynchronous copies (pinned staging buffers overlap the copies with the
+ * caller's decompression of the next chunk); token scales are validated on the device at the end
+ * instead of by a host pass over every token.  No whole-corpus host copy is needed.
+ *
+ * msb_docs_create_for_upload takes the same arguments as msb_docs_create without the codes, plus
+ * `flags`: MSB_UPLOAD_TOKEN_SCALES allocates a per-token scale vector, MSB_UPLOAD_RESIDUAL an int4
+ * residual stream ([num_tokens, dim/2] codes and [num_tokens] scales).  Until msb_docs_upload_finish
+ * succeeds, every scoring call on the handle fails with MSB_ERR_INVALID_ARGUMENT. */
+#define MSB_UPLOAD_TOKEN_SCALES 1
+#define MSB_UPLOAD_RESIDUAL 2
+#define MSB_ARRAY_CODES 0                 /* [num_tokens, bytes per token] */
+#define MSB_ARRAY_TOKEN_SCALES 1          /* [num_tokens] fp32 */
+#define MSB_ARRAY_RESIDUAL_CODES 2        /* [num_tokens, dim/2] */
+#define MSB_ARRAY_RESIDUAL_TOKEN_SCALES 3 /* [num_tokens] fp32 */
+int msb_docs_create_for_upload(int32_t format, int32_t dim, int64_t num_tokens, const int64_t* offsets,
+                               int64_t num_docs, float scale, int32_t flags, msb_docs** out);
+/* Queues a copy of `bytes` host bytes into array `which` at byte offset `offset` on the handle's
+ * stream and returns at once with a ticket.  The host buffer must stay unchanged until
+ * msb_docs_upload_wait(ticket) returns (it is read asynchronously; pinned memory from
+ * msb_pinned_alloc lets the copy overlap host work).  Ranges outside the array are rejected. */
+int msb_docs_upload(msb_docs* docs, int32_t which, int64_t offset, const void* host, int64_t bytes,
+                    int64_t* ticket);
+int msb_docs_upload_wait(msb_docs* docs, int64_t ticket);
+/* Waits for every queued copy, checks the arrays on the device (int4 codes hold no nibble 8, the
+ * value -8; token scales are finite and > 0, with the messages of msb_docs_set_token_scales /
+ * msb_docs_set_residual), records `residual_scale` (ignored without MSB_UPLOAD_RESIDUAL) and opens
+ * the handle for scoring. */
+int msb_docs_upload_finish(msb_docs* docs, float residual_scale);
+/* Page-locked host staging buffers (cudaHostAlloc, portable across devices). */
+int msb_pinned_alloc(int64_t bytes, void** out);
+int msb_pinned_free(void* ptr);
+
 /* ---- scoring (host buffers, synchronous) -------------------------------
  * maxsim_batch / score_batch / score_candidates_batch / score_residual_batch /
  * score_residual_candidates_batch / maxsim_batch_int8q

@@ -42,11 +42,14 @@ from maxsim_b200.experimental import (
     topk_int4_maxsim,
 )
 from maxsim_b200.sdk import MODE_PRESETS, Corpus, CorpusMemoryReport, Index, Reranker, SearchResult
+from maxsim_b200.loader import load_reranker, load_resident_corpus
 
 __all__ = [
     "PackedDocs",
     "Corpus",
     "Index",
+    "load_reranker",
+    "load_resident_corpus",
     "Reranker",
     "SearchResult",
     "CorpusMemoryReport",

@@ -23,6 +23,12 @@ MSB_ERR_INTERNAL = 4
 
 FORMAT_INT4 = 0
 FORMAT_BINARY = 1
+UPLOAD_TOKEN_SCALES = 1
+UPLOAD_RESIDUAL = 2
+ARRAY_CODES = 0
+ARRAY_TOKEN_SCALES = 1
+ARRAY_RESIDUAL_CODES = 2
+ARRAY_RESIDUAL_TOKEN_SCALES = 3
 QUERY_F32 = 0
 QUERY_I8 = 1
 REDUCER_IDS = {"maxsim": 0, "weighted_maxsim": 1, "topk2": 2, "topk4": 3, "smoothsim": 4}
@@ -84,6 +90,12 @@ SIGNATURES = {
     "msb_docs_clear_doc_scales": (ctypes.c_int, [_vp]),
     "msb_docs_set_residual": (ctypes.c_int, [_vp, _vp, _i64, _f32, _vp]),
     "msb_docs_clear_residual": (ctypes.c_int, [_vp]),
+    "msb_docs_create_for_upload": (ctypes.c_int, [_i32, _i32, _i64, _vp, _i64, _f32, _i32, ctypes.POINTER(_vp)]),
+    "msb_docs_upload": (ctypes.c_int, [_vp, _i32, _i64, _vp, _i64, ctypes.POINTER(_i64)]),
+    "msb_docs_upload_wait": (ctypes.c_int, [_vp, _i64]),
+    "msb_docs_upload_finish": (ctypes.c_int, [_vp, _f32]),
+    "msb_pinned_alloc": (ctypes.c_int, [_i64, ctypes.POINTER(_vp)]),
+    "msb_pinned_free": (ctypes.c_int, [_vp]),
     "msb_docs_score": (ctypes.c_int, [_vp, _vp, _i32, _i32, ctypes.POINTER(ScoreOpts), _vp, _i64, _vp]),
     "msb_docs_topk": (ctypes.c_int, [_vp, _vp, _i32, _i32, _i32, ctypes.POINTER(ScoreOpts), _vp, _vp]),
     "msb_docs_cascade_topk": (ctypes.c_int, [_vp, _vp, _i32, _i32, _i32, _i32, ctypes.POINTER(ScoreOpts), _vp, _vp]),

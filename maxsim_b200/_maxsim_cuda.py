@@ -442,6 +442,22 @@ class CudaInt4PackedDocs(_Handle):
             raise ValueError("scale must be finite and > 0")
         super().__init__(packed, offsets, dim, scale)
 
+    @classmethod
+    def _for_upload(cls, offsets, num_tokens, dim, scale, flags):
+        """A handle whose arrays are allocated but not filled (``msb_docs_create_for_upload``); the
+        streaming loader fills them and finishes the upload before any scoring call."""
+        scale = float(np.float32(scale))
+        if not (scale > 0.0) or not np.isfinite(scale):
+            raise ValueError("scale must be finite and > 0")
+        offsets = _i64(offsets)
+        self = cls.__new__(cls)
+        self._h = ctypes.c_void_p()
+        self._dim = int(dim)
+        check(lib.msb_docs_create_for_upload(cls._format, int(dim), int(num_tokens), _vp(offsets),
+                                             offsets.shape[0] - 1, ctypes.c_float(scale), int(flags),
+                                             ctypes.byref(self._h)))
+        return self
+
     @property
     def scale(self):
         return float(self._info().scale)

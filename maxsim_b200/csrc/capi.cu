@@ -21,6 +21,8 @@ void launch_quantize_rows(const float*, int64_t, int, int8_t*, float*, int32_t*,
 void launch_topk_rows(const float*, int64_t, int, int64_t, int, const int64_t*, bool, float*, int64_t*, cudaStream_t);
 void launch_pack_int4(const float*, int64_t, int, bool, uint8_t*, float*, float*, void*, cudaStream_t);
 void launch_pack_signs(const float*, int64_t, int, uint8_t*, float*, cudaStream_t);
+void launch_check_positive_finite(const float*, int64_t, unsigned int*, cudaStream_t);
+void launch_check_int4_codes(const uint8_t*, int64_t, unsigned int*, cudaStream_t);
 bool tc_scan_supported(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, bool residual);
 void launch_tc_scan(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, float*, void* ws,
                     size_t ws_bytes, cudaStream_t);
@@ -134,6 +136,14 @@ struct msb_docs {
   // streams ready operand tiles with tiled TMA instead of expanding every tile for every query batch.
   DeviceBuf codes8;
   bool codes8_failed = false;  // allocation failed once: keep using the expanding scan
+  // Streaming upload (msb_docs_create_for_upload .. msb_docs_upload_finish): scoring is refused while
+  // open; each queued copy records an event in a small ring that its ticket names.
+  static constexpr int kUploadEvents = 16;
+  bool upload_open = false;
+  int32_t upload_flags = 0;
+  int64_t upload_serial = 0;
+  cudaEvent_t upload_events[kUploadEvents] = {};
+  DeviceBuf w_check;
 
   size_t bytes_per_token() const { return format == kFormatInt4 ? dim / 2 : dim / 8; }
   int64_t resident_bytes() const {
@@ -143,7 +153,7 @@ struct msb_docs {
   int64_t workspace_bytes() const {
     return static_cast<int64_t>(w_query.cap + w_qcodes.cap + w_qwords.cap + w_qscale.cap + w_qsum.cap +
                                 w_scores.cap + w_cands.cap + w_weights.cap + w_top_s.cap + w_top_i.cap +
-                                w_override.cap + w_fine.cap + w_tc.cap);
+                                w_override.cap + w_fine.cap + w_tc.cap + w_check.cap);
   }
   ~msb_docs() {
     int prev = -1;
@@ -153,8 +163,10 @@ struct msb_docs {
     DeviceBuf* all[] = {&codes,   &offsets,  &token_scale, &doc_scale, &residual_codes, &residual_token_scale,
                         &w_query, &w_qcodes, &w_qwords,    &w_qscale,  &w_qsum,         &w_scores,
                         &w_cands, &w_weights, &w_top_s,    &w_top_i,   &w_override,     &w_fine,
-                        &w_tc,    &codes8};
+                        &w_tc,    &codes8,   &w_check};
     for (DeviceBuf* b : all) b->release();
+    for (cudaEvent_t& e : upload_events)
+      if (e) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
     if (prev >= 0) cudaSetDevice(prev);
   }
@@ -322,7 +334,7 @@ void check_tc_flag(msb_docs* h, cudaStream_t s) {
 void check_query(msb_docs* h, const void* q, int batch, int qtok) {
   if (batch < 0 || qtok < 0) throw InvalidArgument("query must have shape [batch, query_tokens, dim]");
   if (!q && static_cast<int64_t>(batch) * qtok > 0) throw InvalidArgument("query pointer is NULL");
-  (void)h;
+  if (h && h->upload_open) throw InvalidArgument("the corpus upload has not finished (msb_docs_upload_finish)");
 }
 
 void check_candidates(msb_docs* h, const int64_t* c, int64_t m) {
@@ -597,6 +609,152 @@ int msb_docs_set_residual(msb_docs* h, const uint8_t* codes, int64_t num_tokens,
     check(cudaStreamSynchronize(h->stream), "synchronize residual upload");
     h->residual_scale = scale;
     h->has_residual = true;
+  });
+}
+
+int msb_docs_create_for_upload(int32_t format, int32_t dim, int64_t num_tokens, const int64_t* offsets,
+                               int64_t num_docs, float scale, int32_t flags, msb_docs** out) {
+  return guarded([&] {
+    if (!out) throw InvalidArgument("out is NULL");
+    *out = nullptr;
+    if (format == kFormatInt4 && (!(scale > 0.0F) || !std::isfinite(scale)))
+      throw InvalidArgument("scale must be finite and > 0");
+    if (flags & ~(MSB_UPLOAD_TOKEN_SCALES | MSB_UPLOAD_RESIDUAL)) throw InvalidArgument("unknown upload flags");
+    msb_docs* h = create_common(format, dim, num_tokens, offsets, num_docs);
+    try {
+      h->scale = format == kFormatInt4 ? scale : 1.0F;
+      const size_t n = static_cast<size_t>(num_tokens);
+      const size_t cbytes = h->bytes_per_token() * n;
+      if (cbytes) h->codes.ensure(cbytes, "cudaMalloc packed docs");
+      h->offsets.ensure(sizeof(int64_t) * (num_docs + 1) + kTailPad, "cudaMalloc offsets");
+      check(cudaMemcpyAsync(h->offsets.ptr, offsets, sizeof(int64_t) * (num_docs + 1), cudaMemcpyHostToDevice,
+                            h->stream),
+            "copy offsets to device");
+      if (flags & MSB_UPLOAD_TOKEN_SCALES)
+        h->token_scale.ensure(sizeof(float) * n + kTailPad, "cudaMalloc resident token scale vector");
+      if (flags & MSB_UPLOAD_RESIDUAL) {
+        const size_t rbytes = static_cast<size_t>(dim / 2) * n;
+        h->residual_codes.ensure(rbytes > 0 ? rbytes : 4, "cudaMalloc resident int4 residual data");
+        h->residual_token_scale.ensure(n > 0 ? sizeof(float) * n : 4, "cudaMalloc resident int4 residual token scales");
+      }
+      for (cudaEvent_t& e : h->upload_events)
+        check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "create upload event");
+      check(cudaStreamSynchronize(h->stream), "synchronize upload setup");
+      h->upload_flags = flags;
+      h->upload_open = true;
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+int msb_docs_upload(msb_docs* h, int32_t which, int64_t offset, const void* host, int64_t bytes, int64_t* ticket) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    if (!h->upload_open) throw InvalidArgument("the handle is not open for upload (msb_docs_create_for_upload)");
+    if (offset < 0 || bytes < 0) throw InvalidArgument("upload offset and size must be nonnegative");
+    if (bytes > 0 && !host) throw InvalidArgument("host pointer is NULL");
+    const int64_t n = h->num_tokens;
+    unsigned char* base = nullptr;
+    int64_t size = 0;
+    switch (which) {
+      case MSB_ARRAY_CODES:
+        base = static_cast<unsigned char*>(h->codes.ptr);
+        size = static_cast<int64_t>(h->bytes_per_token()) * n;
+        break;
+      case MSB_ARRAY_TOKEN_SCALES:
+        if (!(h->upload_flags & MSB_UPLOAD_TOKEN_SCALES)) throw InvalidArgument("the handle has no token scale upload");
+        base = static_cast<unsigned char*>(h->token_scale.ptr);
+        size = 4 * n;
+        break;
+      case MSB_ARRAY_RESIDUAL_CODES:
+        if (!(h->upload_flags & MSB_UPLOAD_RESIDUAL)) throw InvalidArgument("the handle has no residual upload");
+        base = static_cast<unsigned char*>(h->residual_codes.ptr);
+        size = static_cast<int64_t>(h->dim / 2) * n;
+        break;
+      case MSB_ARRAY_RESIDUAL_TOKEN_SCALES:
+        if (!(h->upload_flags & MSB_UPLOAD_RESIDUAL)) throw InvalidArgument("the handle has no residual upload");
+        base = static_cast<unsigned char*>(h->residual_token_scale.ptr);
+        size = 4 * n;
+        break;
+      default:
+        throw InvalidArgument("unknown upload array");
+    }
+    if (offset > size || bytes > size - offset) throw InvalidArgument("upload range exceeds the array");
+    DeviceGuard g(h->device);
+    if (bytes > 0)
+      check(cudaMemcpyAsync(base + offset, host, static_cast<size_t>(bytes), cudaMemcpyHostToDevice, h->stream),
+            "upload chunk to device");
+    const int64_t t = ++h->upload_serial;
+    check(cudaEventRecord(h->upload_events[t % msb_docs::kUploadEvents], h->stream), "record upload event");
+    if (ticket) *ticket = t;
+  });
+}
+
+int msb_docs_upload_wait(msb_docs* h, int64_t ticket) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    if (ticket <= 0 || ticket > h->upload_serial) throw InvalidArgument("unknown upload ticket");
+    DeviceGuard g(h->device);
+    // A slot reused by a later copy on the same stream completes after this ticket's copy.
+    check(cudaEventSynchronize(h->upload_events[ticket % msb_docs::kUploadEvents]), "wait for upload");
+  });
+}
+
+int msb_docs_upload_finish(msb_docs* h, float residual_scale) {
+  return guarded([&] {
+    if (!h) throw InvalidArgument("handle is NULL");
+    if (!h->upload_open) throw InvalidArgument("the handle is not open for upload (msb_docs_create_for_upload)");
+    const bool residual = (h->upload_flags & MSB_UPLOAD_RESIDUAL) != 0;
+    if (residual) {
+      if (h->format == kFormatBinary && residual_scale != 1.0F)
+        throw InvalidArgument("a binary handle's residual stream uses per-token scales only (scale must be 1)");
+      if (!(residual_scale > 0.0F) || !std::isfinite(residual_scale))
+        throw InvalidArgument("residual scale must be finite and > 0");
+    }
+    DeviceGuard g(h->device);
+    h->w_check.ensure(4 * sizeof(unsigned int), "cudaMalloc upload check flags");
+    unsigned int* bad = static_cast<unsigned int*>(h->w_check.ptr);
+    check(cudaMemsetAsync(bad, 0, 4 * sizeof(unsigned int), h->stream), "clear upload check flags");
+    const int64_t rbytes = static_cast<int64_t>(h->dim / 2) * h->num_tokens;
+    if (h->format == kFormatInt4) launch_check_int4_codes(static_cast<const uint8_t*>(h->codes.ptr), rbytes, bad, h->stream);
+    if (h->upload_flags & MSB_UPLOAD_TOKEN_SCALES)
+      launch_check_positive_finite(static_cast<const float*>(h->token_scale.ptr), h->num_tokens, bad + 1, h->stream);
+    if (residual) {
+      launch_check_int4_codes(static_cast<const uint8_t*>(h->residual_codes.ptr), rbytes, bad + 2, h->stream);
+      launch_check_positive_finite(static_cast<const float*>(h->residual_token_scale.ptr), h->num_tokens, bad + 3,
+                                   h->stream);
+    }
+    unsigned int flags[4] = {0, 0, 0, 0};
+    check(cudaMemcpyAsync(flags, bad, sizeof(flags), cudaMemcpyDeviceToHost, h->stream), "read upload check flags");
+    check(cudaStreamSynchronize(h->stream), "synchronize upload");
+    if (flags[0]) throw InvalidArgument("int4 codes must be symmetric int4 values in [-7, 7]");
+    if (flags[1]) throw InvalidArgument("token scales must be finite and > 0");
+    if (flags[2]) throw InvalidArgument("residual int4 codes must be symmetric int4 values in [-7, 7]");
+    if (flags[3]) throw InvalidArgument("residual token scales must be finite and > 0");
+    h->has_token_scale = (h->upload_flags & MSB_UPLOAD_TOKEN_SCALES) != 0;
+    if (residual) {
+      h->residual_scale = residual_scale;
+      h->has_residual = true;
+    }
+    h->upload_open = false;
+  });
+}
+
+int msb_pinned_alloc(int64_t bytes, void** out) {
+  return guarded([&] {
+    if (!out) throw InvalidArgument("out is NULL");
+    *out = nullptr;
+    if (bytes <= 0) throw InvalidArgument("staging buffer size must be > 0");
+    check(cudaHostAlloc(out, static_cast<size_t>(bytes), cudaHostAllocPortable), "cudaHostAlloc staging buffer");
+  });
+}
+
+int msb_pinned_free(void* ptr) {
+  return guarded([&] {
+    if (ptr) check(cudaFreeHost(ptr), "cudaFreeHost staging buffer");
   });
 }
 

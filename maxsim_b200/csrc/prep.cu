@@ -8,6 +8,8 @@
 //   nibble layout   src/maxsim/experimental.py:604-609   even dim in the low nibble
 //   sign bits       src/maxsim/_api.py:49-54             bit i of byte i/8, x >= 0 -> 1
 // fp32 division is IEEE (__fdiv_rn) and rintf rounds half to even, as NumPy.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace msb {
@@ -112,6 +114,52 @@ void launch_pack_signs(const float* x, int64_t n, int dim, uint8_t* bits, float*
   pack_signs_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(x, n, dim, bits, mean_abs);
   count_launch();
   check(cudaGetLastError(), "launch sign pack kernel");
+}
+
+// Sets *bad to 1 when any value is not finite or not > 0 (the reference's token-scale rule,
+// cuda_extension.cu:2753-2758 / experimental.py:699-700, checked on the device after an upload).
+__global__ void check_positive_finite_kernel(const float* __restrict__ x, int64_t n, unsigned int* __restrict__ bad) {
+  bool ok = true;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float v = x[i];
+    ok = ok && v > 0.0F && isfinite(v);
+  }
+  if (__any_sync(0xFFFFFFFFu, !ok) && (threadIdx.x & 31) == 0) atomicOr(bad, 1u);
+}
+
+// Sets *bad to 1 when any nibble of the int4 codes is 8 (the value -8): symmetric int4 codes lie in
+// [-7, 7] (reference experimental.py _validate_int4_packed, checked on the unpacked values).
+// A byte holds a nibble n == 8 iff (n ^ 8) == 0; zero bytes are found four at a time.
+__global__ void check_int4_codes_kernel(const uint32_t* __restrict__ words, int64_t nwords,
+                                        unsigned int* __restrict__ bad) {
+  bool ok = true;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nwords;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t w = words[i];
+    const uint32_t lo = (w & 0x0F0F0F0Fu) ^ 0x08080808u, hi = ((w >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+    const uint32_t zl = (lo - 0x01010101u) & ~lo & 0x80808080u, zh = (hi - 0x01010101u) & ~hi & 0x80808080u;
+    ok = ok && (zl | zh) == 0u;
+  }
+  if (__any_sync(0xFFFFFFFFu, !ok) && (threadIdx.x & 31) == 0) atomicOr(bad, 1u);
+}
+
+void launch_check_int4_codes(const uint8_t* codes, int64_t bytes, unsigned int* bad, cudaStream_t stream) {
+  if (bytes <= 0) return;
+  const int64_t nwords = bytes / 4;  // int4 rows are dim / 2 bytes, dim % 8 == 0
+  const int64_t blocks = std::min<int64_t>((nwords + 255) / 256, 148 * 16);
+  check_int4_codes_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      reinterpret_cast<const uint32_t*>(codes), nwords, bad);
+  count_launch();
+  check(cudaGetLastError(), "launch int4 code check kernel");
+}
+
+void launch_check_positive_finite(const float* x, int64_t n, unsigned int* bad, cudaStream_t stream) {
+  if (n <= 0) return;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 16);
+  check_positive_finite_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, n, bad);
+  count_launch();
+  check(cudaGetLastError(), "launch token scale check kernel");
 }
 
 }  // namespace msb

@@ -172,7 +172,10 @@ class Corpus:
         raise ValueError(_MODE_ERROR)
 
     # -- persistence (npz schema 2) ----------------------------------------
-    def save(self, path) -> None:
+    def save(self, path, *, compress: bool = True) -> None:
+        """Reference ``Corpus.save`` (src/maxsim/sdk.py:203-250): one ``.npz``, schema 2.
+        ``compress=False`` stores the members uncompressed (``np.savez``); int4 codes hardly compress,
+        and stored members stream to the GPU at file-read speed (``maxsim_b200.loader``)."""
         _validate_corpus(self)
         out = Path(path)
         out.parent.mkdir(parents=True, exist_ok=True)
@@ -243,7 +246,7 @@ class Corpus:
         else:
             raise ValueError("corpus has no packed payload")
         with out.open("wb") as handle:
-            np.savez_compressed(handle, **arrays)
+            (np.savez_compressed if compress else np.savez)(handle, **arrays)
         object.__setattr__(self, "_source_path", out.resolve())
 
     @classmethod
@@ -385,6 +388,18 @@ class Reranker:
         self._doc_index = {doc_id: i for i, doc_id in enumerate(self.corpus.doc_ids)}
 
     @classmethod
+    def _from_resident(cls, corpus: Corpus, *, int4_query: Literal["fp32", "int8"] = "fp32") -> "Reranker":
+        """Wrap a corpus whose payload the streaming loader already placed and checked on the device."""
+        if int4_query not in {"fp32", "int8"}:
+            raise ValueError("int4_query must be 'fp32' or 'int8'")
+        self = cls.__new__(cls)
+        self.corpus = corpus
+        self.device = "cuda"
+        self.int4_query = int4_query
+        self._doc_index = {doc_id: i for i, doc_id in enumerate(corpus.doc_ids)}
+        return self
+
+    @classmethod
     def from_corpus(cls, corpus: Corpus, *, device: Literal["cpu", "cuda"] = "cuda",
                     int4_query: Literal["fp32", "int8"] = "fp32") -> "Reranker":
         return cls(corpus, device=device, int4_query=int4_query)
@@ -392,6 +407,12 @@ class Reranker:
     @classmethod
     def load(cls, path, *, device: Literal["cpu", "cuda"] = "cuda",
              int4_query: Literal["fp32", "int8"] = "fp32") -> "Reranker":
+        """Reference ``Reranker.load`` (src/maxsim/sdk.py:393-396).  On CUDA the int4 family streams
+        from the file into device memory (``maxsim_b200.loader``); the device arrays are the same."""
+        if device == "cuda" and int4_query in {"fp32", "int8"}:
+            from maxsim_b200.loader import load_reranker
+
+            return load_reranker(path, int4_query=int4_query)
         return cls.from_corpus(Corpus.load(path), device=device, int4_query=int4_query)
 
     def search_arrays(self, query_embeddings, *, k: int = 10, rescore_candidates: int | None = None,

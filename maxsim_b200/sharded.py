@@ -81,6 +81,23 @@ class ShardedReranker:
         self._dist = dist
         self._bufs = {}
 
+    @classmethod
+    def load(cls, path, *, rank: int, world_size: int, int8_query: bool = True, group=None, **load_kw):
+        """This rank's shard of a saved int4 index, streamed from the file into the current CUDA
+        device (``maxsim_b200.loader``): each rank reads only its own documents' bytes."""
+        from maxsim_b200.loader import load_resident_corpus
+
+        with np.load(path, allow_pickle=False) as data:
+            offsets = np.ascontiguousarray(data["doc_offsets"], dtype=np.int64)
+        bounds = shard_bounds(offsets, world_size)
+        lo, hi = int(bounds[rank]), int(bounds[rank + 1])
+        corpus = load_resident_corpus(path, doc_range=(lo, hi), **load_kw)
+        if corpus.mode not in ("int4", "int4_per_token"):
+            raise ValueError("ShardedReranker.load supports the int4 and int4_per_token modes")
+        info = ShardInfo(rank=rank, world_size=world_size, doc_lo=lo, doc_hi=hi,
+                         num_docs_total=offsets.shape[0] - 1)
+        return cls(corpus.int4_packed.data, info, int8_query=int8_query, group=group)
+
     def _buffers(self, batch: int, k: int, device):
         key = (batch, k)
         if key not in self._bufs:
