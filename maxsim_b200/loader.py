@@ -30,8 +30,12 @@ from pathlib import Path
 import numpy as np
 from numpy.lib import format as npy_format
 
-from maxsim_b200 import _lib
-from maxsim_b200._lib import check, lib
+
+def _native():
+    """The C-ABI library, imported on first use (the package imports without a built library)."""
+    from maxsim_b200 import _lib
+
+    return _lib
 
 _STREAMED_MODES = frozenset({"int4", "int4_per_token", "int4_residual"})
 
@@ -91,7 +95,7 @@ class _Staging:
         try:
             for _ in range(count):
                 ptr = ctypes.c_void_p()
-                check(lib.msb_pinned_alloc(self.nbytes, ctypes.byref(ptr)))
+                _native().check(_native().lib.msb_pinned_alloc(self.nbytes, ctypes.byref(ptr)))
                 self._ptrs.append(ptr)
                 self._views.append(np.ctypeslib.as_array((ctypes.c_uint8 * self.nbytes).from_address(ptr.value)))
                 self._tickets.append(0)
@@ -104,13 +108,14 @@ class _Staging:
         slot = self._next
         self._next = (self._next + 1) % len(self._ptrs)
         if self._tickets[slot]:
-            check(lib.msb_docs_upload_wait(handle, self._tickets[slot]))
+            _native().check(_native().lib.msb_docs_upload_wait(handle, self._tickets[slot]))
             self._tickets[slot] = 0
         return slot, self._views[slot]
 
     def submit(self, handle, slot: int, which: int, offset: int, nbytes: int) -> None:
         ticket = ctypes.c_int64()
-        check(lib.msb_docs_upload(handle, which, offset, self._ptrs[slot], nbytes, ctypes.byref(ticket)))
+        _native().check(_native().lib.msb_docs_upload(handle, which, offset, self._ptrs[slot], nbytes,
+                                                       ctypes.byref(ticket)))
         self._tickets[slot] = int(ticket.value)
 
     def drain(self, handle) -> bool:
@@ -118,13 +123,13 @@ class _Staging:
         ok = True
         for slot, ticket in enumerate(self._tickets):
             if ticket:
-                ok = lib.msb_docs_upload_wait(handle, ticket) == _lib.MSB_OK and ok
+                ok = _native().lib.msb_docs_upload_wait(handle, ticket) == _native().MSB_OK and ok
                 self._tickets[slot] = 0
         return ok
 
     def free(self) -> None:
         for ptr in self._ptrs:
-            lib.msb_pinned_free(ptr)
+            _native().lib.msb_pinned_free(ptr)
         self._ptrs, self._views, self._tickets = [], [], []
 
 
@@ -192,6 +197,8 @@ def load_resident_corpus(path, *, doc_range: tuple[int, int] | None = None, chun
     from maxsim_b200.sdk import Corpus, _move_corpus, _validate_offset_values
     from maxsim_b200 import _maxsim_cuda
 
+    _lib = _native()
+    lib, check = _lib.lib, _lib.check
     stats = {} if stats is None else stats
     t_start = time.perf_counter()
     source = Path(path).resolve()

@@ -76,3 +76,20 @@ def test_uncompressed_save_round_trips(tmp_path):
     assert again.doc_ids == idx.doc_ids
     assert np.array_equal(again.int4_packed.data, idx.int4_packed.data)
     assert np.array_equal(again.int4_packed.token_scale, idx.int4_packed.token_scale)
+
+
+def test_package_imports_without_the_built_library(tmp_path):
+    """A fresh checkout has no libmaxsim_b200.so yet: importing the package (and its build module)
+    must work so the library can be built; only a call into the library fails."""
+    import shutil
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    src = Path(m.__file__).parent
+    shutil.copytree(src, tmp_path / "maxsim_b200", ignore=shutil.ignore_patterns("*.so", "_build", "__pycache__"))
+    code = ("import maxsim_b200, maxsim_b200.loader, maxsim_b200.build\n"
+            "try:\n    maxsim_b200.loader._native()\nexcept ImportError as e:\n    print('missing:', e)\n")
+    out = subprocess.run([sys.executable, "-c", code], cwd=tmp_path, capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    assert "missing:" in out.stdout and "no CPU fallback" in out.stdout
