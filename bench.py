@@ -58,6 +58,42 @@ WORKLOAD = ("C4: 100,000 pages x 1,030 tokens (dim 128) per-token int4 (6.59 GB 
             "1,024 queries x 24 tokens int8, batch 64, full-scan top-10")
 
 
+def batch_sweep(args, torch, _lib, handle, queries, device):
+    """One line per batch size: scan + top-k of the whole resident corpus, CUDA events on the launching
+    stream, against both roofs (algorithmic HBM bytes and int8 tensor ops of that batch)."""
+    hbm_peak, bf16_peak, peak_kind = _peaks()
+    int8_peak = 2.0 * bf16_peak
+    n_tok = NUM_PAGES * PAGE_TOKENS
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    for b in (int(x) for x in args.batch_sweep.split(",")):
+        nb = queries.shape[0] // b
+        qb = queries[:nb * b].view(nb, b, QUERY_TOKENS, DIM)
+        out_s = torch.empty((b, TOP_K), dtype=torch.float32, device=device)
+        out_i = torch.empty((b, TOP_K), dtype=torch.int64, device=device)
+        for i in range(args.warmup):
+            handle.topk_batch_device(qb[i % nb], TOP_K, out_s, out_i, int8_query=True, stream=stream.cuda_stream)
+        reps = max(3, args.steps)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        torch.cuda.synchronize(device)
+        ev[0].record(stream)
+        for i in range(reps):
+            handle.topk_batch_device(qb[i % nb], TOP_K, out_s, out_i, int8_query=True, stream=stream.cuda_stream)
+        ev[1].record(stream)
+        torch.cuda.synchronize(device)
+        ms = ev[0].elapsed_time(ev[1]) / reps
+        algo_bytes = n_tok * (DIM // 2 + 4) + 8 * (NUM_PAGES + 1) + b * QUERY_TOKENS * DIM + b * TOP_K * 12
+        algo_ops = 2.0 * b * QUERY_TOKENS * n_tok * DIM
+        hbm_ms, tc_ms = 1e3 * algo_bytes / (hbm_peak * 1e9), 1e3 * algo_ops / (int8_peak * 1e12)
+        print(json.dumps({"sweep": "batch", "batch": b, "query_rows": b * QUERY_TOKENS, "ms": ms,
+                          "queries_per_s": b / (ms * 1e-3), "hbm_gbs": algo_bytes / (ms * 1e-3) / 1e9,
+                          "tensor_tops": algo_ops / (ms * 1e-3) / 1e12, "hbm_roof_ms": hbm_ms, "tensor_roof_ms": tc_ms,
+                          "bound": "tensor" if tc_ms > hbm_ms else "hbm", "frac_of_roof": max(hbm_ms, tc_ms) / ms,
+                          "peaks": f"HBM {hbm_peak} GB/s, int8 {int8_peak} TOP/s ({peak_kind})",
+                          "workload": f"C4 corpus ({NUM_PAGES} pages x {PAGE_TOKENS} tokens), int8 queries x "
+                                      f"{QUERY_TOKENS} tokens, top-{TOP_K}"}), flush=True)
+
+
 def _peaks():
     path = REPO / "MEASURED_PEAKS.json"
     if path.exists():
@@ -230,6 +266,9 @@ def main() -> None:
     ap.add_argument("--engine", type=int, default=0, help="0 auto, 1 SIMT, 2 tensor core")
     ap.add_argument("--pages", type=int, default=NUM_PAGES,
                     help="corpus pages (default: the C4 workload; smaller values are for profiling captures)")
+    ap.add_argument("--batch-sweep", default=None,
+                    help="comma-separated batch sizes: time the scan + top-k per batch size on the resident corpus "
+                         "and print one roofline line per size instead of the bench line (HBM/tensor crossover)")
     args = ap.parse_args()
     globals()["NUM_PAGES"] = args.pages
     if args.warmup < 3:
@@ -281,6 +320,10 @@ def main() -> None:
     queries, _ = make_queries(torch, device)
     n_batches = NUM_QUERIES // BATCH
     queries = queries.view(n_batches, BATCH, QUERY_TOKENS, DIM)  # one step = one [64, 24, 128] batch
+    if args.batch_sweep:
+        if world == 1:
+            batch_sweep(args, torch, _lib, handle, queries.view(-1, QUERY_TOKENS, DIM), device)
+        return
     info = ShardInfo(rank=rank, world_size=world, doc_lo=page_lo, doc_hi=page_hi, num_docs_total=NUM_PAGES)
     searcher = ShardedReranker(handle, info, int8_query=True)
     work_stream = torch.cuda.Stream(device)  # every timed launch goes to this stream

@@ -59,7 +59,6 @@ namespace tc {
 
 constexpr int kTileN = 128;       // tokens per tile (MMA N)
 constexpr int kG = 2;             // query tiles per unit, sharing every expanded token tile
-constexpr int kStages = 4;        // expanded-tile ring (B operand), released by the MMA commit
 constexpr int kMeta = 8;          // tile metadata ring (scales, document ends), released by the epilogue
 constexpr int kRaw = 6;           // raw-code ring filled by bulk copies
 constexpr int kAccBufs = 2;       // token-tile accumulator buffers (each kG x 128 TMEM columns)
@@ -103,7 +102,6 @@ constexpr int kATileBytes = 128 * 128;                 // 16 KB
 constexpr int kBTileBytes = kTileN * 128;              // 16 KB
 constexpr int kRawCodeBytes = kTileN * 64;             // 8 KB
 constexpr int kRawScaleFloats = kTileN + 4;            // aligned superset of the tile's scales
-constexpr int kRawBytes = ((kRawCodeBytes + kRawScaleFloats * 4 + 127) / 128) * 128;
 constexpr int kUoffEntries = kMaxRangeDocs + 4;
 // Token scales in the order the epilogue threads consume them: column c = 64h + 8j + 2t + b is held by
 // threads with t % 4 = t at index h * 80 + t * 20 + 2j + b, so each thread reads its 16 scales of a
@@ -120,18 +118,29 @@ struct StageMeta {
   int32_t valid;             // valid columns
 };
 constexpr int kMetaBytes = ((sizeof(StageMeta) + 127) / 128) * 128;
-constexpr int kOffA = 0;                                         // [2 buffers][kG] query tiles
-constexpr int kOffB = kOffA + 2 * kG * kATileBytes;
-constexpr int kOffRaw = kOffB + kStages * kBTileBytes;
-constexpr int kOffMeta = kOffRaw + kRaw * kRawBytes;
-constexpr int kOffUoff = kOffMeta + kMeta * kMetaBytes;
-constexpr int kOffRow = kOffUoff + 2 * kUoffEntries * 8;
 constexpr int kRowBytes = kSegGroup * kG * 128 * 4;    // [group][query tile][row]
-constexpr int kOffBar = kOffRow + kRowBytes + 128;     // + per-group doc ids
-constexpr int kNumBars = 2 * kStages + 2 * kMeta + 2 * kRaw + kAccBufs + 8;
-constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 64 + 1024;  // + alignment slack
-static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
-static_assert(kOffUoff % 16 == 0 && kOffRaw % 16 == 0 && kRawBytes % 16 == 0, "bulk-copy alignment");
+// Shared-memory layout (bytes, from a 1024-aligned base).  When operand tiles arrive by TMA from the
+// resident int8 copy (kPre), the raw ring carries only token scales, and the bytes the expanding path
+// uses for raw int4 rows hold more B stages instead: a deeper operand prefetch for passes that are
+// bound by DRAM latency (few query tiles, so little work per tile).
+template <bool kPre>
+struct Layout {
+  static constexpr int stages = kPre ? 8 : 4;            // B ring, released by the MMA commit
+  static constexpr int raw_code_bytes = kPre ? 0 : kRawCodeBytes;
+  static constexpr int raw_bytes = ((raw_code_bytes + kRawScaleFloats * 4 + 127) / 128) * 128;
+  static constexpr int off_a = 0;                        // [2 buffers][kG] query tiles
+  static constexpr int off_b = off_a + 2 * kG * kATileBytes;
+  static constexpr int off_raw = off_b + stages * kBTileBytes;
+  static constexpr int off_meta = off_raw + kRaw * raw_bytes;
+  static constexpr int off_uoff = off_meta + kMeta * kMetaBytes;
+  static constexpr int off_row = off_uoff + 2 * kUoffEntries * 8;
+  static constexpr int off_bar = off_row + kRowBytes + 128;  // + per-group doc ids
+  static constexpr int num_bars = 2 * stages + 2 * kMeta + 2 * kRaw + kAccBufs + 8;
+  static constexpr int bytes = off_bar + num_bars * 8 + 64 + 1024;  // + alignment slack
+  static_assert(bytes <= 227 * 1024, "shared memory budget");
+  static_assert(off_b % 1024 == 0 && kBTileBytes % 1024 == 0, "128-byte-swizzled operand tiles");
+  static_assert(off_uoff % 16 == 0 && off_raw % 16 == 0 && raw_bytes % 16 == 0, "bulk-copy alignment");
+};
 
 // ---------------------------------------------------------------------------
 // PTX wrappers
@@ -294,13 +303,14 @@ struct Ring {
 // tile metadata.  Otherwise the loader copies raw int4 rows and the expanders build the B stage.
 template <bool kTokenScale, bool kPre>
 __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap) {
+  using L = Layout<kPre>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                          ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* full = bars;                         // [kStages]  expanders -> MMA
-  uint64_t* tile_done = full + kStages;          // [kStages]  MMA commit -> expanders (stage free), epilogue (acc full)
-  uint64_t* m_full = tile_done + kStages;        // [kMeta]    expanders -> epilogue
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::off_bar);
+  uint64_t* full = bars;                         // [stages]   expanders or TMA -> MMA
+  uint64_t* tile_done = full + L::stages;        // [stages]   MMA commit -> loader/expanders (stage free), epilogue
+  uint64_t* m_full = tile_done + L::stages;      // [kMeta]    expanders -> epilogue
   uint64_t* m_empty = m_full + kMeta;            // [kMeta]    epilogue -> expanders
   uint64_t* raw_full = m_empty + kMeta;          // [kRaw]     bulk copies -> expanders
   uint64_t* raw_empty = raw_full + kRaw;         // [kRaw]     expanders -> loader
@@ -309,17 +319,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
   uint64_t* a_empty = a_full + 2;                // [2]        MMA commit -> expanders
   uint64_t* u_full = a_empty + 2;                // [2]        unit offsets bulk copy -> segment warp
   uint64_t* u_empty = u_full + 2;                // [2]        segment warp -> loader
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::num_bars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* rowval = reinterpret_cast<float*>(smem + kOffRow);                      // [group][kG][128]
-  int32_t* group_doc = reinterpret_cast<int32_t*>(smem + kOffRow + kRowBytes);  // [kSegGroup]
+  float* rowval = reinterpret_cast<float*>(smem + L::off_row);                      // [group][kG][128]
+  int32_t* group_doc = reinterpret_cast<int32_t*>(smem + L::off_row + kRowBytes);  // [kSegGroup]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int Q = p.qtok;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < L::stages; ++s) {
       mbar_init(&full[s], kPre ? 1 : kXWarps);  // kPre: the loader's expect_tx + the TMA's bytes
       mbar_init(&tile_done[s], 1);
     }
@@ -367,26 +377,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           const int64_t count = ((unit.d_hi + 1 - first) + 1) & ~1LL;
           const uint32_t bytes = static_cast<uint32_t>(count * 8);
           mbar_expect_tx(&u_full[ub], bytes);
-          bulk_g2s(smem + kOffUoff + ub * kUoffEntries * 8, p.offsets + first, bytes, &u_full[ub]);
+          bulk_g2s(smem + L::off_uoff + ub * kUoffEntries * 8, p.offsets + first, bytes, &u_full[ub]);
         }
         for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
           if (kPre) {
             // B stage: wait until the MMAs that read it have completed, then one tiled TMA load
             if (!mbar_wait(&tile_done[stg.idx], stg.phase ^ 1, abort_flag, p.error, 43)) goto done;
             mbar_expect_tx(&full[stg.idx], static_cast<uint32_t>(kBTileBytes));
-            tma_load_2d(smem + kOffB + stg.idx * kBTileBytes, &tmap, 0, static_cast<int>(t0), &full[stg.idx]);
-            stg.next<kStages>();
+            tma_load_2d(smem + L::off_b + stg.idx * kBTileBytes, &tmap, 0, static_cast<int>(t0), &full[stg.idx]);
+            stg.next<L::stages>();
           }
           if (!mbar_wait(&raw_empty[raw.idx], raw.phase ^ 1, abort_flag, p.error, 42)) goto done;
           const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
-          unsigned char* rb = smem + kOffRaw + raw.idx * kRawBytes;
+          unsigned char* rb = smem + L::off_raw + raw.idx * L::raw_bytes;
           const uint32_t code_bytes = kPre ? 0u : static_cast<uint32_t>(valid) * 64u;
           uint32_t scale_bytes = 0;
           const int64_t s_first = t0 & ~3LL;
           if (kTokenScale) scale_bytes = static_cast<uint32_t>(((t0 + valid - s_first + 3) & ~3LL) * 4);
           mbar_expect_tx(&raw_full[raw.idx], code_bytes + scale_bytes);
           if (!kPre) bulk_g2s(rb, p.codes + t0 * 64, code_bytes, &raw_full[raw.idx]);
-          if (kTokenScale) bulk_g2s(rb + kRawCodeBytes, p.token_scale + s_first, scale_bytes, &raw_full[raw.idx]);
+          if (kTokenScale) bulk_g2s(rb + L::raw_code_bytes, p.token_scale + s_first, scale_bytes, &raw_full[raw.idx]);
           raw.next<kRaw>();
         }
       }
@@ -405,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       for (int row = xtid; row < 128; row += kXWarps * 32) {  // query rows of each tile of the pair
 #pragma unroll
         for (int g = 0; g < kG; ++g) {
-          unsigned char* A = smem + kOffA + (abuf * kG + g) * kATileBytes;
+          unsigned char* A = smem + L::off_a + (abuf * kG + g) * kATileBytes;
           const int b = (unit.qpair * kG + g) * p.qpt + row / Q;
           const bool valid = row < p.qpt * Q && b < p.batch;
           const int4* src = reinterpret_cast<const int4*>(p.qwords + (static_cast<int64_t>(b) * Q + row % Q) * 32);
@@ -422,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         if (lane == 0) mbar_arrive(&a_full[abuf]);
       }
       const int ub = iter & 1;
-      const int64_t* uoff = reinterpret_cast<const int64_t*>(smem + kOffUoff + ub * kUoffEntries * 8);
+      const int64_t* uoff = reinterpret_cast<const int64_t*>(smem + L::off_uoff + ub * kUoffEntries * 8);
       const int64_t ufirst = unit.d_lo & ~1LL;
       if (xwarp == 0 && !mbar_wait(&u_full[ub], (iter >> 1) & 1, abort_flag, p.error, 13)) goto done;
       int64_t next_doc = unit.d_lo;  // first document whose end has not been passed
@@ -430,12 +440,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         if (!mbar_wait(&raw_full[raw.idx], raw.phase, abort_flag, p.error, 14)) goto done;
         if (!kPre && !mbar_wait(&tile_done[stg.idx], stg.phase ^ 1, abort_flag, p.error, 12)) goto done;
         if (!mbar_wait(&m_empty[mst.idx], mst.phase ^ 1, abort_flag, p.error, 15)) goto done;
-        const unsigned char* rb = smem + kOffRaw + raw.idx * kRawBytes;
-        unsigned char* Bt = smem + kOffB + stg.idx * kBTileBytes;
-        StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kOffMeta + mst.idx * kMetaBytes);
+        const unsigned char* rb = smem + L::off_raw + raw.idx * L::raw_bytes;
+        unsigned char* Bt = smem + L::off_b + stg.idx * kBTileBytes;
+        StageMeta* meta = reinterpret_cast<StageMeta*>(smem + L::off_meta + mst.idx * kMetaBytes);
         const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
         if (kPre && kTokenScale) {
-          const float* rs = reinterpret_cast<const float*>(rb + kRawCodeBytes);
+          const float* rs = reinterpret_cast<const float*>(rb + L::raw_code_bytes);
           for (int r = xtid; r < valid; r += kXWarps * 32) meta->scale[scale_slot(r)] = rs[(t0 & 3) + r];
         }
 #pragma unroll 1
@@ -463,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
           }
           if (kTokenScale) {
-            const float* rs = reinterpret_cast<const float*>(rb + kRawCodeBytes);
+            const float* rs = reinterpret_cast<const float*>(rb + L::raw_code_bytes);
             meta->scale[scale_slot(r)] = rs[(t0 & 3) + r];
           }
         }
@@ -503,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           mbar_arrive(&raw_empty[raw.idx]);
         }
         raw.next<kRaw>();
-        stg.next<kStages>();
+        stg.next<L::stages>();
         mst.next<kMeta>();
       }
       if (xwarp == 0 && lane == 0) mbar_arrive(&u_empty[ub]);
@@ -520,13 +530,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       // query tiles of the pair that hold at least one query
       const int n_tiles = min(kG, (p.batch - unit.qpair * kG * p.qpt + p.qpt - 1) / p.qpt);
       if (!mbar_wait(&a_full[abuf], (iter >> 1) & 1, abort_flag, p.error, 21)) goto done;
-      const uint32_t a_addr = smem_u32(smem + kOffA + abuf * kG * kATileBytes);
+      const uint32_t a_addr = smem_u32(smem + L::off_a + abuf * kG * kATileBytes);
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
         if (!mbar_wait(&full[stg.idx], stg.phase, abort_flag, p.error, 22)) goto done;
         if (!mbar_wait(&acc_empty[acc.idx], acc.phase ^ 1, abort_flag, p.error, 23)) goto done;
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t b_addr = smem_u32(smem + kOffB + stg.idx * kBTileBytes);
+          const uint32_t b_addr = smem_u32(smem + L::off_b + stg.idx * kBTileBytes);
           for (int g = 0; g < n_tiles; ++g) {
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((acc.idx * kG + g) * kTileN);
             const uint32_t ag = a_addr + static_cast<uint32_t>(g * kATileBytes);
@@ -540,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           mma_commit(&tile_done[stg.idx]);
         }
         __syncwarp();
-        stg.next<kStages>();
+        stg.next<L::stages>();
         acc.next<kAccBufs>();
       }
       if (lane == 0) mma_commit(&a_empty[abuf]);
@@ -561,7 +571,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
       const Unit unit = p.units[u];
       const int tile = unit.qpair * kG + g;
-      const bool tile_live = tile * p.qpt < p.batch;
+      // Rows of this warp's TMEM lane quarter that hold query tokens; a quarter without any (small
+      // batches) skips its loads and arithmetic and only walks the document ends with the others.
+      const int tile_rows = max(0, min(p.qpt, p.batch - tile * p.qpt)) * Q;
+      const bool tile_live = q4 * 32 < tile_rows;
       // the row this thread stores when a document ends: i = t % 4
       const int wrow = q4 * 32 + 16 * (tc >> 1) + 8 * (tc & 1) + tq;
       const int wb = tile * p.qpt + wrow / Q;
@@ -578,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         // Acquire the expanders' metadata writes for this tile (meta ring slot).
         if (!mbar_wait(&m_full[mst.idx], mst.phase, abort_flag, p.error, 32)) goto done;
         tc_fence_after();
-        const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + kOffMeta + mst.idx * kMetaBytes);
+        const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + L::off_meta + mst.idx * kMetaBytes);
         const int valid = meta->valid;
         const int nseg = meta->nseg;
         const bool last_tile = t0 + kTileN >= unit.tok_hi;
@@ -734,7 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           if (!released) mbar_arrive(&acc_empty[acc.idx]);
           mbar_arrive(&m_empty[mst.idx]);
         }
-        stg.next<kStages>();
+        stg.next<L::stages>();
         acc.next<kAccBufs>();
         mst.next<kMeta>();
       }
@@ -955,16 +968,16 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   const int grid = std::min<int>(sms, prm.num_units);
   const bool pre = d.codes8 != nullptr;
   const CUtensorMap tmap = pre ? make_codes8_map(d.codes8, d.num_tokens) : CUtensorMap{};
-  auto go = [&](auto kernel) {
-    check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes), "set tc smem");
-    kernel<<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(prm, tmap);
+  auto go = [&](auto kernel, int smem_bytes) {
+    check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes), "set tc smem");
+    kernel<<<grid, tc::kThreads, smem_bytes, stream>>>(prm, tmap);
   };
   if (d.token_scale) {
-    if (pre) go(tc::tc_scan_kernel<true, true>);
-    else go(tc::tc_scan_kernel<true, false>);
+    if (pre) go(tc::tc_scan_kernel<true, true>, tc::Layout<true>::bytes);
+    else go(tc::tc_scan_kernel<true, false>, tc::Layout<false>::bytes);
   } else {
-    if (pre) go(tc::tc_scan_kernel<false, true>);
-    else go(tc::tc_scan_kernel<false, false>);
+    if (pre) go(tc::tc_scan_kernel<false, true>, tc::Layout<true>::bytes);
+    else go(tc::tc_scan_kernel<false, false>, tc::Layout<false>::bytes);
   }
   count_launch();
   check(cudaGetLastError(), "launch tensor-core scan kernel");
