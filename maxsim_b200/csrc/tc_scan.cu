@@ -622,17 +622,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               released = true;
             }
             if (kTokenScale) {
-              // exact int32 dot -> float, then fl(dot * s_t)
+              // exact int32 dot -> float (all 64 first), then fl(dot * s_t)
+#pragma unroll
+              for (int k = 0; k < 32; ++k) {
+                ra[k] = __float_as_uint(__int2float_rn(static_cast<int32_t>(ra[k])));
+                rb[k] = __float_as_uint(__int2float_rn(static_cast<int32_t>(rb[k])));
+              }
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                ra[4 * j + 0] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(ra[4 * j + 0])), sc[j].x));
-                ra[4 * j + 1] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(ra[4 * j + 1])), sc[j].y));
-                ra[4 * j + 2] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(ra[4 * j + 2])), sc[j].x));
-                ra[4 * j + 3] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(ra[4 * j + 3])), sc[j].y));
-                rb[4 * j + 0] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(rb[4 * j + 0])), sc[j].x));
-                rb[4 * j + 1] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(rb[4 * j + 1])), sc[j].y));
-                rb[4 * j + 2] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(rb[4 * j + 2])), sc[j].x));
-                rb[4 * j + 3] = __float_as_uint(__fmul_rn(__int2float_rn(static_cast<int32_t>(rb[4 * j + 3])), sc[j].y));
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float s1 = (e & 1) ? sc[j].y : sc[j].x;
+                  ra[4 * j + e] = __float_as_uint(__fmul_rn(__uint_as_float(ra[4 * j + e]), s1));
+                  rb[4 * j + e] = __float_as_uint(__fmul_rn(__uint_as_float(rb[4 * j + e]), s1));
+                }
               }
             }
           }
@@ -646,13 +649,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 if (kTokenScale) {
 #define MSB_ROWMAX(X, s, R)                                                                                \
   {                                                                                                        \
-    float m0 = fmaxf(__uint_as_float(X[2 * s]), __uint_as_float(X[2 * s + 1]));                            \
-    float m1 = fmaxf(__uint_as_float(X[4 + 2 * s]), __uint_as_float(X[4 + 2 * s + 1]));                    \
-    _Pragma("unroll") for (int j = 2; j < 8; j += 2) {                                                     \
-      m0 = fmax3(m0, __uint_as_float(X[4 * j + 2 * s]), __uint_as_float(X[4 * j + 2 * s + 1]));            \
-      m1 = fmax3(m1, __uint_as_float(X[4 * j + 4 + 2 * s]), __uint_as_float(X[4 * j + 4 + 2 * s + 1]));    \
-    }                                                                                                      \
-    R = fmax3(R, m0, m1);                                                                                  \
+    float m0 = fmax3(__uint_as_float(X[2 * s]), __uint_as_float(X[2 * s + 1]), __uint_as_float(X[16 + 2 * s])); \
+    float m1 = fmax3(__uint_as_float(X[4 + 2 * s]), __uint_as_float(X[4 + 2 * s + 1]),                     \
+                     __uint_as_float(X[20 + 2 * s]));                                                      \
+    float m2 = fmax3(__uint_as_float(X[8 + 2 * s]), __uint_as_float(X[8 + 2 * s + 1]),                     \
+                     __uint_as_float(X[16 + 2 * s + 1]));                                                  \
+    float m3 = fmax3(__uint_as_float(X[12 + 2 * s]), __uint_as_float(X[12 + 2 * s + 1]),                   \
+                     __uint_as_float(X[20 + 2 * s + 1]));                                                  \
+    m0 = fmax3(m0, __uint_as_float(X[24 + 2 * s]), __uint_as_float(X[24 + 2 * s + 1]));                  \
+    m1 = fmax3(m1, __uint_as_float(X[28 + 2 * s]), __uint_as_float(X[28 + 2 * s + 1]));                  \
+    R = fmax3(R, fmax3(m0, m1, m2), m3);                                                                   \
   }
                   MSB_ROWMAX(ra, 0, run[0]) MSB_ROWMAX(ra, 1, run[1]) MSB_ROWMAX(rb, 0, run[2]) MSB_ROWMAX(rb, 1, run[3])
 #undef MSB_ROWMAX
