@@ -135,7 +135,7 @@ struct Layout {
   static constexpr int off_uoff = off_meta + kMeta * kMetaBytes;
   static constexpr int off_row = off_uoff + 2 * kUoffEntries * 8;
   static constexpr int off_bar = off_row + kRowBytes + 128;  // + per-group doc ids
-  static constexpr int num_bars = 2 * stages + 2 * kMeta + 2 * kRaw + kAccBufs + 8;
+  static constexpr int num_bars = 2 * stages + 2 * kMeta + 2 * kRaw + kAccBufs + 9;
   static constexpr int bytes = off_bar + num_bars * 8 + 64 + 1024;  // + alignment slack
   static_assert(bytes <= 227 * 1024, "shared memory budget");
   static_assert(off_b % 1024 == 0 && kBTileBytes % 1024 == 0, "128-byte-swizzled operand tiles");
@@ -196,9 +196,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void named_bar(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   // K-major, no swizzle: 8-row x 16-byte core matrices; LBO between core
   // matrices along K, SBO between 8-row groups; version 1 (bits 46-47).
@@ -319,6 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
   uint64_t* a_empty = a_full + 2;                // [2]        MMA commit -> expanders
   uint64_t* u_full = a_empty + 2;                // [2]        unit offsets bulk copy -> segment warp
   uint64_t* u_empty = u_full + 2;                // [2]        segment warp -> loader
+  uint64_t* epi_bar = u_empty + 2;               // [1]        epilogue warps among themselves (document flush)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::num_bars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* rowval = reinterpret_cast<float*>(smem + L::off_row);                      // [group][kG][128]
@@ -348,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       mbar_init(&u_full[a], 1);
       mbar_init(&u_empty[a], 1);
     }
+    mbar_init(epi_bar, kEpiWarps);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -509,9 +508,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         __syncwarp();
         if (lane == 0) {
           if (!kPre) mbar_arrive(&full[stg.idx]);
-          mbar_arrive(&m_full[mst.idx]);
           mbar_arrive(&raw_empty[raw.idx]);
         }
+        // With TMA operand tiles, expander warp 0 also waits for the tile's MMAs, so that m_full tells the
+        // epilogue both that the metadata is written and that the accumulators are ready: one barrier
+        // wait per tile on the epilogue's critical path instead of two.
+        if (kPre && xwarp == 0 && !mbar_wait(&tile_done[stg.idx], stg.phase, abort_flag, p.error, 16)) goto done;
+        if (lane == 0) mbar_arrive(&m_full[mst.idx]);
         raw.next<kRaw>();
         stg.next<L::stages>();
         mst.next<kMeta>();
@@ -568,6 +571,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     const int tq = lane >> 2, tc = lane & 3;
     const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
     Ring stg, acc, mst;
+    // Barrier among the epilogue warps around a document flush: an mbarrier with bounded waits, so a
+    // warp that gives up on a timeout never leaves the others waiting for good.
+    uint32_t epi_phase = 0;
+    auto epi_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(epi_bar);
+      const bool ok = mbar_wait(epi_bar, epi_phase, abort_flag, p.error, 33);
+      epi_phase ^= 1u;
+      return ok;
+    };
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
       const Unit unit = p.units[u];
       const int tile = unit.qpair * kG + g;
@@ -587,8 +600,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       int32_t run_i[4] = {INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN};    // tensor-scale variant
       int pending = 0;
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
-        if (!mbar_wait(&tile_done[stg.idx], stg.phase, abort_flag, p.error, 31)) goto done;
-        // Acquire the expanders' metadata writes for this tile (meta ring slot).
+        if (!kPre && !mbar_wait(&tile_done[stg.idx], stg.phase, abort_flag, p.error, 31)) goto done;
+        // Acquire the expanders' metadata writes for this tile (meta ring slot) and, with TMA operand
+        // tiles, the completion of its MMAs (observed by expander warp 0 before it arrives).
         if (!mbar_wait(&m_full[mst.idx], mst.phase, abort_flag, p.error, 32)) goto done;
         tc_fence_after();
         const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + L::off_meta + mst.idx * kMetaBytes);
@@ -731,7 +745,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             }
             ++sgi;
             if (++pending == kSegGroup || (sgi == nseg && last_tile)) {
-              named_bar(1, kEpiWarps * 32);
+              if (!epi_sync()) goto done;
               for (int x = etid; x < pending * nq; x += kEpiWarps * 32) {
                 const int gd = x / nq, qx = x % nq;
                 const int gq = qx < nq0 ? 0 : 1;
@@ -742,7 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 p.out[static_cast<int64_t>((unit.qpair * kG + gq) * p.qpt + qq) * p.num_docs + group_doc[gd]] =
                     __fmul_rn(sacc, p.scale);
               }
-              named_bar(1, kEpiWarps * 32);
+              if (!epi_sync()) goto done;
               pending = 0;
             }
           }
