@@ -280,6 +280,30 @@ __device__ __forceinline__ void tmem_ld16x256b_x8(uint32_t taddr, uint32_t* r) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Maximum of row s (0 or 1) of a 16x256b chunk half X (its 16 values X[4j + 2s], X[4j + 2s + 1]) folded
+// into R: four independent chains of three-input maxima.
+__device__ __forceinline__ float row_max16(const uint32_t* X, int s, float R) {
+  float m0 = fmax3(__uint_as_float(X[2 * s]), __uint_as_float(X[2 * s + 1]), __uint_as_float(X[16 + 2 * s]));
+  float m1 = fmax3(__uint_as_float(X[4 + 2 * s]), __uint_as_float(X[4 + 2 * s + 1]), __uint_as_float(X[20 + 2 * s]));
+  const float m2 =
+      fmax3(__uint_as_float(X[8 + 2 * s]), __uint_as_float(X[8 + 2 * s + 1]), __uint_as_float(X[16 + 2 * s + 1]));
+  const float m3 =
+      fmax3(__uint_as_float(X[12 + 2 * s]), __uint_as_float(X[12 + 2 * s + 1]), __uint_as_float(X[20 + 2 * s + 1]));
+  m0 = fmax3(m0, __uint_as_float(X[24 + 2 * s]), __uint_as_float(X[24 + 2 * s + 1]));
+  m1 = fmax3(m1, __uint_as_float(X[28 + 2 * s]), __uint_as_float(X[28 + 2 * s + 1]));
+  return fmax3(R, fmax3(m0, m1, m2), m3);
+}
+__device__ __forceinline__ int32_t row_max16i(const uint32_t* X, int s, int32_t R) {
+  int32_t m0 = max(static_cast<int32_t>(X[2 * s]), static_cast<int32_t>(X[2 * s + 1]));
+  int32_t m1 = max(static_cast<int32_t>(X[4 + 2 * s]), static_cast<int32_t>(X[4 + 2 * s + 1]));
+#pragma unroll
+  for (int j = 2; j < 8; j += 2) {
+    m0 = __vimax3_s32(m0, static_cast<int32_t>(X[4 * j + 2 * s]), static_cast<int32_t>(X[4 * j + 2 * s + 1]));
+    m1 = __vimax3_s32(m1, static_cast<int32_t>(X[4 * j + 4 + 2 * s]), static_cast<int32_t>(X[4 * j + 4 + 2 * s + 1]));
+  }
+  return __vimax3_s32(R, m0, m1);
+}
+
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
@@ -612,7 +636,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         const uint32_t tbase = tmem_base + lane_base + static_cast<uint32_t>((acc.idx * kG + g) * kTileN);
         int sgi = 0;
         bool released = false;
-        for (int c0 = 0; c0 < valid; c0 += 64) {
+#pragma unroll
+        for (int ci = 0; ci < 2; ++ci) {
+          const int c0 = 64 * ci;
+          if (c0 >= valid) break;
           const int c1 = min(c0 + 64, valid);  // this chunk's valid columns [c0, c1)
           uint32_t ra[32], rb[32];              // lanes +0..15 (rows i = 0, 1) and +16..31 (rows i = 2, 3)
           if (tile_live) {
@@ -653,6 +680,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               }
             }
           }
+          if (nseg == 0 && tile_live && c1 == c0 + 64) {
+            // no document ends in this tile and the open document covers the whole chunk: no walk
+            if (kTokenScale) {
+              run[0] = row_max16(ra, 0, run[0]);
+              run[1] = row_max16(ra, 1, run[1]);
+              run[2] = row_max16(rb, 0, run[2]);
+              run[3] = row_max16(rb, 1, run[3]);
+            } else {
+              run_i[0] = row_max16i(ra, 0, run_i[0]);
+              run_i[1] = row_max16i(ra, 1, run_i[1]);
+              run_i[2] = row_max16i(rb, 0, run_i[2]);
+              run_i[3] = row_max16i(rb, 1, run_i[3]);
+            }
+            continue;
+          }
           int a = c0;
           while (true) {
             const int e = nseg == 0 ? 0x7FFF : (sgi < nseg ? meta->seg_end[sgi] : 0x7FFF);
@@ -661,36 +703,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               if (a == c0 && bnd == c0 + 64) {
                 // whole chunk inside one document: two independent chains per row
                 if (kTokenScale) {
-#define MSB_ROWMAX(X, s, R)                                                                                \
-  {                                                                                                        \
-    float m0 = fmax3(__uint_as_float(X[2 * s]), __uint_as_float(X[2 * s + 1]), __uint_as_float(X[16 + 2 * s])); \
-    float m1 = fmax3(__uint_as_float(X[4 + 2 * s]), __uint_as_float(X[4 + 2 * s + 1]),                     \
-                     __uint_as_float(X[20 + 2 * s]));                                                      \
-    float m2 = fmax3(__uint_as_float(X[8 + 2 * s]), __uint_as_float(X[8 + 2 * s + 1]),                     \
-                     __uint_as_float(X[16 + 2 * s + 1]));                                                  \
-    float m3 = fmax3(__uint_as_float(X[12 + 2 * s]), __uint_as_float(X[12 + 2 * s + 1]),                   \
-                     __uint_as_float(X[20 + 2 * s + 1]));                                                  \
-    m0 = fmax3(m0, __uint_as_float(X[24 + 2 * s]), __uint_as_float(X[24 + 2 * s + 1]));                  \
-    m1 = fmax3(m1, __uint_as_float(X[28 + 2 * s]), __uint_as_float(X[28 + 2 * s + 1]));                  \
-    R = fmax3(R, fmax3(m0, m1, m2), m3);                                                                   \
-  }
-                  MSB_ROWMAX(ra, 0, run[0]) MSB_ROWMAX(ra, 1, run[1]) MSB_ROWMAX(rb, 0, run[2]) MSB_ROWMAX(rb, 1, run[3])
-#undef MSB_ROWMAX
+                  run[0] = row_max16(ra, 0, run[0]);
+                  run[1] = row_max16(ra, 1, run[1]);
+                  run[2] = row_max16(rb, 0, run[2]);
+                  run[3] = row_max16(rb, 1, run[3]);
                 } else {
-#define MSB_ROWMAXI(X, s, R)                                                                               \
-  {                                                                                                        \
-    int32_t m0 = max(static_cast<int32_t>(X[2 * s]), static_cast<int32_t>(X[2 * s + 1]));                  \
-    int32_t m1 = max(static_cast<int32_t>(X[4 + 2 * s]), static_cast<int32_t>(X[4 + 2 * s + 1]));          \
-    _Pragma("unroll") for (int j = 2; j < 8; j += 2) {                                                     \
-      m0 = __vimax3_s32(m0, static_cast<int32_t>(X[4 * j + 2 * s]), static_cast<int32_t>(X[4 * j + 2 * s + 1])); \
-      m1 = __vimax3_s32(m1, static_cast<int32_t>(X[4 * j + 4 + 2 * s]),                                   \
-                        static_cast<int32_t>(X[4 * j + 4 + 2 * s + 1]));                                   \
-    }                                                                                                      \
-    R = __vimax3_s32(R, m0, m1);                                                                           \
-  }
-                  MSB_ROWMAXI(ra, 0, run_i[0]) MSB_ROWMAXI(ra, 1, run_i[1]) MSB_ROWMAXI(rb, 0, run_i[2])
-                  MSB_ROWMAXI(rb, 1, run_i[3])
-#undef MSB_ROWMAXI
+                  run_i[0] = row_max16i(ra, 0, run_i[0]);
+                  run_i[1] = row_max16i(ra, 1, run_i[1]);
+                  run_i[2] = row_max16i(rb, 0, run_i[2]);
+                  run_i[3] = row_max16i(rb, 1, run_i[3]);
                 }
               } else {
                 const int la = a - c0 - 2 * tc, lb = bnd - c0 - 2 * tc;  // element (j, b) is column 8j + b here
