@@ -97,8 +97,11 @@ int64_t msb_launch_count(void);
  * where unsupported).  "tc_int8_cache": 1 (default) lets the tensor-core engine
  * keep a resident int8 copy of an int4 corpus (128 B per token, built on first
  * use and counted in resident_bytes) and stream operand tiles from it with
- * TMA; 0 expands int4 rows per tile instead.  Unknown names return
- * MSB_ERR_INVALID_ARGUMENT. */
+ * TMA; 0 expands int4 rows per tile instead.  "tc_f16_cache": 1 keeps an f16
+ * copy instead (256 B per token, per-token-scale corpora) and runs kind::f16
+ * MMAs whose fp32 accumulators hold the exact integer dots, so the epilogue
+ * converts nothing; 0 (default) because its doubled MMA and operand traffic
+ * made it slower.  Unknown names return MSB_ERR_INVALID_ARGUMENT. */
 int msb_set_option(const char* name, int64_t value);
 int msb_get_option(const char* name, int64_t* value);
 

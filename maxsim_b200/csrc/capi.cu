@@ -29,11 +29,14 @@ void launch_tc_scan(const DocsView&, const QueryView&, const ReduceView&, const 
 size_t tc_scan_workspace_bytes(const DocsView&, const QueryView&, const TargetsView&);
 bool tc_int8_cache_supported(const DocsView&);
 void launch_expand_codes8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t);
+void launch_expand_codes16(const uint8_t* codes, int64_t num_tokens, uint16_t* out, cudaStream_t);
 
 static std::atomic<int64_t> g_launches{0};
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 static std::atomic<int> g_engine{0};  // 0 auto, 1 SIMT, 2 tensor core
 static std::atomic<int> g_tc_int8_cache{1};  // keep an int8-expanded copy of int4 corpora for the tc engine
+static std::atomic<int> g_tc_f16_cache{0};   // keep an f16 copy instead (per-token scales): no conversion in the
+                                             // epilogue, but twice the MMAs and operand bytes; measured slower
 static std::atomic<uint64_t> g_corpus_serial{0};
 }  // namespace msb
 
@@ -136,6 +139,10 @@ struct msb_docs {
   // streams ready operand tiles with tiled TMA instead of expanding every tile for every query batch.
   DeviceBuf codes8;
   bool codes8_failed = false;  // allocation failed once: keep using the expanding scan
+  // The same values as f16 ([N, 128], 256 B per token): tensor-core f16 operands whose fp32 accumulators
+  // hold the exact integer dot, so the epilogue converts nothing.
+  DeviceBuf codes16;
+  bool codes16_failed = false;
   // Streaming upload (msb_docs_create_for_upload .. msb_docs_upload_finish): scoring is refused while
   // open; each queued copy records an event in a small ring that its ticket names.
   static constexpr int kUploadEvents = 16;
@@ -147,7 +154,7 @@ struct msb_docs {
 
   size_t bytes_per_token() const { return format == kFormatInt4 ? dim / 2 : dim / 8; }
   int64_t resident_bytes() const {
-    return static_cast<int64_t>(codes.cap + codes8.cap + offsets.cap + token_scale.cap + doc_scale.cap + residual_codes.cap +
+    return static_cast<int64_t>(codes.cap + codes8.cap + codes16.cap + offsets.cap + token_scale.cap + doc_scale.cap + residual_codes.cap +
                                 residual_token_scale.cap);
   }
   int64_t workspace_bytes() const {
@@ -163,7 +170,7 @@ struct msb_docs {
     DeviceBuf* all[] = {&codes,   &offsets,  &token_scale, &doc_scale, &residual_codes, &residual_token_scale,
                         &w_query, &w_qcodes, &w_qwords,    &w_qscale,  &w_qsum,         &w_scores,
                         &w_cands, &w_weights, &w_top_s,    &w_top_i,   &w_override,     &w_fine,
-                        &w_tc,    &codes8,   &w_check};
+                        &w_tc,    &codes8,   &codes16,   &w_check};
     for (DeviceBuf* b : all) b->release();
     for (cudaEvent_t& e : upload_events)
       if (e) cudaEventDestroy(e);
@@ -297,7 +304,23 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
     const size_t ws = tc_scan_workspace_bytes(r.docs, qv, tg);
     h->w_tc.ensure(ws > 0 ? ws : 16, "cudaMalloc tensor-core scan workspace");
     DocsView dv = r.docs;
-    if (g_tc_int8_cache.load() && !h->codes8_failed && tc_int8_cache_supported(dv)) {
+    if (g_tc_f16_cache.load() && !h->codes16_failed && dv.token_scale && tc_int8_cache_supported(dv)) {
+      if (!h->codes16.ptr) {
+        const size_t bytes = static_cast<size_t>(h->num_tokens) * 256;
+        void* p = nullptr;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) {
+          (void)cudaGetLastError();  // not enough memory for the f16 copy: use the int8 copy
+          h->codes16_failed = true;
+        } else {
+          h->codes16.ptr = p;
+          h->codes16.cap = bytes;
+          launch_expand_codes16(h->codes.as<uint8_t>(), h->num_tokens, static_cast<uint16_t*>(h->codes16.ptr),
+                                stream);
+        }
+      }
+      if (h->codes16.ptr) dv.codes16 = static_cast<const uint16_t*>(h->codes16.ptr);
+    }
+    if (!dv.codes16 && g_tc_int8_cache.load() && !h->codes8_failed && tc_int8_cache_supported(dv)) {
       if (!h->codes8.ptr) {
         const size_t bytes = static_cast<size_t>(h->num_tokens) * 128;
         void* p = nullptr;
@@ -418,6 +441,11 @@ int msb_set_option(const char* name, int64_t value) {
       g_tc_int8_cache.store(static_cast<int>(value));
       return;
     }
+    if (std::strcmp(name, "tc_f16_cache") == 0) {
+      if (value != 0 && value != 1) throw InvalidArgument("tc_f16_cache must be 0 or 1");
+      g_tc_f16_cache.store(static_cast<int>(value));
+      return;
+    }
     throw InvalidArgument(std::string("unknown option: ") + name);
   });
 }
@@ -431,6 +459,10 @@ int msb_get_option(const char* name, int64_t* value) {
     }
     if (std::strcmp(name, "tc_int8_cache") == 0) {
       *value = g_tc_int8_cache.load();
+      return;
+    }
+    if (std::strcmp(name, "tc_f16_cache") == 0) {
+      *value = g_tc_f16_cache.load();
       return;
     }
     throw InvalidArgument(std::string("unknown option: ") + name);

@@ -51,6 +51,7 @@ struct DocsView {
   const int64_t* host_offsets;  // host copy of offsets (work partitioning)
   uint64_t corpus_id;          // unique per resident corpus (keys host-side caches)
   const uint8_t* codes8;       // int4 codes expanded to int8 in scan K order [N, 128], or nullptr
+  const uint16_t* codes16;     // the same as f16 values [N, 128], or nullptr (tensor-core f16 operands)
   int64_t num_docs;
   int64_t num_tokens;
   int dim;

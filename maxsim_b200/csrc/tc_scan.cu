@@ -46,7 +46,8 @@
 //     document ends, and tiles without document ends skip the walk.
 // Every mbarrier wait is bounded (%globaltimer); on timeout the kernel raises
 // an error flag, drains, frees its TMEM and returns.
-#include <cuda.h>  // CUtensorMap (the encoder is fetched through cudaGetDriverEntryPoint)
+#include <cuda.h>
+#include <cuda_fp16.h>  // CUtensorMap (the encoder is fetched through cudaGetDriverEntryPoint)
 
 #include <algorithm>
 #include <mutex>
@@ -123,14 +124,19 @@ constexpr int kRowBytes = kSegGroup * kG * 128 * 4;    // [group][query tile][ro
 // resident int8 copy (kPre), the raw ring carries only token scales, and the bytes the expanding path
 // uses for raw int4 rows hold more B stages instead: a deeper operand prefetch for passes that are
 // bound by DRAM latency (few query tiles, so little work per tile).
-template <bool kPre>
+// With f16 operands (kF16, from the resident f16 copy) each operand tile is twice as large (two 128-byte
+// swizzled K halves of 64 values) and the query tiles are single-buffered to keep 4 B stages.
+template <bool kPre, bool kF16 = false>
 struct Layout {
-  static constexpr int stages = kPre ? 8 : 4;            // B ring, released by the MMA commit
+  static constexpr int stages = kF16 ? 4 : (kPre ? 8 : 4);  // B ring, released by the MMA commit
+  static constexpr int a_tile = kF16 ? 2 * kATileBytes : kATileBytes;
+  static constexpr int b_tile = kF16 ? 2 * kBTileBytes : kBTileBytes;
+  static constexpr int a_bufs = kF16 ? 1 : 2;
   static constexpr int raw_code_bytes = kPre ? 0 : kRawCodeBytes;
   static constexpr int raw_bytes = ((raw_code_bytes + kRawScaleFloats * 4 + 127) / 128) * 128;
-  static constexpr int off_a = 0;                        // [2 buffers][kG] query tiles
-  static constexpr int off_b = off_a + 2 * kG * kATileBytes;
-  static constexpr int off_raw = off_b + stages * kBTileBytes;
+  static constexpr int off_a = 0;                        // [a_bufs][kG] query tiles
+  static constexpr int off_b = off_a + a_bufs * kG * a_tile;
+  static constexpr int off_raw = off_b + stages * b_tile;
   static constexpr int off_meta = off_raw + kRaw * raw_bytes;
   static constexpr int off_uoff = off_meta + kMeta * kMetaBytes;
   static constexpr int off_row = off_uoff + 2 * kUoffEntries * 8;
@@ -138,7 +144,7 @@ struct Layout {
   static constexpr int num_bars = 2 * stages + 2 * kMeta + 2 * kRaw + kAccBufs + 9;
   static constexpr int bytes = off_bar + num_bars * 8 + 64 + 1024;  // + alignment slack
   static_assert(bytes <= 227 * 1024, "shared memory budget");
-  static_assert(off_b % 1024 == 0 && kBTileBytes % 1024 == 0, "128-byte-swizzled operand tiles");
+  static_assert(off_b % 1024 == 0 && b_tile % 1024 == 0 && a_tile % 1024 == 0, "128-byte-swizzled operand tiles");
   static_assert(off_uoff % 16 == 0 && off_raw % 16 == 0 && raw_bytes % 16 == 0, "bulk-copy alignment");
 };
 
@@ -207,6 +213,14 @@ __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
       ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -322,9 +336,10 @@ struct Ring {
 // kPre: the int4 codes were expanded once into an int8 copy (same K order); each B stage is a tiled TMA
 // load of 128 rows from it, landing in the 128-byte-swizzled layout, and the expanders only stage the
 // tile metadata.  Otherwise the loader copies raw int4 rows and the expanders build the B stage.
-template <bool kTokenScale, bool kPre>
+template <bool kTokenScale, bool kPre, bool kF16>
 __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap) {
-  using L = Layout<kPre>;
+  using L = Layout<kPre, kF16>;
+  static_assert(!kF16 || (kPre && kTokenScale), "f16 operands come from the resident copy, with token scales");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                          ~static_cast<uintptr_t>(1023));
@@ -406,8 +421,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           if (kPre) {
             // B stage: wait until the MMAs that read it have completed, then one tiled TMA load
             if (!mbar_wait(&tile_done[stg.idx], stg.phase ^ 1, abort_flag, p.error, 43)) goto done;
-            mbar_expect_tx(&full[stg.idx], static_cast<uint32_t>(kBTileBytes));
-            tma_load_2d(smem + L::off_b + stg.idx * kBTileBytes, &tmap, 0, static_cast<int>(t0), &full[stg.idx]);
+            mbar_expect_tx(&full[stg.idx], static_cast<uint32_t>(L::b_tile));
+            unsigned char* bdst = smem + L::off_b + stg.idx * L::b_tile;
+            tma_load_2d(bdst, &tmap, 0, static_cast<int>(t0), &full[stg.idx]);
+            // f16: the second K half (values 64..127, byte 128 of each row: x * 2 B is 16-byte aligned)
+            if (kF16) tma_load_2d(bdst + kBTileBytes, &tmap, 64, static_cast<int>(t0), &full[stg.idx]);
             stg.next<L::stages>();
           }
           if (!mbar_wait(&raw_empty[raw.idx], raw.phase ^ 1, abort_flag, p.error, 42)) goto done;
@@ -432,20 +450,38 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     int iter = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
       const Unit unit = p.units[u];
-      const int abuf = iter & 1;
-      if (iter >= 2 && !mbar_wait(&a_empty[abuf], ((iter >> 1) - 1) & 1, abort_flag, p.error, 11)) goto done;
+      const int abuf = iter % L::a_bufs;
+      const int ause = iter / L::a_bufs;
+      if (ause >= 1 && !mbar_wait(&a_empty[abuf], (ause - 1) & 1, abort_flag, p.error, 11)) goto done;
 #pragma unroll 1
       for (int row = xtid; row < 128; row += kXWarps * 32) {  // query rows of each tile of the pair
 #pragma unroll
         for (int g = 0; g < kG; ++g) {
-          unsigned char* A = smem + L::off_a + (abuf * kG + g) * kATileBytes;
+          unsigned char* A = smem + L::off_a + (abuf * kG + g) * L::a_tile;
           const int b = (unit.qpair * kG + g) * p.qpt + row / Q;
           const bool valid = row < p.qpt * Q && b < p.batch;
           const int4* src = reinterpret_cast<const int4*>(p.qwords + (static_cast<int64_t>(b) * Q + row % Q) * 32);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             int4 v = valid ? __ldg(src + c) : make_int4(0, 0, 0, 0);
-            *reinterpret_cast<int4*>(A + tile_off(row, c)) = v;
+            if (kF16) {
+              // 16 int8 values -> 16 f16 (exact): 32 bytes at byte 32c of the row, K half c / 4
+              const uint32_t w[4] = {static_cast<uint32_t>(v.x), static_cast<uint32_t>(v.y),
+                                     static_cast<uint32_t>(v.z), static_cast<uint32_t>(v.w)};
+              uint32_t h2[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int8_t lo = static_cast<int8_t>((w[i >> 1] >> (16 * (i & 1))) & 0xFF);
+                const int8_t hi = static_cast<int8_t>((w[i >> 1] >> (16 * (i & 1) + 8)) & 0xFF);
+                h2[i] = static_cast<uint32_t>(__half_as_ushort(__int2half_rn(lo))) |
+                        (static_cast<uint32_t>(__half_as_ushort(__int2half_rn(hi))) << 16);
+              }
+              unsigned char* Ah = A + (c >> 2) * kATileBytes;
+              *reinterpret_cast<uint4*>(Ah + tile_off(row, 2 * (c & 3))) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+              *reinterpret_cast<uint4*>(Ah + tile_off(row, 2 * (c & 3) + 1)) = make_uint4(h2[4], h2[5], h2[6], h2[7]);
+            } else {
+              *reinterpret_cast<int4*>(A + tile_off(row, c)) = v;
+            }
           }
         }
       }
@@ -464,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         if (!kPre && !mbar_wait(&tile_done[stg.idx], stg.phase ^ 1, abort_flag, p.error, 12)) goto done;
         if (!mbar_wait(&m_empty[mst.idx], mst.phase ^ 1, abort_flag, p.error, 15)) goto done;
         const unsigned char* rb = smem + L::off_raw + raw.idx * L::raw_bytes;
-        unsigned char* Bt = smem + L::off_b + stg.idx * kBTileBytes;
+        unsigned char* Bt = smem + L::off_b + stg.idx * L::b_tile;
         StageMeta* meta = reinterpret_cast<StageMeta*>(smem + L::off_meta + mst.idx * kMetaBytes);
         const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
         if (kPre && kTokenScale) {
@@ -547,31 +583,45 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     }
   } else if (warp == kMmaWarp) {
     // =================== MMA issuer ===================
+    // instruction descriptors: D s32, A/B s8 (kind::i8) or D f32, A/B f16 (kind::f16); K-major; N, M
     constexpr uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kTileN >> 3) << 17) |
                                (static_cast<uint32_t>(128 >> 4) << 24);
+    constexpr uint32_t idesc16 = (1u << 4) | (static_cast<uint32_t>(kTileN >> 3) << 17) |
+                                 (static_cast<uint32_t>(128 >> 4) << 24);
     Ring stg, acc;
     int iter = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
       const Unit unit = p.units[u];
-      const int abuf = iter & 1;
+      const int abuf = iter % L::a_bufs;
       // query tiles of the pair that hold at least one query
       const int n_tiles = min(kG, (p.batch - unit.qpair * kG * p.qpt + p.qpt - 1) / p.qpt);
-      if (!mbar_wait(&a_full[abuf], (iter >> 1) & 1, abort_flag, p.error, 21)) goto done;
-      const uint32_t a_addr = smem_u32(smem + L::off_a + abuf * kG * kATileBytes);
+      if (!mbar_wait(&a_full[abuf], (iter / L::a_bufs) & 1, abort_flag, p.error, 21)) goto done;
+      const uint32_t a_addr = smem_u32(smem + L::off_a + abuf * kG * L::a_tile);
       for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
         if (!mbar_wait(&full[stg.idx], stg.phase, abort_flag, p.error, 22)) goto done;
         if (!mbar_wait(&acc_empty[acc.idx], acc.phase ^ 1, abort_flag, p.error, 23)) goto done;
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t b_addr = smem_u32(smem + L::off_b + stg.idx * kBTileBytes);
+          const uint32_t b_addr = smem_u32(smem + L::off_b + stg.idx * L::b_tile);
           for (int g = 0; g < n_tiles; ++g) {
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((acc.idx * kG + g) * kTileN);
-            const uint32_t ag = a_addr + static_cast<uint32_t>(g * kATileBytes);
+            const uint32_t ag = a_addr + static_cast<uint32_t>(g * L::a_tile);
+            if (kF16) {
+              // 8 steps of K = 16 f16 (32 bytes): 4 per 128-byte K half, the halves 16 KB apart
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint64_t ad = umma_desc(ag + 32u * k, 16u, 1024u);
-              const uint64_t bd = umma_desc(b_addr + 32u * k, 16u, 1024u);
-              mma_i8(d_tmem, ad, bd, idesc, k > 0 ? 1u : 0u);
+              for (int k = 0; k < 8; ++k) {
+                const uint32_t off = static_cast<uint32_t>((k >> 2) * kBTileBytes + 32 * (k & 3));
+                const uint64_t ad = umma_desc(ag + off, 16u, 1024u);
+                const uint64_t bd = umma_desc(b_addr + off, 16u, 1024u);
+                mma_f16(d_tmem, ad, bd, idesc16, k > 0 ? 1u : 0u);
+              }
+            } else {
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const uint64_t ad = umma_desc(ag + 32u * k, 16u, 1024u);
+                const uint64_t bd = umma_desc(b_addr + 32u * k, 16u, 1024u);
+                mma_i8(d_tmem, ad, bd, idesc, k > 0 ? 1u : 0u);
+              }
             }
           }
           mma_commit(&tile_done[stg.idx]);
@@ -663,11 +713,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               released = true;
             }
             if (kTokenScale) {
-              // exact int32 dot -> float (all 64 first), then fl(dot * s_t)
+              // exact int32 dot -> float (all 64 first), then fl(dot * s_t); f16 operands accumulate the
+              // same integer exactly in fp32 (|products| <= 1016, |sums| < 2^17), so nothing to convert
+              if (!kF16) {
 #pragma unroll
-              for (int k = 0; k < 32; ++k) {
-                ra[k] = __float_as_uint(__int2float_rn(static_cast<int32_t>(ra[k])));
-                rb[k] = __float_as_uint(__int2float_rn(static_cast<int32_t>(rb[k])));
+                for (int k = 0; k < 32; ++k) {
+                  ra[k] = __float_as_uint(__int2float_rn(static_cast<int32_t>(ra[k])));
+                  rb[k] = __float_as_uint(__int2float_rn(static_cast<int32_t>(rb[k])));
+                }
               }
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
@@ -869,7 +922,42 @@ __global__ void expand_codes8_kernel(const uint4* __restrict__ in, int64_t n_chu
     out[2 * i + 1] = make_uint4(o[4], o[5], o[6], o[7]);
   }
 }
+// int4 codes -> f16 values in the same K order as the int8 copy (16 input bytes -> 32 values, 64 bytes).
+__global__ void expand_codes16_kernel(const uint4* __restrict__ in, int64_t n_chunks, uint4* __restrict__ out) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_chunks;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint4 v = __ldg(in + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t o[4];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {  // low nibbles of bytes 4j..4j+3, then their high nibbles
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          int n0 = static_cast<int>((w[j] >> (16 * q + 4 * half)) & 0xF);
+          int n1 = static_cast<int>((w[j] >> (16 * q + 8 + 4 * half)) & 0xF);
+          n0 -= (n0 & 8) << 1;  // two's complement nibble
+          n1 -= (n1 & 8) << 1;
+          o[2 * half + q] = static_cast<uint32_t>(__half_as_ushort(__int2half_rn(n0))) |
+                            (static_cast<uint32_t>(__half_as_ushort(__int2half_rn(n1))) << 16);
+        }
+      }
+      out[4 * i + j] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
 }  // namespace tc
+
+void launch_expand_codes16(const uint8_t* codes, int64_t num_tokens, uint16_t* out, cudaStream_t stream) {
+  const int64_t chunks = num_tokens * 4;
+  if (chunks == 0) return;
+  const int blocks = static_cast<int>(std::min<int64_t>((chunks + 255) / 256, 148LL * 16));
+  tc::expand_codes16_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const uint4*>(codes), chunks,
+                                                        reinterpret_cast<uint4*>(out));
+  count_launch();
+  check(cudaGetLastError(), "launch f16 expansion kernel");
+}
 
 void launch_expand_codes8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t stream) {
   const int64_t chunks = num_tokens * 4;
@@ -883,7 +971,7 @@ void launch_expand_codes8(const uint8_t* codes, int64_t num_tokens, uint8_t* out
 
 namespace {
 // 2D tensor map over the int8 copy: {128 bytes, N rows}, box {128, 128}, 128-byte swizzle, zero fill.
-CUtensorMap make_codes8_map(const uint8_t* codes8, int64_t num_tokens) {
+CUtensorMap make_operand_map(const void* base, int64_t num_tokens, bool f16) {
   using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -900,12 +988,15 @@ CUtensorMap make_codes8_map(const uint8_t* codes8, int64_t num_tokens) {
       encode = reinterpret_cast<EncodeFn>(fn);
     }
   }
+  // int8 copy: {128 bytes, N rows}, box {128, 128}; f16 copy: {128 values, N rows} (256-byte rows), box
+  // {64, 128} = one 128-byte K half.  128-byte swizzle (the UMMA layout), zero fill.
   CUtensorMap m{};
   const cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(num_tokens)};
-  const cuuint64_t strides[1] = {128};
-  const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(tc::kTileN)};
+  const cuuint64_t strides[1] = {f16 ? 256u : 128u};
+  const cuuint32_t box[2] = {f16 ? 64u : 128u, static_cast<cuuint32_t>(tc::kTileN)};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(codes8), dims, strides, box, estr,
+  const CUresult r = encode(&m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                            const_cast<void*>(base), dims, strides, box, estr,
                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw CudaFailure("cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
@@ -1007,18 +1098,22 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   prm.out = out;
   prm.error = err;
   const int grid = std::min<int>(sms, prm.num_units);
-  const bool pre = d.codes8 != nullptr;
-  const CUtensorMap tmap = pre ? make_codes8_map(d.codes8, d.num_tokens) : CUtensorMap{};
+  const bool f16 = d.codes16 != nullptr && d.token_scale != nullptr;
+  const bool pre = f16 || d.codes8 != nullptr;
+  const CUtensorMap tmap = f16   ? make_operand_map(d.codes16, d.num_tokens, true)
+                           : pre ? make_operand_map(d.codes8, d.num_tokens, false)
+                                 : CUtensorMap{};
   auto go = [&](auto kernel, int smem_bytes) {
     check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes), "set tc smem");
     kernel<<<grid, tc::kThreads, smem_bytes, stream>>>(prm, tmap);
   };
   if (d.token_scale) {
-    if (pre) go(tc::tc_scan_kernel<true, true>, tc::Layout<true>::bytes);
-    else go(tc::tc_scan_kernel<true, false>, tc::Layout<false>::bytes);
+    if (f16) go(tc::tc_scan_kernel<true, true, true>, tc::Layout<true, true>::bytes);
+    else if (pre) go(tc::tc_scan_kernel<true, true, false>, tc::Layout<true>::bytes);
+    else go(tc::tc_scan_kernel<true, false, false>, tc::Layout<false>::bytes);
   } else {
-    if (pre) go(tc::tc_scan_kernel<false, true>, tc::Layout<true>::bytes);
-    else go(tc::tc_scan_kernel<false, false>, tc::Layout<false>::bytes);
+    if (pre) go(tc::tc_scan_kernel<false, true, false>, tc::Layout<true>::bytes);
+    else go(tc::tc_scan_kernel<false, false, false>, tc::Layout<false>::bytes);
   }
   count_launch();
   check(cudaGetLastError(), "launch tensor-core scan kernel");

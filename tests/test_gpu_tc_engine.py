@@ -52,17 +52,20 @@ def _run(engine, fn):
         _lib.set_engine(prev)
 
 
-@pytest.fixture(params=[1, 0], ids=["int8_copy", "expanding"], autouse=True)
+@pytest.fixture(autouse=True, params=[(1, 1), (0, 1), (0, 0)], ids=["f16-copy", "int8-copy", "expand"])
 def tc_operands(request):
-    """Run every test with both tensor-core producers: operand tiles streamed by TMA from the resident
-    int8 copy of the corpus, and raw int4 rows expanded in shared memory per tile.  Handles built in
-    a test start with the setting of that test."""
+    """Run every test with each tensor-core operand path: f16 tiles streamed by TMA from the resident f16
+    copy of the corpus (per-token scales only; fp32 accumulators), int8 tiles from the resident int8
+    copy, and raw int4 rows expanded in shared memory per tile.  Handles built in a test start with
+    the setting of that test."""
     from maxsim_b200 import _lib
 
-    prev = _lib.get_option("tc_int8_cache")
-    _lib.set_option("tc_int8_cache", request.param)
+    prev = (_lib.get_option("tc_f16_cache"), _lib.get_option("tc_int8_cache"))
+    _lib.set_option("tc_f16_cache", request.param[0])
+    _lib.set_option("tc_int8_cache", request.param[1])
     yield request.param
-    _lib.set_option("tc_int8_cache", prev)
+    _lib.set_option("tc_f16_cache", prev[0])
+    _lib.set_option("tc_int8_cache", prev[1])
 
 
 @pytest.mark.parametrize("gran", ["token", "tensor"])
