@@ -749,10 +749,43 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             continue;
           }
           int a = c0;
+          bool carry = false;        // the document opened inside this chunk already holds [e, c1)
+          float carry_max[4];
           while (true) {
             const int e = nseg == 0 ? 0x7FFF : (sgi < nseg ? meta->seg_end[sgi] : 0x7FFF);
             const int bnd = min(e, c1);
-            if (bnd > a && tile_live) {
+            const bool split = kTokenScale && tile_live && a == c0 && c1 == c0 + 64 && e > c0 && e < c1 &&
+                               (sgi + 1 < nseg ? meta->seg_end[sgi + 1] : 0x7FFF) > c1;
+            if (split) {
+              // Exactly one document ends strictly inside the chunk: one pass sends each value to the
+              // closing document (columns < e) or to the one that opens (columns >= e), each side
+              // reduced by three-input maxima.
+              const int le = e - c0 - 2 * tc;  // element (j, b) is column c0 + 8j + 2(t % 4) + b
+              float lo[4][2], hi[4][2];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                lo[i][0] = lo[i][1] = hi[i][0] = hi[i][1] = kLowest;
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const bool in0 = 8 * j < le, in1 = 8 * j + 1 < le;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const uint32_t* X = i < 2 ? ra : rb;
+                  const float v0 = __uint_as_float(X[4 * j + 2 * (i & 1)]);
+                  const float v1 = __uint_as_float(X[4 * j + 2 * (i & 1) + 1]);
+                  lo[i][j & 1] = fmax3(lo[i][j & 1], in0 ? v0 : kLowest, in1 ? v1 : kLowest);
+                  hi[i][j & 1] = fmax3(hi[i][j & 1], in0 ? kLowest : v0, in1 ? kLowest : v1);
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                run[i] = fmax3(run[i], lo[i][0], lo[i][1]);
+                carry_max[i] = fmaxf(hi[i][0], hi[i][1]);
+              }
+              carry = true;
+              a = e;
+            } else if (bnd > a && tile_live) {
               if (a == c0 && bnd == c0 + 64) {
                 // whole chunk inside one document: two independent chains per row
                 if (kTokenScale) {
@@ -789,7 +822,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 }
               }
             }
-            if (bnd > a) a = bnd;
+            if (!split && bnd > a) a = bnd;
             if (e > c1) break;  // the open document continues past this chunk (or no ends are left)
             // document meta->seg_doc[sgi] ends: complete each row's maximum across the four threads
             // holding it, stage the row value scaled by the query scale, flush finished documents.
@@ -814,8 +847,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             if (etid == 0) group_doc[pending] = meta->seg_doc[sgi];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              run[i] = kLowest;
+              run[i] = carry ? carry_max[i] : kLowest;
               run_i[i] = INT32_MIN;
+            }
+            if (carry) {
+              carry = false;
+              a = c1;
             }
             ++sgi;
             if (++pending == kSegGroup || (sgi == nseg && last_tile)) {
@@ -825,8 +862,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 const int gq = qx < nq0 ? 0 : 1;
                 const int qq = qx < nq0 ? qx : qx - nq0;
                 const float* rv = rowval + (gd * kG + gq) * 128 + qq * Q;
+                // row order as the reference sums; the loads are issued ahead of the dependent additions
                 float sacc = 0.0F;
-                for (int k = 0; k < Q; ++k) sacc = __fadd_rn(sacc, rv[k]);
+                int k = 0;
+                for (; k + 8 <= Q; k += 8) {
+                  float v[8];
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) v[i] = rv[k + i];
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) sacc = __fadd_rn(sacc, v[i]);
+                }
+                for (; k < Q; ++k) sacc = __fadd_rn(sacc, rv[k]);
                 p.out[static_cast<int64_t>((unit.qpair * kG + gq) * p.qpt + qq) * p.num_docs + group_doc[gd]] =
                     __fmul_rn(sacc, p.scale);
               }
