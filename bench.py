@@ -58,6 +58,113 @@ WORKLOAD = ("C4: 100,000 pages x 1,030 tokens (dim 128) per-token int4 (6.59 GB 
             "1,024 queries x 24 tokens int8, batch 64, full-scan top-10")
 
 
+# RTX 4090 medians the reference publishes for these shapes (its README and raw benchmark files), for
+# context only: other hardware, and the reference times some of them per query through its SDK.
+REF_4090_MS = {
+    ("C0", "int4 per-token full scan, fp32 query"): 8.345, ("C0", "int4 per-token full scan, int8 query"): 2.674,
+    ("C0", "int4 per-token top-10, fp32 query"): 8.385, ("C0", "int4 per-token top-10, int8 query"): 2.722,
+    ("C0", "int4 tensor-scale top-10, fp32 query"): 8.158, ("C0", "int4 tensor-scale top-10, int8 query"): 2.492,
+    ("C0", "int4 residual fused full scan"): 16.114, ("C0", "int4 residual candidates, M=512"): 2.803,
+    ("C0", "int4 per-token candidates fp32, M=512"): 1.503,
+    ("C3", "int4-prefix cascade top-10, M=512"): 15.873, ("C3", "int4-prefix cascade top-10, M=2048"): 23.746,
+    ("C1", "SDK search, tensor int4 + int8 query, 256 queries one by one"): 1119.6,
+    ("C2", "SDK search, binary (max_speed), 256 queries one by one"): 680.0,
+    ("C2", "SDK search, binary + fp16 token scale (balanced), 256 queries one by one"): 700.0,
+}
+
+
+def _clustered(rng, num_docs, lo, hi, dim=DIM):
+    lengths = rng.integers(lo, hi + 1, size=num_docs)
+    offsets = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    cent = rng.standard_normal((num_docs, dim), dtype=np.float32)
+    cent /= np.linalg.norm(cent, axis=1, keepdims=True)
+    docs = np.repeat(cent, lengths, axis=0)
+    docs += NOISE * rng.standard_normal(docs.shape, dtype=np.float32)
+    docs /= np.linalg.norm(docs, axis=1, keepdims=True)
+    return docs, offsets, cent
+
+
+def _queries(rng, cent, batch, qtok, dim=DIM):
+    targets = rng.integers(0, cent.shape[0], size=batch)
+    q = np.repeat(cent[targets][:, None, :], qtok, axis=1)
+    q = q + NOISE * rng.standard_normal(q.shape, dtype=np.float32)
+    return (q / np.linalg.norm(q, axis=2, keepdims=True)).astype(np.float32)
+
+
+def configs_bench(args):
+    """C0-C3 shapes of the reference's benchmarks (seeded synthetic data with their sizes and distributions),
+    timed like the reference's harness: 5 warm-up calls, then 20 timed synchronous calls with host inputs
+    and outputs; median and p95 in ms."""
+    from maxsim_b200 import _api, cascade as casc, experimental as ex
+    from maxsim_b200.sdk import Index, Reranker
+
+    def timed(fn, reps=20, warm=5):
+        for _ in range(warm):
+            fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(1e3 * (time.perf_counter() - t0))
+        ts.sort()
+        return ts[len(ts) // 2], ts[int(0.95 * (len(ts) - 1))]
+
+    def emit(cfg, op, p50, p95, note=""):
+        ref = REF_4090_MS.get((cfg, op))
+        print(json.dumps({"configs": cfg, "op": op, "p50_ms": round(p50, 4), "p95_ms": round(p95, 4),
+                          "reference_rtx4090_p50_ms": ref, "speedup_vs_rtx4090": None if ref is None else round(ref / p50, 2),
+                          "note": note}), flush=True)
+
+    rng = np.random.default_rng(SEED ^ 0x51A7)
+    # C0 / C3: 4,096 docs of U[64, 192] tokens, query [4, 32, 128] from 4 target docs
+    docs, off, cent = _clustered(rng, 4096, 64, 192)
+    q = _queries(rng, cent, 4, 32)
+    tok = ex.int4_to_device(ex.pack_int4_symmetric(docs, off, scale_granularity="token")).data
+    ten = ex.int4_to_device(ex.pack_int4_symmetric(docs, off, scale_granularity="tensor")).data
+    emit("C0", "int4 per-token full scan, fp32 query", *timed(lambda: tok.maxsim_batch(q)))
+    emit("C0", "int4 per-token full scan, int8 query", *timed(lambda: tok.maxsim_batch_int8q(q)))
+    emit("C0", "int4 per-token top-10, fp32 query", *timed(lambda: tok.topk_batch(q, 10)))
+    emit("C0", "int4 per-token top-10, int8 query", *timed(lambda: tok.topk_batch_int8q(q, 10)))
+    emit("C0", "int4 tensor-scale top-10, fp32 query", *timed(lambda: ten.topk_batch(q, 10)))
+    emit("C0", "int4 tensor-scale top-10, int8 query", *timed(lambda: ten.topk_batch_int8q(q, 10)))
+    cand = np.sort(rng.choice(4096, size=512, replace=False)).astype(np.int64)
+    emit("C0", "int4 per-token candidates fp32, M=512", *timed(lambda: tok.score_candidates_batch(q, cand)))
+    res = casc.residual_int4_to_device(casc.pack_residual_int4(docs, off)).prefix_data
+    emit("C0", "int4 residual fused full scan", *timed(lambda: res.score_residual_batch(q)))
+    emit("C0", "int4 residual candidates, M=512", *timed(lambda: res.score_residual_candidates_batch(q, cand)))
+    for m in (512, 1024, 2048):
+        emit("C3", f"int4-prefix cascade top-10, M={m}", *timed(lambda m=m: res.cascade_topk_batch(q, 10, m)))
+    bres = casc.binary_residual_to_device(casc.pack_binary_residual_int4(docs, off))
+    for m in (512, 1024, 2048):
+        emit("C3", f"binary-prefix cascade top-10, M={m}",
+             *timed(lambda m=m: casc.binary_cascade_topk(q, bres, 10, candidates=m, device="cuda")),
+             note="binary sign prefix + per-token int4 residual (no reference counterpart)")
+    del docs, tok, ten, res, bres
+    # C1 / C2: 10,171 docs of U[400, 800] tokens, 256 queries x 20 tokens
+    docs, off, cent = _clustered(rng, 10171, 400, 800)
+    q256 = _queries(rng, cent, 256, 20)
+    ids = [f"d{i}" for i in range(10171)]
+    rr = Reranker(Index.from_embeddings(ids, docs, off, mode="int4"), device="cuda", int4_query="int8")
+    emit("C1", "SDK search, tensor int4 + int8 query, 256 queries one by one",
+         *timed(lambda: [rr.search(q256[i], k=10) for i in range(256)], reps=3, warm=1))
+    h1 = rr.corpus.int4_packed.data
+    emit("C1", "tensor int4 top-10, int8 query, 8 batches of 32",
+         *timed(lambda: [h1.topk_batch_int8q(q256[i:i + 32], 10) for i in range(0, 256, 32)], reps=5, warm=2))
+    del rr, h1
+    for mode, label in (("binary", "binary (max_speed)"), ("binary_token_scale", "binary + fp16 token scale (balanced)")):
+        rb = Reranker(Index.from_embeddings(ids, docs, off, mode=mode), device="cuda")
+        emit("C2", f"SDK search, {label}, 256 queries one by one",
+             *timed(lambda: [rb.search(q256[i], k=10) for i in range(256)], reps=3, warm=1))
+        hb = rb.corpus.packed.data
+        w = rng.uniform(0.5, 1.5, size=20).astype(np.float32)
+        use_ts = mode == "binary_token_scale"
+        for red, kw in (("maxsim", {}), ("weighted_maxsim", {"query_weights": w}), ("topk2", {}), ("topk4", {}),
+                        ("smoothsim", {"temperature": 0.1})):
+            emit("C2", f"{label} full scan, reducer {red}, 256 queries in one batch",
+                 *timed(lambda red=red, kw=kw: hb.score_batch(q256, reducer=red, use_token_scale=use_ts, **kw), reps=5, warm=2))
+        del rb, hb
+
+
 def batch_sweep(args, torch, _lib, handle, queries, device):
     """One line per batch size: scan + top-k of the whole resident corpus, CUDA events on the launching
     stream, against both roofs (algorithmic HBM bytes and int8 tensor ops of that batch)."""
@@ -266,6 +373,9 @@ def main() -> None:
     ap.add_argument("--engine", type=int, default=0, help="0 auto, 1 SIMT, 2 tensor core")
     ap.add_argument("--pages", type=int, default=NUM_PAGES,
                     help="corpus pages (default: the C4 workload; smaller values are for profiling captures)")
+    ap.add_argument("--configs", action="store_true",
+                    help="time the reference's smaller benchmark shapes (C0-C3) through the handle and SDK calls "
+                         "the reference's own benchmarks time, one JSON line per operation, instead of the bench line")
     ap.add_argument("--batch-sweep", default=None,
                     help="comma-separated batch sizes: time the scan + top-k per batch size on the resident corpus "
                          "and print one roofline line per size instead of the bench line (HBM/tensor crossover)")
@@ -287,6 +397,12 @@ def main() -> None:
     from maxsim_b200 import _lib
     from maxsim_b200 import _maxsim_cuda as mc
     from maxsim_b200.sharded import ShardedReranker, ShardInfo, shard_bounds
+
+    if args.configs:
+        if rank == 0:
+            torch.cuda.set_device(local_rank)
+            configs_bench(args)
+        return
 
     _lib.set_engine(args.engine)
     torch.cuda.set_device(local_rank)
