@@ -292,6 +292,122 @@ __global__ void __launch_bounds__(128) simt_scan_kernel(DocsView docs, QueryView
   }
 }
 
+// ---------------------------------------------------------------------------
+// Binary codes x fp32 queries at dim 128: nibble tables.  The sign dot of one query row with one token is
+// sum over the 32 nibbles p of L[p][n_p], where L[p][v] = sum_{j<4} (bit j of v ? +q : -q)[4p + j] and n_p
+// is the token's nibble p (dims 4p..4p+3: bits of byte (4p)/8, LSB first).  A block builds the tables of
+// its query's rows once in shared memory (2 KB per row) and scans kLutDocs documents with them: 32
+// conflict-free table reads and adds per (row, token) instead of 128 loads, selects and adds.  Each
+// thread loads a token's 16 code bytes once per group of kLutRows query rows.  The per-row sum order is
+// nibble-wise (the reference adds dims in order), within the fp32 paths' tolerance.
+// ---------------------------------------------------------------------------
+constexpr int kLutDocs = 16;
+constexpr int kLutRows = 8;
+constexpr int kLutMaxQ = 48;
+
+template <int R>
+__global__ void __launch_bounds__(128) bin_lut_scan_kernel(DocsView docs, QueryView qv, ReduceView red,
+                                                           TargetsView tg, float* __restrict__ out) {
+  using P = Red<R>;
+  using S = typename P::S;
+  extern __shared__ __align__(16) float lut_smem[];
+  const int Q = qv.qtok;
+  float* lut = lut_smem;                  // [Q][32][16]
+  float* row_value = lut + Q * 512;       // [Q]
+  S* part = reinterpret_cast<S*>(row_value + ((Q + 3) & ~3));  // [4 warps][kLutRows]
+  const int b = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t T = tg.ids ? tg.count : docs.num_docs;
+  for (int e = threadIdx.x; e < Q * 512; e += blockDim.x) {
+    const int r = e >> 9, pos = (e >> 4) & 31, v = e & 15;
+    const float* qr = qv.f32 + (static_cast<int64_t>(b) * Q + r) * 128 + 4 * pos;
+    float acc = 0.0F;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc += ((v >> j) & 1) ? qr[j] : -qr[j];
+    lut[e] = acc;
+  }
+  __syncthreads();
+  const int64_t j_end = min(T, static_cast<int64_t>(blockIdx.x + 1) * kLutDocs);
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * kLutDocs; j < j_end; ++j) {
+    const int64_t d = tg.ids ? (tg.per_row ? tg.ids[static_cast<int64_t>(b) * T + j] : tg.ids[j]) : j;
+    const int64_t start = docs.offsets[d];
+    const int64_t end = docs.offsets[d + 1];
+    const float doc_scale = docs.doc_scale ? docs.doc_scale[d] : docs.scale;
+    for (int r0 = 0; r0 < Q; r0 += kLutRows) {
+      S st[kLutRows];
+#pragma unroll
+      for (int g = 0; g < kLutRows; ++g) st[g] = P::init();
+      for (int64_t t = start + threadIdx.x; t < end; t += blockDim.x) {
+        const uint4 c = __ldg(reinterpret_cast<const uint4*>(docs.codes + t * 16));
+        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+        const float ts = docs.token_scale ? docs.token_scale[t] : 1.0F;
+#pragma unroll
+        for (int g = 0; g < kLutRows; ++g) {
+          if (r0 + g < Q) {
+            const float* L = lut + (r0 + g) * 512;
+            float s0 = 0.0F, s1 = 0.0F;
+#pragma unroll
+            for (int pos = 0; pos < 32; pos += 2) {
+              s0 += L[16 * pos + ((w[pos >> 3] >> (4 * (pos & 7))) & 15u)];
+              s1 += L[16 * (pos + 1) + ((w[pos >> 3] >> (4 * ((pos + 1) & 7))) & 15u)];
+            }
+            float sim = s0 + s1;
+            if (docs.token_scale) sim *= ts;
+            if (P::kScaleFirst) sim *= doc_scale;
+            P::add(st[g], sim, red.temperature);
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < kLutRows; ++g) {
+#pragma unroll
+        for (int delta = 16; delta > 0; delta >>= 1) {
+          const S other = P::shfl(st[g], delta);
+          if (lane < delta) st[g] = P::merge(st[g], other, red.temperature);
+        }
+        if (lane == 0) part[warp * kLutRows + g] = st[g];
+      }
+      __syncthreads();
+      if (threadIdx.x < kLutRows && r0 + threadIdx.x < Q) {
+        const int r = r0 + threadIdx.x;
+        S acc = part[threadIdx.x];
+        for (int w2 = 1; w2 < 4; ++w2) acc = P::merge(acc, part[w2 * kLutRows + threadIdx.x], red.temperature);
+        float wt = 1.0F;
+        if (R == kWeighted) wt = red.weights[(red.weights_batched ? static_cast<int64_t>(b) * Q : 0) + r];
+        row_value[r] = P::finish(acc, wt, red.temperature);
+      }
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+      float acc = 0.0F;
+      for (int r = 0; r < Q; ++r) acc += row_value[r];
+      if (!P::kScaleFirst) acc *= doc_scale;
+      out[static_cast<int64_t>(b) * T + j] = acc;
+    }
+    __syncthreads();
+  }
+}
+
+template <int R>
+static void launch_bin_lut(const DocsView& docs, const QueryView& qv, const ReduceView& red, const TargetsView& tg,
+                           float* out, cudaStream_t stream) {
+  const int64_t T = tg.ids ? tg.count : docs.num_docs;
+  const int64_t gx = (T + kLutDocs - 1) / kLutDocs;
+  if (gx == 0 || qv.batch == 0) return;
+  const int Q = qv.qtok;
+  const size_t smem = sizeof(float) * (static_cast<size_t>(Q) * 512 + ((Q + 3) & ~3)) +
+                      sizeof(typename Red<R>::S) * 4 * kLutRows;
+  // a per-device function attribute: set on every launch (cheap), so every device a process uses has it
+  check(cudaFuncSetAttribute(bin_lut_scan_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)),
+        "set binary table scan shared memory");
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(qv.batch));
+  bin_lut_scan_kernel<R><<<grid, 128, smem, stream>>>(docs, qv, red, tg, out);
+  count_launch();
+  check(cudaGetLastError(), "launch binary table scan kernel");
+}
+
 template <int Kind, int Mode>
 static void launch_kind_mode(const DocsView& docs, const QueryView& qv, const ReduceView& red, const TargetsView& tg,
                              float* out, cudaStream_t stream) {
@@ -327,6 +443,15 @@ void launch_simt_scan(const DocsView& docs, const QueryView& qv, const ReduceVie
   if (docs.format == kFormatInt4) {
     if (qv.mode == kQueryI8) launch_kind_mode<kKindInt4, kQueryI8>(docs, qv, red, tg, out, stream);
     else launch_kind_mode<kKindInt4, kQueryF32>(docs, qv, red, tg, out, stream);
+  } else if (qv.mode == kQueryF32 && docs.dim == 128 && qv.qtok >= 1 && qv.qtok <= kLutMaxQ && qv.batch <= 65535) {
+    switch (red.reducer) {
+      case kMaxSim: launch_bin_lut<kMaxSim>(docs, qv, red, tg, out, stream); break;
+      case kWeighted: launch_bin_lut<kWeighted>(docs, qv, red, tg, out, stream); break;
+      case kTopK2: launch_bin_lut<kTopK2>(docs, qv, red, tg, out, stream); break;
+      case kTopK4: launch_bin_lut<kTopK4>(docs, qv, red, tg, out, stream); break;
+      case kSmooth: launch_bin_lut<kSmooth>(docs, qv, red, tg, out, stream); break;
+      default: throw InvalidArgument("unknown reducer");
+    }
   } else {
     if (qv.mode == kQueryI8) launch_kind_mode<kKindBinary, kQueryI8>(docs, qv, red, tg, out, stream);
     else launch_kind_mode<kKindBinary, kQueryF32>(docs, qv, red, tg, out, stream);
