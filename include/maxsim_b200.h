@@ -21,7 +21,8 @@
  *     caller keeps nothing alive.  A handle's scratch buffers grow
  *     monotonically and are reused across calls (reference :2350-2360), so a
  *     handle must not be used by two threads at once.
- *   - `*_device` entry points take device pointers and enqueue work on
+ *   - `*_device` entry points take device pointers (the query, outputs,
+ *     candidates and the pointers in msb_score_opts) and enqueue work on
  *     `stream` (a cudaStream_t; NULL is the legacy default stream) without
  *     synchronising.  The other entry points take host pointers and return
  *     after the results are in host memory, like the reference methods.

@@ -112,14 +112,17 @@ def _opts(reducer=0, query_mode=0, weights=None, weight_rows=1, temperature=1.0,
     o = _lib.ScoreOpts()
     o.reducer = reducer
     o.query_mode = query_mode
-    o.weights = None if weights is None else weights.ctypes.data
+    # host arrays for the synchronous calls; torch CUDA tensors for the *_device calls
+    o.weights = None if weights is None else (weights.data_ptr() if hasattr(weights, "data_ptr")
+                                              else weights.ctypes.data)
     o.weight_rows = weight_rows
     o.temperature = temperature
     o.use_residual = int(bool(use_residual))
     o.use_token_scale = int(bool(use_token_scale))
     o.use_doc_scale = int(bool(use_doc_scale))
     o.scale = float(scale)
-    o.doc_scale_override = None if override is None else override.ctypes.data
+    o.doc_scale_override = None if override is None else (override.data_ptr() if hasattr(override, "data_ptr")
+                                                          else override.ctypes.data)
     return o
 
 

@@ -360,6 +360,27 @@ void check_query(msb_docs* h, const void* q, int batch, int qtok) {
   if (h && h->upload_open) throw InvalidArgument("the corpus upload has not finished (msb_docs_upload_finish)");
 }
 
+// The *_device entry points dereference their pointers in kernels: a pageable host pointer handed to
+// one would fault the GPU, so it is refused here, before anything is enqueued.  Device, managed and
+// pinned (mapped, unified-address) host memory are accessible from the device.
+void require_device_accessible(const void* p, const char* what) {
+  if (!p) return;
+  cudaPointerAttributes attr{};
+  const cudaError_t e = cudaPointerGetAttributes(&attr, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // clear the non-sticky error
+    throw InvalidArgument(std::string(what) + " is not a CUDA pointer");
+  }
+  if (attr.type == cudaMemoryTypeUnregistered)
+    throw InvalidArgument(std::string(what) + " must be device memory on a *_device call (got a host pointer)");
+}
+
+void require_device_opts(const msb_score_opts* o) {
+  if (!o) return;
+  if (o->reducer == kWeighted) require_device_accessible(o->weights, "opts.weights");
+  require_device_accessible(o->doc_scale_override, "opts.doc_scale_override");
+}
+
 void check_candidates(msb_docs* h, const int64_t* c, int64_t m) {
   for (int64_t i = 0; i < m; ++i)
     if (c[i] < 0 || c[i] >= h->num_docs)
@@ -930,6 +951,10 @@ int msb_docs_score_device(msb_docs* h, const float* query, int32_t batch, int32_
     if (!h) throw InvalidArgument("handle is NULL");
     check_query(h, query, batch, qtok);
     DeviceGuard g(h->device);
+    if (static_cast<int64_t>(batch) * qtok > 0) require_device_accessible(query, "query");
+    require_device_accessible(candidates, "candidates");
+    require_device_accessible(out, "out");
+    require_device_opts(opts);
     cudaStream_t s = pick_stream(h, stream);
     Resolved r = resolve(h, opts, batch, qtok, opts ? opts->weights : nullptr, opts ? opts->doc_scale_override : nullptr);
     TargetsView tg{};
@@ -948,6 +973,10 @@ int msb_docs_topk_device(msb_docs* h, const float* query, int32_t batch, int32_t
     if (k < 1 || k > h->num_docs) throw InvalidArgument("k must be between 1 and num_docs");
     check_query(h, query, batch, qtok);
     DeviceGuard g(h->device);
+    if (static_cast<int64_t>(batch) * qtok > 0) require_device_accessible(query, "query");
+    require_device_accessible(out_scores, "out_scores");
+    require_device_accessible(out_ids, "out_ids");
+    require_device_opts(opts);
     cudaStream_t s = pick_stream(h, stream);
     Resolved r = resolve(h, opts, batch, qtok, opts ? opts->weights : nullptr, opts ? opts->doc_scale_override : nullptr);
     if (batch == 0) return;
@@ -1048,6 +1077,15 @@ extern "C" int msb_docs_topk_device_noalloc(msb_docs* h, const float* query, int
     check_query(h, query, batch, qtok);
     DeviceGuard g(h->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // (the pointer checks are host queries, made when the stream is not being captured into a graph)
+    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+    check(cudaStreamIsCapturing(s, &capturing), "query stream capture status");
+    if (capturing == cudaStreamCaptureStatusNone) {
+      if (static_cast<int64_t>(batch) * qtok > 0) require_device_accessible(query, "query");
+      require_device_accessible(out_scores, "out_scores");
+      require_device_accessible(out_ids, "out_ids");
+      require_device_opts(opts);
+    }
     Resolved r = resolve(h, opts, batch, qtok, opts ? opts->weights : nullptr, opts ? opts->doc_scale_override : nullptr);
     if (batch == 0) return;
     // Scratch layout: scores [batch, num_docs] fp32, then (int8 queries) codes,

@@ -408,6 +408,144 @@ static void launch_bin_lut(const DocsView& docs, const QueryView& qv, const Redu
   check(cudaGetLastError(), "launch binary table scan kernel");
 }
 
+// ---------------------------------------------------------------------------
+// int4 codes (and the int4 residual stream) x fp32 queries at dim 128: register-blocked rows.
+// One warp per (target, query): its lanes stride the document's tokens, RG query rows at a time.  A
+// lane converts the 8 nibbles of a code word to floats once (exactly: the bits 0x4B000000 | (nibble ^ 8)
+// are the float 2^23 + value + 8) and feeds them to the RG rows' FMA chains, the group's query values
+// staged in shared memory and read as broadcasts.  Each row's chain runs over the dims in order like
+// dot_int4_f32, so the values are bit-identical to the general kernel's.  The warp merges its lanes with
+// shuffles and lane 0 adds the row values in row order.  Single-warp blocks (tens of thousands for a
+// full scan) let the block scheduler balance documents of different lengths across the SMs.
+// ---------------------------------------------------------------------------
+template <int R, bool kRes, int RG>
+__global__ void __launch_bounds__(32) int4_rows_scan_kernel(DocsView docs, QueryView qv, ReduceView red,
+                                                            TargetsView tg, float* __restrict__ out) {
+  using P = Red<R>;
+  using S = typename P::S;
+  __shared__ __align__(16) float qs[RG * 128];
+  const int Q = qv.qtok;
+  const int lane = threadIdx.x;
+  const int b = blockIdx.y;
+  const int64_t j = blockIdx.x;
+  const int64_t T = tg.ids ? tg.count : docs.num_docs;
+  const int64_t d = tg.ids ? (tg.per_row ? tg.ids[static_cast<int64_t>(b) * T + j] : tg.ids[j]) : j;
+  const int64_t start = docs.offsets[d];
+  const int64_t end = docs.offsets[d + 1];
+  const float4* qsrc = reinterpret_cast<const float4*>(qv.f32 + static_cast<int64_t>(b) * Q * 128);
+  float total = 0.0F;
+  for (int r0 = 0; r0 < Q; r0 += RG) {
+    __syncwarp();  // the previous group's readers are done
+#pragma unroll
+    for (int e = lane; e < RG * 32; e += 32) {
+      const int r = r0 + (e >> 5);
+      reinterpret_cast<float4*>(qs)[e] = r < Q ? __ldg(qsrc + static_cast<int64_t>(r0) * 32 + e) : make_float4(0, 0, 0, 0);
+    }
+    __syncwarp();
+    S st[RG];
+#pragma unroll
+    for (int g = 0; g < RG; ++g) st[g] = P::init();
+    for (int64_t t = start + lane; t < end; t += 32) {
+      float dot[2][RG];
+#pragma unroll
+      for (int pass = 0; pass < (kRes ? 2 : 1); ++pass) {
+        const uint4* src = reinterpret_cast<const uint4*>((pass == 0 ? docs.codes : docs.codes2) + t * 64);
+        float acc[RG];
+#pragma unroll
+        for (int g = 0; g < RG; ++g) acc[g] = 0.0F;
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4) {
+          const uint4 cv = __ldg(src + v4);
+          const uint32_t wv[4] = {cv.x ^ 0x88888888u, cv.y ^ 0x88888888u, cv.z ^ 0x88888888u, cv.w ^ 0x88888888u};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int word = 4 * v4 + k;  // dims 8 word .. 8 word + 7; nibble n is dim 8 word + n
+            float val[8];
+#pragma unroll
+            for (int n = 0; n < 8; ++n)
+              val[n] = __int_as_float(static_cast<int>(((wv[k] >> (4 * n)) & 15u) | 0x4B000000u)) - 8388616.0F;
+#pragma unroll
+            for (int g = 0; g < RG; ++g) {
+              const float4 qa = *reinterpret_cast<const float4*>(qs + g * 128 + 8 * word);
+              const float4 qb = *reinterpret_cast<const float4*>(qs + g * 128 + 8 * word + 4);
+              acc[g] = fmaf(val[0], qa.x, acc[g]);
+              acc[g] = fmaf(val[1], qa.y, acc[g]);
+              acc[g] = fmaf(val[2], qa.z, acc[g]);
+              acc[g] = fmaf(val[3], qa.w, acc[g]);
+              acc[g] = fmaf(val[4], qb.x, acc[g]);
+              acc[g] = fmaf(val[5], qb.y, acc[g]);
+              acc[g] = fmaf(val[6], qb.z, acc[g]);
+              acc[g] = fmaf(val[7], qb.w, acc[g]);
+            }
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < RG; ++g) dot[pass][g] = acc[g];
+      }
+      const float ts = docs.token_scale ? docs.token_scale[t] : 1.0F;
+      const float ts2 = kRes ? docs.token_scale2[t] : 0.0F;
+#pragma unroll
+      for (int g = 0; g < RG; ++g) {
+        float sim;
+        if (kRes) {
+          sim = dot[0][g] * docs.scale * ts + dot[1][g] * docs.scale2 * ts2;
+        } else {
+          sim = dot[0][g];
+          if (docs.token_scale) sim *= ts;
+          if (P::kScaleFirst) sim *= docs.scale;
+        }
+        P::add(st[g], sim, red.temperature);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < RG; ++g) {
+#pragma unroll
+      for (int delta = 16; delta > 0; delta >>= 1) {
+        const S other = P::shfl(st[g], delta);
+        if (lane < delta) st[g] = P::merge(st[g], other, red.temperature);
+      }
+      const int r = r0 + g;
+      if (r < Q) {
+        float wt = 1.0F;
+        if (R == kWeighted) wt = red.weights[(red.weights_batched ? static_cast<int64_t>(b) * Q : 0) + r];
+        total += P::finish(st[g], wt, red.temperature);  // lane 0's value is the row's; rows in order
+      }
+    }
+  }
+  if (lane == 0) {
+    if (!kRes && !P::kScaleFirst) total *= docs.scale;
+    out[static_cast<int64_t>(b) * T + j] = total;
+  }
+}
+
+template <int R, bool kRes>
+static void launch_int4_lut(const DocsView& docs, const QueryView& qv, const ReduceView& red, const TargetsView& tg,
+                            float* out, cudaStream_t stream) {
+  // 16-row groups where the reducer state is one value and one stream is read; 8 for the top-k and smooth
+  // states and for the two residual streams (whose 16-row form does not fit in registers)
+  constexpr int RG = (!kRes && (R == kMaxSim || R == kWeighted)) ? 16 : 8;
+  const int64_t T = tg.ids ? tg.count : docs.num_docs;
+  if (T == 0 || qv.batch == 0) return;
+  if (T > 0x7FFFFFFFLL) throw InvalidArgument("too many targets for one scan");
+  dim3 grid(static_cast<unsigned>(T), static_cast<unsigned>(qv.batch));
+  int4_rows_scan_kernel<R, kRes, RG><<<grid, 32, 0, stream>>>(docs, qv, red, tg, out);
+  count_launch();
+  check(cudaGetLastError(), "launch int4 row-blocked scan kernel");
+}
+
+template <bool kRes>
+static void launch_int4_lut_reducer(const DocsView& docs, const QueryView& qv, const ReduceView& red,
+                                    const TargetsView& tg, float* out, cudaStream_t stream) {
+  switch (red.reducer) {
+    case kMaxSim: launch_int4_lut<kMaxSim, kRes>(docs, qv, red, tg, out, stream); break;
+    case kWeighted: launch_int4_lut<kWeighted, kRes>(docs, qv, red, tg, out, stream); break;
+    case kTopK2: launch_int4_lut<kTopK2, kRes>(docs, qv, red, tg, out, stream); break;
+    case kTopK4: launch_int4_lut<kTopK4, kRes>(docs, qv, red, tg, out, stream); break;
+    case kSmooth: launch_int4_lut<kSmooth, kRes>(docs, qv, red, tg, out, stream); break;
+    default: throw InvalidArgument("unknown reducer");
+  }
+}
+
 template <int Kind, int Mode>
 static void launch_kind_mode(const DocsView& docs, const QueryView& qv, const ReduceView& red, const TargetsView& tg,
                              float* out, cudaStream_t stream) {
@@ -432,9 +570,14 @@ static void launch_kind_mode(const DocsView& docs, const QueryView& qv, const Re
 
 void launch_simt_scan(const DocsView& docs, const QueryView& qv, const ReduceView& red, const TargetsView& tg,
                       bool residual, float* out, cudaStream_t stream) {
+  // (int4 row-blocked scan: dim 128; the query is read as float4, so a caller's device pointer must be
+  // 16-byte aligned; codes are the handle's own allocations)
+  const bool i4_lut = docs.dim == 128 && qv.qtok >= 1 && qv.batch <= 65535 &&
+                      (reinterpret_cast<uintptr_t>(qv.f32) & 15) == 0;
   if (residual) {
     if (qv.mode != kQueryF32) throw InvalidArgument("residual scoring takes fp32 queries");
     if (docs.format == kFormatBinary) launch_kind_mode<kKindResidualBinary, kQueryF32>(docs, qv, red, tg, out, stream);
+    else if (i4_lut) launch_int4_lut_reducer<true>(docs, qv, red, tg, out, stream);
     else launch_kind_mode<kKindResidual, kQueryF32>(docs, qv, red, tg, out, stream);
     return;
   }
@@ -442,6 +585,7 @@ void launch_simt_scan(const DocsView& docs, const QueryView& qv, const ReduceVie
     throw InvalidArgument("int8 queries support reducer='maxsim' only");
   if (docs.format == kFormatInt4) {
     if (qv.mode == kQueryI8) launch_kind_mode<kKindInt4, kQueryI8>(docs, qv, red, tg, out, stream);
+    else if (i4_lut) launch_int4_lut_reducer<false>(docs, qv, red, tg, out, stream);
     else launch_kind_mode<kKindInt4, kQueryF32>(docs, qv, red, tg, out, stream);
   } else if (qv.mode == kQueryF32 && docs.dim == 128 && qv.qtok >= 1 && qv.qtok <= kLutMaxQ && qv.batch <= 65535) {
     switch (red.reducer) {
