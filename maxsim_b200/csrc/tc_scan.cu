@@ -336,10 +336,16 @@ struct Ring {
 // kPre: the int4 codes were expanded once into an int8 copy (same K order); each B stage is a tiled TMA
 // load of 128 rows from it, landing in the 128-byte-swizzled layout, and the expanders only stage the
 // tile metadata.  Otherwise the loader copies raw int4 rows and the expanders build the B stage.
-template <bool kTokenScale, bool kPre, bool kF16>
+// kDigits: fp32 queries as three int8 digit planes (split_query_digits_kernel).  Query row rho of a tile
+// (32 per tile) has its digit k on TMEM lane 32 (rho / 8) + 8 k + rho % 8 (k = 3: zeros), the four lanes
+// one epilogue thread holds, which combines them to d0 + 256 d1 + 65536 d2 before the scale and maximum.
+template <bool kTokenScale, bool kPre, bool kF16, bool kDigits = false>
 __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap) {
   using L = Layout<kPre, kF16>;
   static_assert(!kF16 || (kPre && kTokenScale), "f16 operands come from the resident copy, with token scales");
+  static_assert(!(kF16 && kDigits), "digit-plane queries use int8 operands");
+  constexpr bool kFloat = kTokenScale || kDigits;  // row maxima in fp32; int32 for the tensor-scale dots
+  constexpr int kRows = kDigits ? 1 : 4;            // query rows an epilogue thread holds
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                          ~static_cast<uintptr_t>(1023));
@@ -458,9 +464,23 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
 #pragma unroll
         for (int g = 0; g < kG; ++g) {
           unsigned char* A = smem + L::off_a + (abuf * kG + g) * L::a_tile;
-          const int b = (unit.qpair * kG + g) * p.qpt + row / Q;
-          const bool valid = row < p.qpt * Q && b < p.batch;
-          const int4* src = reinterpret_cast<const int4*>(p.qwords + (static_cast<int64_t>(b) * Q + row % Q) * 32);
+          int b, qrow;
+          bool valid;
+          int64_t src_row;
+          if (kDigits) {
+            const int k = (row >> 3) & 3;                   // digit plane of this lane
+            const int rho = ((row >> 5) << 3) | (row & 7);  // query row of the tile
+            b = (unit.qpair * kG + g) * p.qpt + rho / Q;
+            qrow = rho % Q;
+            valid = k < 3 && rho < p.qpt * Q && b < p.batch;
+            src_row = valid ? static_cast<int64_t>(k) * p.batch * Q + static_cast<int64_t>(b) * Q + qrow : 0;
+          } else {
+            b = (unit.qpair * kG + g) * p.qpt + row / Q;
+            qrow = row % Q;
+            valid = row < p.qpt * Q && b < p.batch;
+            src_row = valid ? static_cast<int64_t>(b) * Q + qrow : 0;
+          }
+          const int4* src = reinterpret_cast<const int4*>(p.qwords + src_row * 32);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             int4 v = valid ? __ldg(src + c) : make_int4(0, 0, 0, 0);
@@ -661,9 +681,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       // Rows of this warp's TMEM lane quarter that hold query tokens; a quarter without any (small
       // batches) skips its loads and arithmetic and only walks the document ends with the others.
       const int tile_rows = max(0, min(p.qpt, p.batch - tile * p.qpt)) * Q;
-      const bool tile_live = q4 * 32 < tile_rows;
-      // the row this thread stores when a document ends: i = t % 4
-      const int wrow = q4 * 32 + 16 * (tc >> 1) + 8 * (tc & 1) + tq;
+      const bool tile_live = (kDigits ? 8 * q4 : 32 * q4) < tile_rows;
+      // the row this thread stores when a document ends: i = t % 4 (digit planes: the one query row of
+      // the four lanes, stored by t % 4 = 0)
+      const int wrow = kDigits ? 8 * q4 + tq : q4 * 32 + 16 * (tc >> 1) + 8 * (tc & 1) + tq;
+      const bool w_store = !kDigits || tc == 0;
       const int wb = tile * p.qpt + wrow / Q;
       const bool w_valid = wrow < p.qpt * Q && wb < p.batch;
       const float qs = w_valid ? __ldg(p.qscale + static_cast<int64_t>(wb) * Q + wrow % Q) : 0.0F;
@@ -712,7 +734,22 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               if (lane == 0) mbar_arrive(&acc_empty[acc.idx]);
               released = true;
             }
-            if (kTokenScale) {
+            if (kDigits) {
+              // rows 0, 1, 2 are the digit planes' exact dots: d0 + 256 d1 is exact in int32 (|d| <= 2^17),
+              // one rounding to float and one fused multiply-add, then fl(dot * s_t); the result in row 0
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+#pragma unroll
+                for (int b2 = 0; b2 < 2; ++b2) {
+                  const int32_t d0 = static_cast<int32_t>(ra[4 * j + b2]);
+                  const int32_t d1 = static_cast<int32_t>(ra[4 * j + 2 + b2]);
+                  const int32_t d2 = static_cast<int32_t>(rb[4 * j + b2]);
+                  float v = __fmaf_rn(__int2float_rn(d2), 65536.0F, __int2float_rn(d0 + 256 * d1));
+                  if (kTokenScale) v = __fmul_rn(v, b2 ? sc[j].y : sc[j].x);
+                  ra[4 * j + b2] = __float_as_uint(v);
+                }
+              }
+            } else if (kTokenScale) {
               // exact int32 dot -> float (all 64 first), then fl(dot * s_t); f16 operands accumulate the
               // same integer exactly in fp32 (|products| <= 1016, |sums| < 2^17), so nothing to convert
               if (!kF16) {
@@ -735,11 +772,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           }
           if (nseg == 0 && tile_live && c1 == c0 + 64) {
             // no document ends in this tile and the open document covers the whole chunk: no walk
-            if (kTokenScale) {
+            if (kFloat) {
               run[0] = row_max16(ra, 0, run[0]);
-              run[1] = row_max16(ra, 1, run[1]);
-              run[2] = row_max16(rb, 0, run[2]);
-              run[3] = row_max16(rb, 1, run[3]);
+              if (!kDigits) {
+                run[1] = row_max16(ra, 1, run[1]);
+                run[2] = row_max16(rb, 0, run[2]);
+                run[3] = row_max16(rb, 1, run[3]);
+              }
             } else {
               run_i[0] = row_max16i(ra, 0, run_i[0]);
               run_i[1] = row_max16i(ra, 1, run_i[1]);
@@ -754,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           while (true) {
             const int e = nseg == 0 ? 0x7FFF : (sgi < nseg ? meta->seg_end[sgi] : 0x7FFF);
             const int bnd = min(e, c1);
-            const bool split = kTokenScale && tile_live && a == c0 && c1 == c0 + 64 && e > c0 && e < c1 &&
+            const bool split = kFloat && tile_live && a == c0 && c1 == c0 + 64 && e > c0 && e < c1 &&
                                (sgi + 1 < nseg ? meta->seg_end[sgi + 1] : 0x7FFF) > c1;
             if (split) {
               // Exactly one document ends strictly inside the chunk: one pass sends each value to the
@@ -770,7 +809,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               for (int j = 0; j < 8; ++j) {
                 const bool in0 = 8 * j < le, in1 = 8 * j + 1 < le;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
+                for (int i = 0; i < kRows; ++i) {
                   const uint32_t* X = i < 2 ? ra : rb;
                   const float v0 = __uint_as_float(X[4 * j + 2 * (i & 1)]);
                   const float v1 = __uint_as_float(X[4 * j + 2 * (i & 1) + 1]);
@@ -788,11 +827,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             } else if (bnd > a && tile_live) {
               if (a == c0 && bnd == c0 + 64) {
                 // whole chunk inside one document: two independent chains per row
-                if (kTokenScale) {
+                if (kFloat) {
                   run[0] = row_max16(ra, 0, run[0]);
-                  run[1] = row_max16(ra, 1, run[1]);
-                  run[2] = row_max16(rb, 0, run[2]);
-                  run[3] = row_max16(rb, 1, run[3]);
+                  if (!kDigits) {
+                    run[1] = row_max16(ra, 1, run[1]);
+                    run[2] = row_max16(rb, 0, run[2]);
+                    run[3] = row_max16(rb, 1, run[3]);
+                  }
                 } else {
                   run_i[0] = row_max16i(ra, 0, run_i[0]);
                   run_i[1] = row_max16i(ra, 1, run_i[1]);
@@ -807,11 +848,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                   for (int b2 = 0; b2 < 2; ++b2) {
                     const int cc = 8 * j + b2;
                     const bool in = cc >= la && cc < lb;
-                    if (kTokenScale) {
+                    if (kFloat) {
                       run[0] = in ? fmaxf(run[0], __uint_as_float(ra[4 * j + b2])) : run[0];
-                      run[1] = in ? fmaxf(run[1], __uint_as_float(ra[4 * j + 2 + b2])) : run[1];
-                      run[2] = in ? fmaxf(run[2], __uint_as_float(rb[4 * j + b2])) : run[2];
-                      run[3] = in ? fmaxf(run[3], __uint_as_float(rb[4 * j + 2 + b2])) : run[3];
+                      if (!kDigits) {
+                        run[1] = in ? fmaxf(run[1], __uint_as_float(ra[4 * j + 2 + b2])) : run[1];
+                        run[2] = in ? fmaxf(run[2], __uint_as_float(rb[4 * j + b2])) : run[2];
+                        run[3] = in ? fmaxf(run[3], __uint_as_float(rb[4 * j + 2 + b2])) : run[3];
+                      }
                     } else {
                       run_i[0] = in ? max(run_i[0], static_cast<int32_t>(ra[4 * j + b2])) : run_i[0];
                       run_i[1] = in ? max(run_i[1], static_cast<int32_t>(ra[4 * j + 2 + b2])) : run_i[1];
@@ -827,13 +870,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             // document meta->seg_doc[sgi] ends: complete each row's maximum across the four threads
             // holding it, stage the row value scaled by the query scale, flush finished documents.
             float best;
-            if (kTokenScale) {
+            if (kFloat) {
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
+              for (int i = 0; i < kRows; ++i) {
                 run[i] = fmaxf(run[i], __shfl_xor_sync(0xFFFFFFFFu, run[i], 1));
                 run[i] = fmaxf(run[i], __shfl_xor_sync(0xFFFFFFFFu, run[i], 2));
               }
-              best = tc == 0 ? run[0] : tc == 1 ? run[1] : tc == 2 ? run[2] : run[3];
+              best = kDigits ? run[0] : tc == 0 ? run[0] : tc == 1 ? run[1] : tc == 2 ? run[2] : run[3];
             } else {
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
@@ -843,7 +886,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               const int32_t bi = tc == 0 ? run_i[0] : tc == 1 ? run_i[1] : tc == 2 ? run_i[2] : run_i[3];
               best = bi == INT32_MIN ? kLowest : __int2float_rn(bi);
             }
-            rowval[(pending * kG + g) * 128 + wrow] = w_valid ? __fmul_rn(best, qs) : 0.0F;
+            if (w_store) rowval[(pending * kG + g) * 128 + wrow] = w_valid ? __fmul_rn(best, qs) : 0.0F;
             if (etid == 0) group_doc[pending] = meta->seg_doc[sgi];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -933,7 +976,8 @@ int sm_count() {
 
 TcPlan plan_for(const DocsView& d, const QueryView& q, int sms) {
   TcPlan pl{};
-  pl.qpt = 128 / q.qtok;
+  // int8 queries: 128 query rows per tile; fp32 queries as digit planes: 32 (four TMEM lanes a row)
+  pl.qpt = (q.mode == kQueryF32 ? 32 : 128) / q.qtok;
   pl.n_qtiles = (q.batch + pl.qpt - 1) / pl.qpt;
   pl.n_pairs = (pl.n_qtiles + tc::kG - 1) / tc::kG;
   // 2 x SM-count ranges: every CTA gets 2 * n_pairs equal units; ranges of
@@ -1005,6 +1049,70 @@ void launch_expand_codes16(const uint8_t* codes, int64_t num_tokens, uint16_t* o
   check(cudaGetLastError(), "launch f16 expansion kernel");
 }
 
+namespace tc {
+// fp32 query rows -> three int8 digit planes for the tensor-core scan (dim 128).  Row r is scaled by
+// 2^S, S = 22 - E where max|x| = f * 2^E, f in [0.5, 1), so its largest element lies in [2^21, 2^22],
+// and rounded to integers q (|q| <= 2^22).  The signed base-256 digits q = d0 + 256 d1 + 65536 d2
+// (d0, d1 in [-128, 127], |d2| <= 65) are packed like the int8 query words (nibble order: per 8 dims
+// the even dims' bytes, then the odd dims'), plane k at words + k * rows * 32.  The scan's dot of plane
+// k with a token is an exact int32; the three combine to the exact dot of q, and qscale = 2^-S (a power
+// of two, exact) brings it back to the query's scale.  A row of zeros has S = 0; a row holding a
+// non-finite value gets qscale NaN, so its scores are NaN.
+__global__ void split_query_digits_kernel(const float* __restrict__ q, int64_t rows, int32_t* __restrict__ words,
+                                          float* __restrict__ qscale) {
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4 v = __ldg(reinterpret_cast<const float4*>(q + row * 128) + lane);  // dims 4 lane .. 4 lane + 3
+  float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  const bool finite = __all_sync(0xFFFFFFFFu, isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+#pragma unroll
+  for (int delta = 16; delta > 0; delta >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, delta));
+  int S = 0;
+  if (m > 0.0F && finite) {
+    int E = 0;
+    (void)frexpf(m, &E);
+    S = min(22 - E, 149);  // rows below 2^-127 keep fewer bits rather than a zero qscale
+  }
+  const float x[4] = {v.x, v.y, v.z, v.w};
+  uint32_t dig[3] = {0, 0, 0};  // 4 bytes of each plane, dims 4 lane + i
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int qi = finite ? __float2int_rn(ldexpf(x[i], S)) : 0;
+    const int d0 = static_cast<int8_t>(qi & 0xFF);
+    const int r1 = (qi - d0) >> 8;
+    const int d1 = static_cast<int8_t>(r1 & 0xFF);
+    const int d2 = (r1 - d1) >> 8;
+    dig[0] |= static_cast<uint32_t>(d0 & 0xFF) << (8 * i);
+    dig[1] |= static_cast<uint32_t>(d1 & 0xFF) << (8 * i);
+    dig[2] |= static_cast<uint32_t>(d2 & 0xFF) << (8 * i);
+  }
+  // nibble order: group g = lane / 2 (dims 8g .. 8g + 7); word 2g holds the even dims, 2g + 1 the odd.
+  // Lane 2g holds dims 8g..8g+3 and lane 2g + 1 dims 8g+4..8g+7: exchange and interleave.
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const uint32_t mine = dig[k];
+    const uint32_t other = __shfl_xor_sync(0xFFFFFFFFu, mine, 1);
+    const uint32_t first = (lane & 1) ? other : mine;   // dims 8g + 0..3
+    const uint32_t second = (lane & 1) ? mine : other;  // dims 8g + 4..7
+    // even dims: bytes 0, 2 of first, then 0, 2 of second; odd dims: bytes 1, 3 of each
+    const uint32_t even = __byte_perm(first, second, 0x6420);
+    const uint32_t odd = __byte_perm(first, second, 0x7531);
+    words[(static_cast<int64_t>(k) * rows + row) * 32 + lane] = static_cast<int32_t>((lane & 1) ? odd : even);
+  }
+  if (lane == 0) qscale[row] = finite ? ldexpf(1.0F, -S) : __int_as_float(0x7FC00000);
+}
+}  // namespace tc
+
+void launch_split_query_digits(const float* q, int64_t rows, int32_t* words, float* qscale, cudaStream_t stream) {
+  if (rows <= 0) return;
+  const int64_t threads = rows * 32;
+  tc::split_query_digits_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(q, rows, words,
+                                                                                                  qscale);
+  count_launch();
+  check(cudaGetLastError(), "launch query digit-split kernel");
+}
+
 void launch_expand_codes8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t stream) {
   const int64_t chunks = num_tokens * 4;
   if (chunks == 0) return;
@@ -1052,9 +1160,13 @@ CUtensorMap make_operand_map(const void* base, int64_t num_tokens, bool f16) {
 
 bool tc_scan_supported(const DocsView& d, const QueryView& q, const ReduceView& r, const TargetsView& tg,
                        bool residual) {
-  return !residual && d.format == kFormatInt4 && d.dim == 128 && q.mode == kQueryI8 && r.reducer == kMaxSim &&
-         tg.ids == nullptr && q.qtok >= 1 && q.qtok <= 128 && q.batch >= 1 && d.num_docs <= 0x7FFFFFFF &&
-         d.host_offsets != nullptr;
+  // fp32 queries run as digit planes: at most 32 query tokens (one tile), and the digit split reads the
+  // query as float4, so a caller's device pointer must be 16-byte aligned
+  const bool mode_ok = q.mode == kQueryI8
+                           ? q.qtok <= 128
+                           : (q.mode == kQueryF32 && q.qtok <= 32 && (reinterpret_cast<uintptr_t>(q.f32) & 15) == 0);
+  return !residual && d.format == kFormatInt4 && d.dim == 128 && mode_ok && r.reducer == kMaxSim &&
+         tg.ids == nullptr && q.qtok >= 1 && q.batch >= 1 && d.num_docs <= 0x7FFFFFFF && d.host_offsets != nullptr;
 }
 
 size_t tc_scan_workspace_bytes(const DocsView& d, const QueryView& q, const TargetsView&) {
@@ -1144,7 +1256,8 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   prm.out = out;
   prm.error = err;
   const int grid = std::min<int>(sms, prm.num_units);
-  const bool f16 = d.codes16 != nullptr && d.token_scale != nullptr;
+  const bool digits = q.mode == kQueryF32;
+  const bool f16 = !digits && d.codes16 != nullptr && d.token_scale != nullptr;
   const bool pre = f16 || d.codes8 != nullptr;
   const CUtensorMap tmap = f16   ? make_operand_map(d.codes16, d.num_tokens, true)
                            : pre ? make_operand_map(d.codes8, d.num_tokens, false)
@@ -1153,7 +1266,15 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
     check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes), "set tc smem");
     kernel<<<grid, tc::kThreads, smem_bytes, stream>>>(prm, tmap);
   };
-  if (d.token_scale) {
+  if (digits) {
+    if (d.token_scale) {
+      if (pre) go(tc::tc_scan_kernel<true, true, false, true>, tc::Layout<true>::bytes);
+      else go(tc::tc_scan_kernel<true, false, false, true>, tc::Layout<false>::bytes);
+    } else {
+      if (pre) go(tc::tc_scan_kernel<false, true, false, true>, tc::Layout<true>::bytes);
+      else go(tc::tc_scan_kernel<false, false, false, true>, tc::Layout<false>::bytes);
+    }
+  } else if (d.token_scale) {
     if (f16) go(tc::tc_scan_kernel<true, true, true>, tc::Layout<true, true>::bytes);
     else if (pre) go(tc::tc_scan_kernel<true, true, false>, tc::Layout<true>::bytes);
     else go(tc::tc_scan_kernel<true, false, false>, tc::Layout<false>::bytes);

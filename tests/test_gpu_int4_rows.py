@@ -18,6 +18,18 @@ pytestmark = pytest.mark.gpu
 REDUCERS = {"maxsim": 0, "weighted_maxsim": 1, "topk2": 2, "topk4": 3, "smoothsim": 4}
 
 
+@pytest.fixture(autouse=True)
+def simt_engine():
+    """MaxSim scans of aligned fp32 queries with up to 32 tokens would otherwise run on the
+    tensor-core engine; this file compares the two SIMT kernels."""
+    from maxsim_b200 import _lib
+
+    prev = _lib.get_engine()
+    _lib.set_engine(1)
+    yield
+    _lib.set_engine(prev)
+
+
 def _handle(gran, residual, seed=5, num_docs=41, max_len=300):
     import maxsim_b200 as m
     from maxsim_b200._maxsim_cuda import CudaInt4PackedDocs

@@ -1,0 +1,158 @@
+"""fp32 queries on the tensor-core engine: int8 digit planes of the query (dim 128, int4 documents).
+
+Each query row is scaled by 2^S so that its largest magnitude lies in [2^21, 2^22], rounded to
+integers and split into three signed base-256 digits; the engine's int8 MMAs give each digit plane's
+dot with a token exactly, and the epilogue combines them as fl(65536 d2 + fl(d0 + 256 d1)) (one fused
+multiply-add), multiplies by the token scale, takes the maxima, scales them back by 2^-S and sums the
+rows in order.  ``_digit_model`` restates that arithmetic in numpy, so the engine must match it bit for
+bit; against the reference's fp32 scoring (the float64 oracle) the only error is the query's rounding
+to 23 bits and the one rounding of each dot, far inside the fp32 paths' 1e-4 tolerance.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import reference_cpu as ref
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def engine():
+    from maxsim_b200 import _lib
+
+    prev = _lib.get_engine()
+    yield _lib
+    _lib.set_engine(prev)
+
+
+def _digits(q):
+    """[R, 128] fp32 -> (three int64 digit planes [3, R, 128], qscale [R] fp32)."""
+    q = np.asarray(q, np.float32)
+    m = np.abs(q).max(axis=1)
+    _, e = np.frexp(m)
+    s = np.where(m > 0, np.minimum(22 - e, 149), 0).astype(np.int64)
+    qi = np.rint(np.ldexp(q, s[:, None]).astype(np.float32)).astype(np.int64)
+    d0 = ((qi + 128) & 255) - 128
+    r1 = (qi - d0) >> 8
+    d1 = ((r1 + 128) & 255) - 128
+    d2 = (r1 - d1) >> 8
+    assert np.array_equal(d0 + 256 * d1 + 65536 * d2, qi) and np.abs(d2).max() <= 65
+    return np.stack([d0, d1, d2]), np.ldexp(np.float32(1), -s).astype(np.float32)
+
+
+def _digit_model(query, values, offsets, scale, token_scale):
+    """The engine's arithmetic for [B, Q, 128] fp32 queries against int4 values [N, 128]."""
+    B, Q, _ = query.shape
+    digits, qscale = _digits(query.reshape(-1, 128))
+    vals = values.astype(np.int64)
+    dots = np.einsum("kri,ti->krt", digits, vals)  # exact integers
+    lo = (dots[0] + 256 * dots[1]).astype(np.float32)
+    v = (dots[2].astype(np.float64) * 65536.0 + lo.astype(np.float64)).astype(np.float32)
+    if token_scale is not None:
+        v = v * np.asarray(token_scale, np.float32)[None, :]
+    D = offsets.shape[0] - 1
+    out = np.zeros((B, D), np.float32)
+    for d in range(D):
+        a, b = offsets[d], offsets[d + 1]
+        if a == b:
+            continue
+        best = v[:, a:b].max(axis=1) * qscale  # [B * Q], exact power-of-two scaling
+        for bi in range(B):
+            acc = np.float32(0)
+            for r in range(Q):
+                acc = np.float32(acc + best[bi * Q + r])
+            out[bi, d] = np.float32(acc * np.float32(scale))
+    return out
+
+
+def _corpus(num_docs, max_len, seed):
+    docs, off = ref.clustered_corpus(num_docs, 0, max_len, seed=seed)
+    return docs, off
+
+
+@pytest.mark.parametrize("gran", ["tensor", "token"])
+@pytest.mark.parametrize("batch,qtok", [(1, 32), (5, 20), (3, 7), (9, 1)])
+def test_digit_planes_bit_exact_and_within_oracle(engine, gran, batch, qtok):
+    import maxsim_b200 as m
+
+    docs, off = _corpus(300, 300, seed=batch * 7 + qtok)
+    q = ref.clustered_queries(docs, off, batch, qtok, seed=qtok)
+    packed = m.pack_int4_symmetric(docs, off, scale_granularity=gran)
+    dev = m.int4_to_device(packed)
+    engine.set_engine(2)  # the tensor-core engine, or an error
+    got = m.int4_maxsim(q, dev)
+    want = _digit_model(q, packed.values, off, packed.scale, packed.token_scale)
+    np.testing.assert_array_equal(got, want)
+    exact = ref.score_int4_fp32(q, packed.values, off, scale=packed.scale, token_scale=packed.token_scale)
+    np.testing.assert_allclose(got, exact, rtol=2e-6, atol=2e-6 * np.abs(exact).max())
+    engine.set_engine(1)
+    simt = m.int4_maxsim(q, dev)
+    np.testing.assert_allclose(got, simt, rtol=1e-5, atol=1e-5 * np.abs(exact).max())
+    engine.set_engine(0)
+    s, i = m.topk_int4_maxsim(q, dev, 10)
+    for row in range(batch):
+        np.testing.assert_array_equal(s[row], np.sort(got[row])[::-1][:10])
+
+
+def test_digit_planes_extreme_row_magnitudes(engine):
+    """Rows of 1e-30 and 1e30 magnitude, a zero row and a one-hot row keep their relative precision."""
+    import maxsim_b200 as m
+
+    docs, off = _corpus(120, 80, seed=5)
+    q = ref.clustered_queries(docs, off, 2, 8, seed=6).astype(np.float32)
+    q[0, 1] *= np.float32(1e-30)
+    q[0, 2] *= np.float32(1e30)
+    q[1, 3] = 0.0
+    q[1, 4] = 0.0
+    q[1, 4, 17] = -0.25
+    packed = m.pack_int4_symmetric(docs, off, scale_granularity="token")
+    dev = m.int4_to_device(packed)
+    engine.set_engine(2)
+    got = m.int4_maxsim(q, dev)
+    np.testing.assert_array_equal(got, _digit_model(q, packed.values, off, packed.scale, packed.token_scale))
+    exact = ref.score_int4_fp32(q, packed.values, off, scale=packed.scale, token_scale=packed.token_scale)
+    np.testing.assert_allclose(got, exact, rtol=2e-6, atol=0)
+
+
+def test_digit_planes_large_corpus_many_units(engine):
+    """About 330k tokens: many work units per CTA, documents crossing tiles and units."""
+    import maxsim_b200 as m
+
+    docs, off = _corpus(3000, 220, seed=9)
+    q = ref.clustered_queries(docs, off, 4, 32, seed=10)
+    packed = m.pack_int4_symmetric(docs, off, scale_granularity="token")
+    dev = m.int4_to_device(packed)
+    engine.set_engine(2)
+    got = m.int4_maxsim(q, dev)
+    np.testing.assert_array_equal(got, _digit_model(q, packed.values, off, packed.scale, packed.token_scale))
+
+
+def test_fp32_scans_outside_the_digit_path_stay_simt(engine):
+    """33 query tokens, or a query pointer that is not 16-byte aligned, run on the SIMT engine."""
+    import torch
+    import maxsim_b200 as m
+
+    docs, off = _corpus(60, 50, seed=3)
+    packed = m.pack_int4_symmetric(docs, off, scale_granularity="token")
+    dev = m.int4_to_device(packed)
+    q33 = ref.clustered_queries(docs, off, 2, 33, seed=4)
+    engine.set_engine(1)
+    want = m.int4_maxsim(q33, dev)
+    engine.set_engine(0)
+    np.testing.assert_array_equal(m.int4_maxsim(q33, dev), want)
+    engine.set_engine(2)
+    with pytest.raises(NotImplementedError):
+        m.int4_maxsim(q33, dev)
+
+    h = dev.data
+    q = ref.clustered_queries(docs, off, 2, 16, seed=5)
+    buf = torch.zeros(q.size + 4, dtype=torch.float32, device="cuda")
+    view = buf[1:1 + q.size].view(q.shape)
+    view.copy_(torch.from_numpy(q))
+    out = torch.empty(2, h.num_docs, device="cuda")
+    engine.set_engine(0)
+    h.score_batch_device(view, out)
+    torch.cuda.synchronize()
+    engine.set_engine(1)
+    np.testing.assert_array_equal(out.cpu().numpy(), m.int4_maxsim(q, dev))
