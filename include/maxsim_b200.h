@@ -98,7 +98,12 @@ int64_t msb_launch_count(void);
  * where unsupported).  "tc_int8_cache": 1 (default) lets the tensor-core engine
  * keep a resident int8 copy of an int4 corpus (128 B per token, built on first
  * use and counted in resident_bytes) and stream operand tiles from it with
- * TMA; 0 expands int4 rows per tile instead.  "tc_f16_cache": 1 keeps an f16
+ * TMA; 0 expands int4 rows per tile instead.  Sign-code (binary) corpora
+ * always keep a +-1 int8 copy when the tensor-core engine scans them (MaxSim,
+ * dim 128, scalar document scale), and use the SIMT engine when there is no
+ * memory for it.  fp32 queries of up to 32 tokens run on the tensor-core
+ * engine as three int8 digit planes of each row's 23-bit fixed-point value
+ * (exact integer dots, one rounding).  "tc_f16_cache": 1 keeps an f16
  * copy instead (256 B per token, per-token-scale corpora) and runs kind::f16
  * MMAs whose fp32 accumulators hold the exact integer dots, so the epilogue
  * converts nothing; 0 (default) because its doubled MMA and operand traffic

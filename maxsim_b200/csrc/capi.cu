@@ -30,6 +30,7 @@ void launch_tc_scan(const DocsView&, const QueryView&, const ReduceView&, const 
 size_t tc_scan_workspace_bytes(const DocsView&, const QueryView&, const TargetsView&);
 bool tc_int8_cache_supported(const DocsView&);
 void launch_expand_codes8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t);
+void launch_expand_binary8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t);
 void launch_expand_codes16(const uint8_t* codes, int64_t num_tokens, uint16_t* out, cudaStream_t);
 
 static std::atomic<int64_t> g_launches{0};
@@ -285,36 +286,17 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
   qv.batch = batch;
   qv.qtok = qtok;
   qv.mode = r.mode;
-  if (r.mode == kQueryI8) {
-    const int64_t rows = static_cast<int64_t>(batch) * qtok;
-    h->w_qcodes.ensure(static_cast<size_t>(rows) * h->dim, "cudaMalloc int8 query codes");
-    h->w_qwords.ensure(static_cast<size_t>(rows) * h->dim, "cudaMalloc int8 query words");
-    h->w_qscale.ensure(static_cast<size_t>(rows) * sizeof(float), "cudaMalloc int8 query scales");
-    h->w_qsum.ensure(static_cast<size_t>(rows) * sizeof(int32_t), "cudaMalloc int8 query sums");
-    launch_quantize_rows(d_query, rows, h->dim, h->w_qcodes.as<int8_t>(), h->w_qscale.as<float>(),
-                         h->w_qsum.as<int32_t>(), h->w_qwords.as<int32_t>(), h->format == kFormatInt4, stream);
-    qv.i8 = h->w_qcodes.as<int8_t>();
-    qv.i8_words = h->w_qwords.as<int32_t>();
-    qv.row_scale = h->w_qscale.as<float>();
-    qv.row_sum = h->w_qsum.as<int32_t>();
-  }
   const int engine = g_engine.load();
   const bool tc_ok = tc_scan_supported(r.docs, qv, r.red, tg, r.residual);
   if (engine == 2 && !tc_ok) throw NotSupported("the tensor-core engine does not support this scan");
-  if (tc_ok && engine != 1) {
-    if (r.mode == kQueryF32) {
-      // fp32 queries: three int8 digit planes and a power-of-two scale per row
-      const int64_t rows = static_cast<int64_t>(batch) * qtok;
-      h->w_qwords.ensure(static_cast<size_t>(rows) * 3 * h->dim, "cudaMalloc query digit planes");
-      h->w_qscale.ensure(static_cast<size_t>(rows) * sizeof(float), "cudaMalloc query digit scales");
-      launch_split_query_digits(d_query, rows, h->w_qwords.as<int32_t>(), h->w_qscale.as<float>(), stream);
-      qv.i8_words = h->w_qwords.as<int32_t>();
-      qv.row_scale = h->w_qscale.as<float>();
-    }
-    const size_t ws = tc_scan_workspace_bytes(r.docs, qv, tg);
-    h->w_tc.ensure(ws > 0 ? ws : 16, "cudaMalloc tensor-core scan workspace");
-    DocsView dv = r.docs;
-    if (g_tc_f16_cache.load() && !h->codes16_failed && dv.token_scale && tc_int8_cache_supported(dv)) {
+  bool use_tc = tc_ok && engine != 1;
+  DocsView dv = r.docs;
+  if (use_tc) {
+    // Resident operand copies for the tensor-core engine, made once per handle: an f16 copy (option), or
+    // the int8 copy (int4 expanded, or +-1 for sign codes).  int4 corpora fall back to expanding per
+    // tile when there is no memory for a copy; binary corpora fall back to the SIMT engine.
+    const bool binary = h->format == kFormatBinary;
+    if (!binary && g_tc_f16_cache.load() && !h->codes16_failed && dv.token_scale && tc_int8_cache_supported(dv)) {
       if (!h->codes16.ptr) {
         const size_t bytes = static_cast<size_t>(h->num_tokens) * 256;
         void* p = nullptr;
@@ -330,21 +312,54 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
       }
       if (h->codes16.ptr) dv.codes16 = static_cast<const uint16_t*>(h->codes16.ptr);
     }
-    if (!dv.codes16 && g_tc_int8_cache.load() && !h->codes8_failed && tc_int8_cache_supported(dv)) {
+    if (!dv.codes16 && (binary || g_tc_int8_cache.load()) && !h->codes8_failed && tc_int8_cache_supported(dv)) {
       if (!h->codes8.ptr) {
         const size_t bytes = static_cast<size_t>(h->num_tokens) * 128;
         void* p = nullptr;
         if (cudaMalloc(&p, bytes) != cudaSuccess) {
-          (void)cudaGetLastError();  // not enough memory for the copy: keep expanding per tile
+          (void)cudaGetLastError();  // not enough memory for the copy
           h->codes8_failed = true;
         } else {
           h->codes8.ptr = p;
           h->codes8.cap = bytes;
-          launch_expand_codes8(h->codes.as<uint8_t>(), h->num_tokens, h->codes8.as<uint8_t>(), stream);
+          if (binary) launch_expand_binary8(h->codes.as<uint8_t>(), h->num_tokens, h->codes8.as<uint8_t>(), stream);
+          else launch_expand_codes8(h->codes.as<uint8_t>(), h->num_tokens, h->codes8.as<uint8_t>(), stream);
         }
       }
       if (h->codes8.ptr) dv.codes8 = h->codes8.as<uint8_t>();
     }
+    if (binary && !dv.codes8) {
+      if (engine == 2) throw NotSupported("no device memory for the tensor-core engine's int8 copy of the sign codes");
+      use_tc = false;
+    }
+  }
+  const int64_t rows = static_cast<int64_t>(batch) * qtok;
+  if (r.mode == kQueryI8) {
+    h->w_qcodes.ensure(static_cast<size_t>(rows) * h->dim, "cudaMalloc int8 query codes");
+    h->w_qwords.ensure(static_cast<size_t>(rows) * h->dim, "cudaMalloc int8 query words");
+    h->w_qscale.ensure(static_cast<size_t>(rows) * sizeof(float), "cudaMalloc int8 query scales");
+    h->w_qsum.ensure(static_cast<size_t>(rows) * sizeof(int32_t), "cudaMalloc int8 query sums");
+    // words in the order the chosen dot reads: nibble order for int4 codes and for the tensor-core
+    // engine's int8 copies, natural order for the SIMT sign-code dot
+    launch_quantize_rows(d_query, rows, h->dim, h->w_qcodes.as<int8_t>(), h->w_qscale.as<float>(),
+                         h->w_qsum.as<int32_t>(), h->w_qwords.as<int32_t>(), h->format == kFormatInt4 || use_tc,
+                         stream);
+    qv.i8 = h->w_qcodes.as<int8_t>();
+    qv.i8_words = h->w_qwords.as<int32_t>();
+    qv.row_scale = h->w_qscale.as<float>();
+    qv.row_sum = h->w_qsum.as<int32_t>();
+  }
+  if (use_tc) {
+    if (r.mode == kQueryF32) {
+      // fp32 queries: three int8 digit planes and a power-of-two scale per row
+      h->w_qwords.ensure(static_cast<size_t>(rows) * 3 * h->dim, "cudaMalloc query digit planes");
+      h->w_qscale.ensure(static_cast<size_t>(rows) * sizeof(float), "cudaMalloc query digit scales");
+      launch_split_query_digits(d_query, rows, h->w_qwords.as<int32_t>(), h->w_qscale.as<float>(), stream);
+      qv.i8_words = h->w_qwords.as<int32_t>();
+      qv.row_scale = h->w_qscale.as<float>();
+    }
+    const size_t ws = tc_scan_workspace_bytes(dv, qv, tg);
+    h->w_tc.ensure(ws > 0 ? ws : 16, "cudaMalloc tensor-core scan workspace");
     launch_tc_scan(dv, qv, r.red, tg, d_out, h->w_tc.ptr, h->w_tc.cap, stream);
     h->tc_used = true;
     return;

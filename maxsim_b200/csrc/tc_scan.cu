@@ -990,7 +990,8 @@ TcPlan plan_for(const DocsView& d, const QueryView& q, int sms) {
 
 bool tc_int8_cache_supported(const DocsView& d) {
   // TMA row coordinates are 32-bit
-  return d.format == kFormatInt4 && d.dim == 128 && d.num_tokens > 0 && d.num_tokens < 0x7FFFFF00LL;
+  return (d.format == kFormatInt4 || d.format == kFormatBinary) && d.dim == 128 && d.num_tokens > 0 &&
+         d.num_tokens < 0x7FFFFF00LL;
 }
 
 namespace tc {
@@ -1050,6 +1051,23 @@ void launch_expand_codes16(const uint8_t* codes, int64_t num_tokens, uint16_t* o
 }
 
 namespace tc {
+// Sign codes [N, 16] (dim 8g + j is bit j of byte g; set = +1) -> int8 rows [N, 128] of +-1 in the scan's
+// K order: per 8 dims, the even dims' bytes then the odd dims' (the order of the int4 copy and of the
+// query words), so the tensor-core scan reads binary and int4 corpora alike.
+__global__ void expand_binary8_kernel(const uint8_t* __restrict__ in, int64_t n_groups, uint2* __restrict__ out) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_groups;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t b = __ldg(in + i);
+    uint32_t even = 0, odd = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      even |= (((b >> (2 * k)) & 1u) ? 0x01u : 0xFFu) << (8 * k);
+      odd |= (((b >> (2 * k + 1)) & 1u) ? 0x01u : 0xFFu) << (8 * k);
+    }
+    out[i] = make_uint2(even, odd);
+  }
+}
+
 // fp32 query rows -> three int8 digit planes for the tensor-core scan (dim 128).  Row r is scaled by
 // 2^S, S = 22 - E where max|x| = f * 2^E, f in [0.5, 1), so its largest element lies in [2^21, 2^22],
 // and rounded to integers q (|q| <= 2^22).  The signed base-256 digits q = d0 + 256 d1 + 65536 d2
@@ -1113,6 +1131,15 @@ void launch_split_query_digits(const float* q, int64_t rows, int32_t* words, flo
   check(cudaGetLastError(), "launch query digit-split kernel");
 }
 
+void launch_expand_binary8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t stream) {
+  const int64_t groups = num_tokens * 16;
+  if (groups == 0) return;
+  const int blocks = static_cast<int>(std::min<int64_t>((groups + 255) / 256, 148LL * 16));
+  tc::expand_binary8_kernel<<<blocks, 256, 0, stream>>>(codes, groups, reinterpret_cast<uint2*>(out));
+  count_launch();
+  check(cudaGetLastError(), "launch sign-code expansion kernel");
+}
+
 void launch_expand_codes8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t stream) {
   const int64_t chunks = num_tokens * 4;
   if (chunks == 0) return;
@@ -1165,8 +1192,10 @@ bool tc_scan_supported(const DocsView& d, const QueryView& q, const ReduceView& 
   const bool mode_ok = q.mode == kQueryI8
                            ? q.qtok <= 128
                            : (q.mode == kQueryF32 && q.qtok <= 32 && (reinterpret_cast<uintptr_t>(q.f32) & 15) == 0);
-  return !residual && d.format == kFormatInt4 && d.dim == 128 && mode_ok && r.reducer == kMaxSim &&
-         tg.ids == nullptr && q.qtok >= 1 && q.batch >= 1 && d.num_docs <= 0x7FFFFFFF && d.host_offsets != nullptr;
+  // binary corpora: a scalar document scale (the epilogue's one factor), read from the resident +-1 copy
+  const bool format_ok = d.format == kFormatInt4 || (d.format == kFormatBinary && d.doc_scale == nullptr);
+  return !residual && format_ok && d.dim == 128 && mode_ok && r.reducer == kMaxSim && tg.ids == nullptr &&
+         q.qtok >= 1 && q.batch >= 1 && d.num_docs <= 0x7FFFFFFF && d.host_offsets != nullptr;
 }
 
 size_t tc_scan_workspace_bytes(const DocsView& d, const QueryView& q, const TargetsView&) {
@@ -1257,8 +1286,10 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   prm.error = err;
   const int grid = std::min<int>(sms, prm.num_units);
   const bool digits = q.mode == kQueryF32;
-  const bool f16 = !digits && d.codes16 != nullptr && d.token_scale != nullptr;
+  const bool f16 = !digits && d.format == kFormatInt4 && d.codes16 != nullptr && d.token_scale != nullptr;
   const bool pre = f16 || d.codes8 != nullptr;
+  // the expanding path decodes int4 rows: binary corpora need their +-1 copy
+  if (d.format == kFormatBinary && !d.codes8) throw CudaFailure("binary tensor-core scan without the int8 copy");
   const CUtensorMap tmap = f16   ? make_operand_map(d.codes16, d.num_tokens, true)
                            : pre ? make_operand_map(d.codes8, d.num_tokens, false)
                                  : CUtensorMap{};

@@ -1,4 +1,4 @@
-"""fp32 queries on the tensor-core engine: int8 digit planes of the query (dim 128, int4 documents).
+"""fp32 queries on the tensor-core engine: int8 digit planes of the query (dim 128, int4 and sign codes).
 
 Each query row is scaled by 2^S so that its largest magnitude lies in [2^21, 2^22], rounded to
 integers and split into three signed base-256 digits; the engine's int8 MMAs give each digit plane's
@@ -156,3 +156,61 @@ def test_fp32_scans_outside_the_digit_path_stay_simt(engine):
     torch.cuda.synchronize()
     engine.set_engine(1)
     np.testing.assert_array_equal(out.cpu().numpy(), m.int4_maxsim(q, dev))
+
+
+# ---------------------------------------------------------------------------
+# Sign-code corpora: the engine reads a resident +-1 int8 copy of the codes
+# ---------------------------------------------------------------------------
+
+def _binary(docs, off, token_scale):
+    import maxsim_b200 as m
+
+    kw = {"token_scale": "mean_abs_fp16"} if token_scale else {}
+    packed = m.pack_signs(docs, off, **kw)
+    return packed, m.to_device(packed, "cuda").data
+
+
+@pytest.mark.parametrize("token_scale", [False, True])
+@pytest.mark.parametrize("batch,qtok", [(1, 20), (6, 32), (4, 5)])
+def test_binary_digit_planes_bit_exact(engine, token_scale, batch, qtok):
+    docs, off = _corpus(250, 260, seed=batch + qtok)
+    q = ref.clustered_queries(docs, off, batch, qtok, seed=qtok + 1)
+    packed, h = _binary(docs, off, token_scale)
+    signs = ref.unpack_signs(packed.data, 128).astype(np.int64)
+    ts = np.asarray(packed.token_scale, np.float32) if token_scale else None
+    engine.set_engine(2)
+    got = h.score_batch(q, scale=0.75, use_token_scale=token_scale)
+    np.testing.assert_array_equal(got, _digit_model(q, signs, off, 0.75, ts))
+    exact = ref.score_binary_fp32(q, packed.data, 128, off, token_scale=ts, doc_scale=0.75)
+    np.testing.assert_allclose(got, exact, rtol=2e-6, atol=2e-6 * np.abs(exact).max())
+    s, i = h.topk_batch(q, 7, scale=0.75, use_token_scale=token_scale)
+    for row in range(batch):
+        np.testing.assert_array_equal(s[row], np.sort(got[row])[::-1][:7])
+
+
+@pytest.mark.parametrize("token_scale", [False, True])
+def test_binary_int8_queries_tensor_core_equals_simt(engine, token_scale):
+    """int8 queries: both engines compute the exact integer dot with +-1, so the scores are identical."""
+    docs, off = _corpus(300, 200, seed=21)
+    q = ref.clustered_queries(docs, off, 5, 32, seed=22)
+    _, h = _binary(docs, off, token_scale)
+    engine.set_engine(2)
+    got = h.maxsim_batch_int8q(q, scale=1.5, use_token_scale=token_scale)
+    engine.set_engine(1)
+    want = h.maxsim_batch_int8q(q, scale=1.5, use_token_scale=token_scale)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_binary_document_scales_stay_simt(engine):
+    import maxsim_b200 as m
+
+    docs, off = _corpus(80, 60, seed=23)
+    q = ref.clustered_queries(docs, off, 2, 16, seed=24)
+    h = m.to_device(m.pack_signs(docs, off, scale="doc"), "cuda").data
+    engine.set_engine(2)
+    with pytest.raises(NotImplementedError):
+        h.score_batch(q, use_scale_vector=True)
+    engine.set_engine(1)
+    want = h.score_batch(q, use_scale_vector=True)
+    engine.set_engine(0)
+    np.testing.assert_array_equal(h.score_batch(q, use_scale_vector=True), want)
