@@ -89,6 +89,8 @@ struct Params {
   const float* qscale;        // [B*Q]
   const Unit* units;
   int num_units;
+  int num_items;              // work items: units, or (twin) pairs of units
+  int twin;                   // one query tile: the two epilogue groups take two units' tiles in turn
   int batch;
   int qtok;
   int qpt;                    // queries per tile
@@ -141,7 +143,7 @@ struct Layout {
   static constexpr int off_uoff = off_meta + kMeta * kMetaBytes;
   static constexpr int off_row = off_uoff + 2 * kUoffEntries * 8;
   static constexpr int off_bar = off_row + kRowBytes + 128;  // + per-group doc ids
-  static constexpr int num_bars = 2 * stages + 2 * kMeta + 2 * kRaw + kAccBufs + 9;
+  static constexpr int num_bars = 2 * stages + 2 * kMeta + 2 * kRaw + kAccBufs + 10;
   static constexpr int bytes = off_bar + num_bars * 8 + 64 + 1024;  // + alignment slack
   static_assert(bytes <= 227 * 1024, "shared memory budget");
   static_assert(off_b % 1024 == 0 && b_tile % 1024 == 0 && a_tile % 1024 == 0, "128-byte-swizzled operand tiles");
@@ -336,6 +338,46 @@ struct Ring {
 // kPre: the int4 codes were expanded once into an int8 copy (same K order); each B stage is a tiled TMA
 // load of 128 rows from it, landing in the 128-byte-swizzled layout, and the expanders only stage the
 // tile metadata.  Otherwise the loader copies raw int4 rows and the expanders build the B stage.
+// A work item is one unit, or in twin mode (a single query tile) the two units 2w and 2w + 1 whose token
+// tiles alternate, side 0 first: epilogue group g takes side g's tiles, so both groups work although only
+// one query tile exists.  A side whose unit has run out of tiles (or an odd unit count's missing unit)
+// contributes empty tiles (no columns), so every role enumerates the same steps.
+struct Item {
+  Unit un[2];
+  int64_t nsteps;
+};
+__device__ __forceinline__ int64_t unit_tiles(const Unit& u) { return (u.tok_hi - u.tok_lo + kTileN - 1) / kTileN; }
+__device__ __forceinline__ Item load_item(const Params& p, int w) {
+  Item it;
+  if (p.twin) {
+    const Unit none{0, 0, 0, 0, 0, 0};
+    it.un[0] = p.units[2 * w];
+    it.un[1] = 2 * w + 1 < p.num_units ? p.units[2 * w + 1] : none;
+    it.nsteps = 2 * max(unit_tiles(it.un[0]), unit_tiles(it.un[1]));
+  } else {
+    it.un[0] = p.units[w];
+    it.un[1] = it.un[0];
+    it.nsteps = unit_tiles(it.un[0]);
+  }
+  return it;
+}
+struct Step {
+  int side;       // unit of the item (0 outside twin mode)
+  int valid;      // columns of the tile (0: an empty tile)
+  bool last;      // the unit's last tile
+  int64_t t0;     // first token
+};
+__device__ __forceinline__ Step step_of(const Params& p, const Item& it, int64_t i) {
+  Step st;
+  st.side = p.twin ? static_cast<int>(i & 1) : 0;
+  const Unit& u = st.side ? it.un[1] : it.un[0];
+  st.t0 = u.tok_lo + (p.twin ? (i >> 1) : i) * kTileN;
+  const int64_t rem = u.tok_hi - st.t0;
+  st.valid = rem <= 0 ? 0 : (rem < kTileN ? static_cast<int>(rem) : kTileN);
+  st.last = rem > 0 && rem <= kTileN;
+  return st;
+}
+
 // kDigits: fp32 queries as three int8 digit planes (split_query_digits_kernel).  Query row rho of a tile
 // (32 per tile) has its digit k on TMEM lane 32 (rho / 8) + 8 k + rho % 8 (k = 3: zeros), the four lanes
 // one epilogue thread holds, which combines them to d0 + 256 d1 + 65536 d2 before the scale and maximum.
@@ -361,11 +403,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
   uint64_t* a_empty = a_full + 2;                // [2]        MMA commit -> expanders
   uint64_t* u_full = a_empty + 2;                // [2]        unit offsets bulk copy -> segment warp
   uint64_t* u_empty = u_full + 2;                // [2]        segment warp -> loader
-  uint64_t* epi_bar = u_empty + 2;               // [1]        epilogue warps among themselves (document flush)
+  uint64_t* epi_bar = u_empty + 2;               // [2]        epilogue warps among themselves (document flush;
+                                                 //            one per group in twin mode)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::num_bars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* rowval = reinterpret_cast<float*>(smem + L::off_row);                      // [group][kG][128]
-  int32_t* group_doc = reinterpret_cast<int32_t*>(smem + L::off_row + kRowBytes);  // [kSegGroup]
+  int32_t* group_doc = reinterpret_cast<int32_t*>(smem + L::off_row + kRowBytes);  // [2][kSegGroup]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -378,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     }
     for (int s = 0; s < kMeta; ++s) {
       mbar_init(&m_full[s], kXWarps);
-      mbar_init(&m_empty[s], kEpiWarps);
+      mbar_init(&m_empty[s], p.twin ? kEpiWarps / 2 : kEpiWarps);  // twin: only the owning group reads a tile
     }
     for (int s = 0; s < kRaw; ++s) {
       mbar_init(&raw_full[s], 1);
@@ -391,7 +434,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       mbar_init(&u_full[a], 1);
       mbar_init(&u_empty[a], 1);
     }
-    mbar_init(epi_bar, kEpiWarps);
+    if (p.twin) {
+      mbar_init(&epi_bar[0], kEpiWarps / 2);
+      mbar_init(&epi_bar[1], kEpiWarps / 2);
+    } else {
+      mbar_init(&epi_bar[0], kEpiWarps);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -411,39 +459,52 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     if (lane == 0) {
       Ring raw, stg;
       int iter = 0;
-      for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
-        const Unit unit = p.units[u];
-        const int ub = iter & 1;
-        if (iter >= 2 && !mbar_wait(&u_empty[ub], ((iter >> 1) - 1) & 1, abort_flag, p.error, 41)) goto done;
-        {
-          // offsets[d_lo .. d_hi] as a 16-byte-aligned superset (the buffer is padded)
-          const int64_t first = unit.d_lo & ~1LL;
-          const int64_t count = ((unit.d_hi + 1 - first) + 1) & ~1LL;
-          const uint32_t bytes = static_cast<uint32_t>(count * 8);
-          mbar_expect_tx(&u_full[ub], bytes);
-          bulk_g2s(smem + L::off_uoff + ub * kUoffEntries * 8, p.offsets + first, bytes, &u_full[ub]);
+      for (int w = blockIdx.x; w < p.num_items; w += gridDim.x, ++iter) {
+        const Item it = load_item(p, w);
+        // Each unit's offsets[d_lo .. d_hi] as a 16-byte-aligned superset (the buffer is padded): slots
+        // alternate between items, or (twin mode) slot s holds side s.
+        for (int side = 0; side < (p.twin ? 2 : 1); ++side) {
+          const int ub = p.twin ? side : (iter & 1);
+          const int use = p.twin ? iter : (iter >> 1);  // earlier uses of the slot
+          if (use >= 1 && !mbar_wait(&u_empty[ub], (use - 1) & 1, abort_flag, p.error, 41)) goto done;
+          const Unit& unit = side ? it.un[1] : it.un[0];
+          if (unit.d_hi > unit.d_lo) {
+            const int64_t first = unit.d_lo & ~1LL;
+            const int64_t count = ((unit.d_hi + 1 - first) + 1) & ~1LL;
+            const uint32_t bytes = static_cast<uint32_t>(count * 8);
+            mbar_expect_tx(&u_full[ub], bytes);
+            bulk_g2s(smem + L::off_uoff + ub * kUoffEntries * 8, p.offsets + first, bytes, &u_full[ub]);
+          } else {
+            mbar_arrive(&u_full[ub]);  // an odd unit count's missing unit: no documents
+          }
         }
-        for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
+        for (int64_t i = 0; i < it.nsteps; ++i) {
+          const Step st = step_of(p, it, i);
+          const int64_t t0 = st.t0;
+          const int valid = st.valid;
           if (kPre) {
             // B stage: wait until the MMAs that read it have completed, then one tiled TMA load
             if (!mbar_wait(&tile_done[stg.idx], stg.phase ^ 1, abort_flag, p.error, 43)) goto done;
-            mbar_expect_tx(&full[stg.idx], static_cast<uint32_t>(L::b_tile));
-            unsigned char* bdst = smem + L::off_b + stg.idx * L::b_tile;
-            tma_load_2d(bdst, &tmap, 0, static_cast<int>(t0), &full[stg.idx]);
-            // f16: the second K half (values 64..127, byte 128 of each row: x * 2 B is 16-byte aligned)
-            if (kF16) tma_load_2d(bdst + kBTileBytes, &tmap, 64, static_cast<int>(t0), &full[stg.idx]);
+            if (valid > 0) {
+              mbar_expect_tx(&full[stg.idx], static_cast<uint32_t>(L::b_tile));
+              unsigned char* bdst = smem + L::off_b + stg.idx * L::b_tile;
+              tma_load_2d(bdst, &tmap, 0, static_cast<int>(t0), &full[stg.idx]);
+              // f16: the second K half (values 64..127, byte 128 of each row: x * 2 B is 16-byte aligned)
+              if (kF16) tma_load_2d(bdst + kBTileBytes, &tmap, 64, static_cast<int>(t0), &full[stg.idx]);
+            } else {
+              mbar_arrive(&full[stg.idx]);  // an empty tile: nothing to load
+            }
             stg.next<L::stages>();
           }
           if (!mbar_wait(&raw_empty[raw.idx], raw.phase ^ 1, abort_flag, p.error, 42)) goto done;
-          const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
           unsigned char* rb = smem + L::off_raw + raw.idx * L::raw_bytes;
           const uint32_t code_bytes = kPre ? 0u : static_cast<uint32_t>(valid) * 64u;
           uint32_t scale_bytes = 0;
           const int64_t s_first = t0 & ~3LL;
-          if (kTokenScale) scale_bytes = static_cast<uint32_t>(((t0 + valid - s_first + 3) & ~3LL) * 4);
+          if (kTokenScale && valid > 0) scale_bytes = static_cast<uint32_t>(((t0 + valid - s_first + 3) & ~3LL) * 4);
           mbar_expect_tx(&raw_full[raw.idx], code_bytes + scale_bytes);
-          if (!kPre) bulk_g2s(rb, p.codes + t0 * 64, code_bytes, &raw_full[raw.idx]);
-          if (kTokenScale) bulk_g2s(rb + L::raw_code_bytes, p.token_scale + s_first, scale_bytes, &raw_full[raw.idx]);
+          if (code_bytes) bulk_g2s(rb, p.codes + t0 * 64, code_bytes, &raw_full[raw.idx]);
+          if (scale_bytes) bulk_g2s(rb + L::raw_code_bytes, p.token_scale + s_first, scale_bytes, &raw_full[raw.idx]);
           raw.next<kRaw>();
         }
       }
@@ -454,8 +515,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     const int xwarp = warp - kXWarp0;
     Ring raw, stg, mst;
     int iter = 0;
-    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
-      const Unit unit = p.units[u];
+    for (int w = blockIdx.x; w < p.num_items; w += gridDim.x, ++iter) {
+      const Item it = load_item(p, w);
+      const int32_t qpair = it.un[0].qpair;  // twin mode: both units hold the one query tile
       const int abuf = iter % L::a_bufs;
       const int ause = iter / L::a_bufs;
       if (ause >= 1 && !mbar_wait(&a_empty[abuf], (ause - 1) & 1, abort_flag, p.error, 11)) goto done;
@@ -470,12 +532,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           if (kDigits) {
             const int k = (row >> 3) & 3;                   // digit plane of this lane
             const int rho = ((row >> 5) << 3) | (row & 7);  // query row of the tile
-            b = (unit.qpair * kG + g) * p.qpt + rho / Q;
+            b = (qpair * kG + g) * p.qpt + rho / Q;
             qrow = rho % Q;
             valid = k < 3 && rho < p.qpt * Q && b < p.batch;
             src_row = valid ? static_cast<int64_t>(k) * p.batch * Q + static_cast<int64_t>(b) * Q + qrow : 0;
           } else {
-            b = (unit.qpair * kG + g) * p.qpt + row / Q;
+            b = (qpair * kG + g) * p.qpt + row / Q;
             qrow = row % Q;
             valid = row < p.qpt * Q && b < p.batch;
             src_row = valid ? static_cast<int64_t>(b) * Q + qrow : 0;
@@ -510,19 +572,28 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[abuf]);
       }
-      const int ub = iter & 1;
-      const int64_t* uoff = reinterpret_cast<const int64_t*>(smem + L::off_uoff + ub * kUoffEntries * 8);
-      const int64_t ufirst = unit.d_lo & ~1LL;
-      if (xwarp == 0 && !mbar_wait(&u_full[ub], (iter >> 1) & 1, abort_flag, p.error, 13)) goto done;
-      int64_t next_doc = unit.d_lo;  // first document whose end has not been passed
-      for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
+      if (xwarp == 0) {
+        for (int side = 0; side < (p.twin ? 2 : 1); ++side) {
+          const int ub = p.twin ? side : (iter & 1);
+          const int use = p.twin ? iter : (iter >> 1);
+          if (!mbar_wait(&u_full[ub], use & 1, abort_flag, p.error, 13)) goto done;
+        }
+      }
+      int64_t next_doc0 = it.un[0].d_lo, next_doc1 = it.un[1].d_lo;  // first documents whose ends are ahead
+      for (int64_t i = 0; i < it.nsteps; ++i) {
+        const Step st = step_of(p, it, i);
+        const Unit& unit = st.side ? it.un[1] : it.un[0];
+        const int ub = p.twin ? st.side : (iter & 1);
+        const int64_t* uoff = reinterpret_cast<const int64_t*>(smem + L::off_uoff + ub * kUoffEntries * 8);
+        const int64_t ufirst = unit.d_lo & ~1LL;
+        const int64_t t0 = st.t0;
         if (!mbar_wait(&raw_full[raw.idx], raw.phase, abort_flag, p.error, 14)) goto done;
         if (!kPre && !mbar_wait(&tile_done[stg.idx], stg.phase ^ 1, abort_flag, p.error, 12)) goto done;
         if (!mbar_wait(&m_empty[mst.idx], mst.phase ^ 1, abort_flag, p.error, 15)) goto done;
         const unsigned char* rb = smem + L::off_raw + raw.idx * L::raw_bytes;
         unsigned char* Bt = smem + L::off_b + stg.idx * L::b_tile;
         StageMeta* meta = reinterpret_cast<StageMeta*>(smem + L::off_meta + mst.idx * kMetaBytes);
-        const int valid = static_cast<int>(unit.tok_hi - t0 < kTileN ? unit.tok_hi - t0 : kTileN);
+        const int valid = st.valid;
         if (kPre && kTokenScale) {
           const float* rs = reinterpret_cast<const float*>(rb + L::raw_code_bytes);
           for (int r = xtid; r < valid; r += kXWarps * 32) meta->scale[scale_slot(r)] = rs[(t0 & 3) + r];
@@ -560,7 +631,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         if (xwarp == 0) {
           int nseg = 0;
           const int64_t tile_end = t0 + valid;
-          while (true) {
+          int64_t next_doc = st.side ? next_doc1 : next_doc0;
+          while (valid > 0) {
             const int64_t d = next_doc + lane;
             const bool in = d < unit.d_hi;
             const int64_t e = in ? uoff[d + 1 - ufirst] : INT64_MAX;
@@ -579,6 +651,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             next_doc += consumed;
             if (consumed < 32) break;
           }
+          if (st.side) next_doc1 = next_doc;
+          else next_doc0 = next_doc;
           if (lane == 0) {
             meta->nseg = nseg;
             meta->valid = valid;
@@ -599,7 +673,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         stg.next<L::stages>();
         mst.next<kMeta>();
       }
-      if (xwarp == 0 && lane == 0) mbar_arrive(&u_empty[ub]);
+      if (xwarp == 0 && lane == 0) {
+        for (int side = 0; side < (p.twin ? 2 : 1); ++side) mbar_arrive(&u_empty[p.twin ? side : (iter & 1)]);
+      }
     }
   } else if (warp == kMmaWarp) {
     // =================== MMA issuer ===================
@@ -610,22 +686,28 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                                  (static_cast<uint32_t>(128 >> 4) << 24);
     Ring stg, acc;
     int iter = 0;
-    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++iter) {
-      const Unit unit = p.units[u];
+    for (int w = blockIdx.x; w < p.num_items; w += gridDim.x, ++iter) {
+      const Item it = load_item(p, w);
       const int abuf = iter % L::a_bufs;
       // query tiles of the pair that hold at least one query
-      const int n_tiles = min(kG, (p.batch - unit.qpair * kG * p.qpt + p.qpt - 1) / p.qpt);
+      const int n_tiles = min(kG, (p.batch - it.un[0].qpair * kG * p.qpt + p.qpt - 1) / p.qpt);
       if (!mbar_wait(&a_full[abuf], (iter / L::a_bufs) & 1, abort_flag, p.error, 21)) goto done;
       const uint32_t a_addr = smem_u32(smem + L::off_a + abuf * kG * L::a_tile);
-      for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
+      for (int64_t i = 0; i < it.nsteps; ++i) {
+        const Step st = step_of(p, it, i);
         if (!mbar_wait(&full[stg.idx], stg.phase, abort_flag, p.error, 22)) goto done;
-        if (!mbar_wait(&acc_empty[acc.idx], acc.phase ^ 1, abort_flag, p.error, 23)) goto done;
+        // twin mode: the steps of sides 0 and 1 share one accumulator buffer (slots 0 and 1)
+        if ((!p.twin || st.side == 0) && !mbar_wait(&acc_empty[acc.idx], acc.phase ^ 1, abort_flag, p.error, 23))
+          goto done;
         tc_fence_after();
         if (lane == 0) {
           const uint32_t b_addr = smem_u32(smem + L::off_b + stg.idx * L::b_tile);
-          for (int g = 0; g < n_tiles; ++g) {
+          // twin mode: query tile 0 against this side's tile, into slot `side`; an empty tile issues nothing
+          const int g_first = p.twin ? st.side : 0;
+          const int g_end = p.twin ? (st.valid > 0 ? st.side + 1 : st.side) : n_tiles;
+          for (int g = g_first; g < g_end; ++g) {
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((acc.idx * kG + g) * kTileN);
-            const uint32_t ag = a_addr + static_cast<uint32_t>(g * L::a_tile);
+            const uint32_t ag = a_addr + static_cast<uint32_t>((p.twin ? 0 : g) * L::a_tile);
             if (kF16) {
               // 8 steps of K = 16 f16 (32 bytes): 4 per 128-byte K half, the halves 16 KB apart
 #pragma unroll
@@ -648,7 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         }
         __syncwarp();
         stg.next<L::stages>();
-        acc.next<kAccBufs>();
+        if (!p.twin || st.side == 1) acc.next<kAccBufs>();
       }
       if (lane == 0) mma_commit(&a_empty[abuf]);
       __syncwarp();
@@ -666,18 +748,24 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
     Ring stg, acc, mst;
     // Barrier among the epilogue warps around a document flush: an mbarrier with bounded waits, so a
-    // warp that gives up on a timeout never leaves the others waiting for good.
+    // warp that gives up on a timeout never leaves the others waiting for good.  In twin mode each
+    // group flushes its own unit's documents, with its own barrier and document-id slots.
+    uint64_t* const flush_bar = epi_bar + (p.twin ? g : 0);
+    int32_t* const gdoc = group_doc + (p.twin ? g * kSegGroup : 0);
+    const int ftid = p.twin ? etid - 128 * g : etid;            // thread index among the flushing threads
+    const int fthreads = p.twin ? 128 : kEpiWarps * 32;
     uint32_t epi_phase = 0;
     auto epi_sync = [&]() -> bool {
       __syncwarp();
-      if (lane == 0) mbar_arrive(epi_bar);
-      const bool ok = mbar_wait(epi_bar, epi_phase, abort_flag, p.error, 33);
+      if (lane == 0) mbar_arrive(flush_bar);
+      const bool ok = mbar_wait(flush_bar, epi_phase, abort_flag, p.error, 33);
       epi_phase ^= 1u;
       return ok;
     };
-    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
-      const Unit unit = p.units[u];
-      const int tile = unit.qpair * kG + g;
+    for (int w = blockIdx.x; w < p.num_items; w += gridDim.x) {
+      const Item it = load_item(p, w);
+      const Unit& unit = (p.twin && g) ? it.un[1] : it.un[0];
+      const int tile = p.twin ? 0 : unit.qpair * kG + g;  // twin mode: both groups score query tile 0
       // Rows of this warp's TMEM lane quarter that hold query tokens; a quarter without any (small
       // batches) skips its loads and arithmetic and only walks the document ends with the others.
       const int tile_rows = max(0, min(p.qpt, p.batch - tile * p.qpt)) * Q;
@@ -690,12 +778,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       const bool w_valid = wrow < p.qpt * Q && wb < p.batch;
       const float qs = w_valid ? __ldg(p.qscale + static_cast<int64_t>(wb) * Q + wrow % Q) : 0.0F;
       const int nq0 = max(0, min(p.qpt, p.batch - (unit.qpair * kG) * p.qpt));
-      const int nq1 = max(0, min(p.qpt, p.batch - (unit.qpair * kG + 1) * p.qpt));
+      const int nq1 = p.twin ? 0 : max(0, min(p.qpt, p.batch - (unit.qpair * kG + 1) * p.qpt));
       const int nq = nq0 + nq1;
       float run[4] = {kLowest, kLowest, kLowest, kLowest};                // open document, per row
       int32_t run_i[4] = {INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN};    // tensor-scale variant
       int pending = 0;
-      for (int64_t t0 = unit.tok_lo; t0 < unit.tok_hi; t0 += kTileN) {
+      for (int64_t si = 0; si < it.nsteps; ++si) {
+        const Step st = step_of(p, it, si);
+        if (p.twin && st.side != g) {
+          // the other group's tile: keep the rings in step without touching its barriers
+          stg.next<L::stages>();
+          if (st.side == 1) acc.next<kAccBufs>();
+          mst.next<kMeta>();
+          continue;
+        }
         if (!kPre && !mbar_wait(&tile_done[stg.idx], stg.phase, abort_flag, p.error, 31)) goto done;
         // Acquire the expanders' metadata writes for this tile (meta ring slot) and, with TMA operand
         // tiles, the completion of its MMAs (observed by expander warp 0 before it arrives).
@@ -704,7 +800,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + L::off_meta + mst.idx * kMetaBytes);
         const int valid = meta->valid;
         const int nseg = meta->nseg;
-        const bool last_tile = t0 + kTileN >= unit.tok_hi;
+        const bool last_tile = st.last;
         const uint32_t tbase = tmem_base + lane_base + static_cast<uint32_t>((acc.idx * kG + g) * kTileN);
         int sgi = 0;
         bool released = false;
@@ -887,7 +983,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               best = bi == INT32_MIN ? kLowest : __int2float_rn(bi);
             }
             if (w_store) rowval[(pending * kG + g) * 128 + wrow] = w_valid ? __fmul_rn(best, qs) : 0.0F;
-            if (etid == 0) group_doc[pending] = meta->seg_doc[sgi];
+            if (ftid == 0) gdoc[pending] = meta->seg_doc[sgi];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               run[i] = carry ? carry_max[i] : kLowest;
@@ -900,11 +996,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             ++sgi;
             if (++pending == kSegGroup || (sgi == nseg && last_tile)) {
               if (!epi_sync()) goto done;
-              for (int x = etid; x < pending * nq; x += kEpiWarps * 32) {
+              for (int x = ftid; x < pending * nq; x += fthreads) {
                 const int gd = x / nq, qx = x % nq;
                 const int gq = qx < nq0 ? 0 : 1;
                 const int qq = qx < nq0 ? qx : qx - nq0;
-                const float* rv = rowval + (gd * kG + gq) * 128 + qq * Q;
+                // twin mode: the group's own row values (slot g) of query tile 0
+                const float* rv = rowval + (gd * kG + (p.twin ? g : gq)) * 128 + qq * Q;
                 // row order as the reference sums; the loads are issued ahead of the dependent additions
                 float sacc = 0.0F;
                 int k = 0;
@@ -916,7 +1013,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                   for (int i = 0; i < 8; ++i) sacc = __fadd_rn(sacc, v[i]);
                 }
                 for (; k < Q; ++k) sacc = __fadd_rn(sacc, rv[k]);
-                p.out[static_cast<int64_t>((unit.qpair * kG + gq) * p.qpt + qq) * p.num_docs + group_doc[gd]] =
+                p.out[static_cast<int64_t>((unit.qpair * kG + gq) * p.qpt + qq) * p.num_docs + gdoc[gd]] =
                     __fmul_rn(sacc, p.scale);
               }
               if (!epi_sync()) goto done;
@@ -931,7 +1028,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           mbar_arrive(&m_empty[mst.idx]);
         }
         stg.next<L::stages>();
-        acc.next<kAccBufs>();
+        if (!p.twin || st.side == 1) acc.next<kAccBufs>();
         mst.next<kMeta>();
       }
     }
@@ -1277,6 +1374,9 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   prm.qscale = q.row_scale;
   prm.units = d_units;
   prm.num_units = num_units;
+  // One query tile: twin mode lets the two epilogue groups take two units' tiles in turn
+  prm.twin = pl.n_qtiles == 1 ? 1 : 0;
+  prm.num_items = prm.twin ? (num_units + 1) / 2 : num_units;
   prm.batch = q.batch;
   prm.qtok = q.qtok;
   prm.qpt = pl.qpt;
@@ -1284,7 +1384,7 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   prm.num_docs = d.num_docs;
   prm.out = out;
   prm.error = err;
-  const int grid = std::min<int>(sms, prm.num_units);
+  const int grid = std::min<int>(sms, prm.num_items);
   const bool digits = q.mode == kQueryF32;
   const bool f16 = !digits && d.format == kFormatInt4 && d.codes16 != nullptr && d.token_scale != nullptr;
   const bool pre = f16 || d.codes8 != nullptr;
