@@ -89,8 +89,7 @@ struct Params {
   const float* qscale;        // [B*Q]
   const Unit* units;
   int num_units;
-  int num_items;              // work items: units, or (twin) pairs of units
-  int twin;                   // one query tile: the two epilogue groups take two units' tiles in turn
+  int num_items;              // work items: units, or (twin mode) pairs of units
   int batch;
   int qtok;
   int qpt;                    // queries per tile
@@ -347,9 +346,10 @@ struct Item {
   int64_t nsteps;
 };
 __device__ __forceinline__ int64_t unit_tiles(const Unit& u) { return (u.tok_hi - u.tok_lo + kTileN - 1) / kTileN; }
+template <bool kTwin>
 __device__ __forceinline__ Item load_item(const Params& p, int w) {
   Item it;
-  if (p.twin) {
+  if (kTwin) {
     const Unit none{0, 0, 0, 0, 0, 0};
     it.un[0] = p.units[2 * w];
     it.un[1] = 2 * w + 1 < p.num_units ? p.units[2 * w + 1] : none;
@@ -367,11 +367,12 @@ struct Step {
   bool last;      // the unit's last tile
   int64_t t0;     // first token
 };
-__device__ __forceinline__ Step step_of(const Params& p, const Item& it, int64_t i) {
+template <bool kTwin>
+__device__ __forceinline__ Step step_of(const Item& it, int64_t i) {
   Step st;
-  st.side = p.twin ? static_cast<int>(i & 1) : 0;
-  const Unit& u = st.side ? it.un[1] : it.un[0];
-  st.t0 = u.tok_lo + (p.twin ? (i >> 1) : i) * kTileN;
+  st.side = kTwin ? static_cast<int>(i & 1) : 0;
+  const Unit& u = (kTwin && st.side) ? it.un[1] : it.un[0];
+  st.t0 = u.tok_lo + (kTwin ? (i >> 1) : i) * kTileN;
   const int64_t rem = u.tok_hi - st.t0;
   st.valid = rem <= 0 ? 0 : (rem < kTileN ? static_cast<int>(rem) : kTileN);
   st.last = rem > 0 && rem <= kTileN;
@@ -381,7 +382,9 @@ __device__ __forceinline__ Step step_of(const Params& p, const Item& it, int64_t
 // kDigits: fp32 queries as three int8 digit planes (split_query_digits_kernel).  Query row rho of a tile
 // (32 per tile) has its digit k on TMEM lane 32 (rho / 8) + 8 k + rho % 8 (k = 3: zeros), the four lanes
 // one epilogue thread holds, which combines them to d0 + 256 d1 + 65536 d2 before the scale and maximum.
-template <bool kTokenScale, bool kPre, bool kF16, bool kDigits = false>
+// kTwin: the pass has one query tile and runs in twin mode (see Item); a template parameter, so that the
+// passes with several query tiles compile to the plain one-unit loop.
+template <bool kTokenScale, bool kPre, bool kF16, bool kDigits = false, bool kTwin = false>
 __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap) {
   using L = Layout<kPre, kF16>;
   static_assert(!kF16 || (kPre && kTokenScale), "f16 operands come from the resident copy, with token scales");
@@ -421,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     }
     for (int s = 0; s < kMeta; ++s) {
       mbar_init(&m_full[s], kXWarps);
-      mbar_init(&m_empty[s], p.twin ? kEpiWarps / 2 : kEpiWarps);  // twin: only the owning group reads a tile
+      mbar_init(&m_empty[s], kTwin ? kEpiWarps / 2 : kEpiWarps);  // twin: only the owning group reads a tile
     }
     for (int s = 0; s < kRaw; ++s) {
       mbar_init(&raw_full[s], 1);
@@ -434,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       mbar_init(&u_full[a], 1);
       mbar_init(&u_empty[a], 1);
     }
-    if (p.twin) {
+    if (kTwin) {
       mbar_init(&epi_bar[0], kEpiWarps / 2);
       mbar_init(&epi_bar[1], kEpiWarps / 2);
     } else {
@@ -460,12 +463,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       Ring raw, stg;
       int iter = 0;
       for (int w = blockIdx.x; w < p.num_items; w += gridDim.x, ++iter) {
-        const Item it = load_item(p, w);
+        const Item it = load_item<kTwin>(p, w);
         // Each unit's offsets[d_lo .. d_hi] as a 16-byte-aligned superset (the buffer is padded): slots
         // alternate between items, or (twin mode) slot s holds side s.
-        for (int side = 0; side < (p.twin ? 2 : 1); ++side) {
-          const int ub = p.twin ? side : (iter & 1);
-          const int use = p.twin ? iter : (iter >> 1);  // earlier uses of the slot
+        for (int side = 0; side < (kTwin ? 2 : 1); ++side) {
+          const int ub = kTwin ? side : (iter & 1);
+          const int use = kTwin ? iter : (iter >> 1);  // earlier uses of the slot
           if (use >= 1 && !mbar_wait(&u_empty[ub], (use - 1) & 1, abort_flag, p.error, 41)) goto done;
           const Unit& unit = side ? it.un[1] : it.un[0];
           if (unit.d_hi > unit.d_lo) {
@@ -479,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           }
         }
         for (int64_t i = 0; i < it.nsteps; ++i) {
-          const Step st = step_of(p, it, i);
+          const Step st = step_of<kTwin>(it, i);
           const int64_t t0 = st.t0;
           const int valid = st.valid;
           if (kPre) {
@@ -516,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     Ring raw, stg, mst;
     int iter = 0;
     for (int w = blockIdx.x; w < p.num_items; w += gridDim.x, ++iter) {
-      const Item it = load_item(p, w);
+      const Item it = load_item<kTwin>(p, w);
       const int32_t qpair = it.un[0].qpair;  // twin mode: both units hold the one query tile
       const int abuf = iter % L::a_bufs;
       const int ause = iter / L::a_bufs;
@@ -573,17 +576,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         if (lane == 0) mbar_arrive(&a_full[abuf]);
       }
       if (xwarp == 0) {
-        for (int side = 0; side < (p.twin ? 2 : 1); ++side) {
-          const int ub = p.twin ? side : (iter & 1);
-          const int use = p.twin ? iter : (iter >> 1);
+        for (int side = 0; side < (kTwin ? 2 : 1); ++side) {
+          const int ub = kTwin ? side : (iter & 1);
+          const int use = kTwin ? iter : (iter >> 1);
           if (!mbar_wait(&u_full[ub], use & 1, abort_flag, p.error, 13)) goto done;
         }
       }
       int64_t next_doc0 = it.un[0].d_lo, next_doc1 = it.un[1].d_lo;  // first documents whose ends are ahead
       for (int64_t i = 0; i < it.nsteps; ++i) {
-        const Step st = step_of(p, it, i);
+        const Step st = step_of<kTwin>(it, i);
         const Unit& unit = st.side ? it.un[1] : it.un[0];
-        const int ub = p.twin ? st.side : (iter & 1);
+        const int ub = kTwin ? st.side : (iter & 1);
         const int64_t* uoff = reinterpret_cast<const int64_t*>(smem + L::off_uoff + ub * kUoffEntries * 8);
         const int64_t ufirst = unit.d_lo & ~1LL;
         const int64_t t0 = st.t0;
@@ -674,7 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         mst.next<kMeta>();
       }
       if (xwarp == 0 && lane == 0) {
-        for (int side = 0; side < (p.twin ? 2 : 1); ++side) mbar_arrive(&u_empty[p.twin ? side : (iter & 1)]);
+        for (int side = 0; side < (kTwin ? 2 : 1); ++side) mbar_arrive(&u_empty[kTwin ? side : (iter & 1)]);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -687,27 +690,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     Ring stg, acc;
     int iter = 0;
     for (int w = blockIdx.x; w < p.num_items; w += gridDim.x, ++iter) {
-      const Item it = load_item(p, w);
+      const Item it = load_item<kTwin>(p, w);
       const int abuf = iter % L::a_bufs;
       // query tiles of the pair that hold at least one query
       const int n_tiles = min(kG, (p.batch - it.un[0].qpair * kG * p.qpt + p.qpt - 1) / p.qpt);
       if (!mbar_wait(&a_full[abuf], (iter / L::a_bufs) & 1, abort_flag, p.error, 21)) goto done;
       const uint32_t a_addr = smem_u32(smem + L::off_a + abuf * kG * L::a_tile);
       for (int64_t i = 0; i < it.nsteps; ++i) {
-        const Step st = step_of(p, it, i);
+        const Step st = step_of<kTwin>(it, i);
         if (!mbar_wait(&full[stg.idx], stg.phase, abort_flag, p.error, 22)) goto done;
         // twin mode: the steps of sides 0 and 1 share one accumulator buffer (slots 0 and 1)
-        if ((!p.twin || st.side == 0) && !mbar_wait(&acc_empty[acc.idx], acc.phase ^ 1, abort_flag, p.error, 23))
+        if ((!kTwin || st.side == 0) && !mbar_wait(&acc_empty[acc.idx], acc.phase ^ 1, abort_flag, p.error, 23))
           goto done;
         tc_fence_after();
         if (lane == 0) {
           const uint32_t b_addr = smem_u32(smem + L::off_b + stg.idx * L::b_tile);
           // twin mode: query tile 0 against this side's tile, into slot `side`; an empty tile issues nothing
-          const int g_first = p.twin ? st.side : 0;
-          const int g_end = p.twin ? (st.valid > 0 ? st.side + 1 : st.side) : n_tiles;
+          const int g_first = kTwin ? st.side : 0;
+          const int g_end = kTwin ? (st.valid > 0 ? st.side + 1 : st.side) : n_tiles;
           for (int g = g_first; g < g_end; ++g) {
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((acc.idx * kG + g) * kTileN);
-            const uint32_t ag = a_addr + static_cast<uint32_t>((p.twin ? 0 : g) * L::a_tile);
+            const uint32_t ag = a_addr + static_cast<uint32_t>((kTwin ? 0 : g) * L::a_tile);
             if (kF16) {
               // 8 steps of K = 16 f16 (32 bytes): 4 per 128-byte K half, the halves 16 KB apart
 #pragma unroll
@@ -730,7 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         }
         __syncwarp();
         stg.next<L::stages>();
-        if (!p.twin || st.side == 1) acc.next<kAccBufs>();
+        if (!kTwin || st.side == 1) acc.next<kAccBufs>();
       }
       if (lane == 0) mma_commit(&a_empty[abuf]);
       __syncwarp();
@@ -750,10 +753,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     // Barrier among the epilogue warps around a document flush: an mbarrier with bounded waits, so a
     // warp that gives up on a timeout never leaves the others waiting for good.  In twin mode each
     // group flushes its own unit's documents, with its own barrier and document-id slots.
-    uint64_t* const flush_bar = epi_bar + (p.twin ? g : 0);
-    int32_t* const gdoc = group_doc + (p.twin ? g * kSegGroup : 0);
-    const int ftid = p.twin ? etid - 128 * g : etid;            // thread index among the flushing threads
-    const int fthreads = p.twin ? 128 : kEpiWarps * 32;
+    uint64_t* const flush_bar = epi_bar + (kTwin ? g : 0);
+    int32_t* const gdoc = group_doc + (kTwin ? g * kSegGroup : 0);
+    const int ftid = kTwin ? etid - 128 * g : etid;            // thread index among the flushing threads
+    const int fthreads = kTwin ? 128 : kEpiWarps * 32;
     uint32_t epi_phase = 0;
     auto epi_sync = [&]() -> bool {
       __syncwarp();
@@ -763,9 +766,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       return ok;
     };
     for (int w = blockIdx.x; w < p.num_items; w += gridDim.x) {
-      const Item it = load_item(p, w);
-      const Unit& unit = (p.twin && g) ? it.un[1] : it.un[0];
-      const int tile = p.twin ? 0 : unit.qpair * kG + g;  // twin mode: both groups score query tile 0
+      const Item it = load_item<kTwin>(p, w);
+      const Unit& unit = (kTwin && g) ? it.un[1] : it.un[0];
+      const int tile = kTwin ? 0 : unit.qpair * kG + g;  // twin mode: both groups score query tile 0
       // Rows of this warp's TMEM lane quarter that hold query tokens; a quarter without any (small
       // batches) skips its loads and arithmetic and only walks the document ends with the others.
       const int tile_rows = max(0, min(p.qpt, p.batch - tile * p.qpt)) * Q;
@@ -778,14 +781,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       const bool w_valid = wrow < p.qpt * Q && wb < p.batch;
       const float qs = w_valid ? __ldg(p.qscale + static_cast<int64_t>(wb) * Q + wrow % Q) : 0.0F;
       const int nq0 = max(0, min(p.qpt, p.batch - (unit.qpair * kG) * p.qpt));
-      const int nq1 = p.twin ? 0 : max(0, min(p.qpt, p.batch - (unit.qpair * kG + 1) * p.qpt));
+      const int nq1 = kTwin ? 0 : max(0, min(p.qpt, p.batch - (unit.qpair * kG + 1) * p.qpt));
       const int nq = nq0 + nq1;
       float run[4] = {kLowest, kLowest, kLowest, kLowest};                // open document, per row
       int32_t run_i[4] = {INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN};    // tensor-scale variant
       int pending = 0;
       for (int64_t si = 0; si < it.nsteps; ++si) {
-        const Step st = step_of(p, it, si);
-        if (p.twin && st.side != g) {
+        const Step st = step_of<kTwin>(it, si);
+        if (kTwin && st.side != g) {
           // the other group's tile: keep the rings in step without touching its barriers
           stg.next<L::stages>();
           if (st.side == 1) acc.next<kAccBufs>();
@@ -1001,7 +1004,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 const int gq = qx < nq0 ? 0 : 1;
                 const int qq = qx < nq0 ? qx : qx - nq0;
                 // twin mode: the group's own row values (slot g) of query tile 0
-                const float* rv = rowval + (gd * kG + (p.twin ? g : gq)) * 128 + qq * Q;
+                const float* rv = rowval + (gd * kG + (kTwin ? g : gq)) * 128 + qq * Q;
                 // row order as the reference sums; the loads are issued ahead of the dependent additions
                 float sacc = 0.0F;
                 int k = 0;
@@ -1028,7 +1031,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           mbar_arrive(&m_empty[mst.idx]);
         }
         stg.next<L::stages>();
-        if (!p.twin || st.side == 1) acc.next<kAccBufs>();
+        if (!kTwin || st.side == 1) acc.next<kAccBufs>();
         mst.next<kMeta>();
       }
     }
@@ -1375,8 +1378,8 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   prm.units = d_units;
   prm.num_units = num_units;
   // One query tile: twin mode lets the two epilogue groups take two units' tiles in turn
-  prm.twin = pl.n_qtiles == 1 ? 1 : 0;
-  prm.num_items = prm.twin ? (num_units + 1) / 2 : num_units;
+  const bool twin = pl.n_qtiles == 1;
+  prm.num_items = twin ? (num_units + 1) / 2 : num_units;
   prm.batch = q.batch;
   prm.qtok = q.qtok;
   prm.qpt = pl.qpt;
@@ -1393,26 +1396,31 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   const CUtensorMap tmap = f16   ? make_operand_map(d.codes16, d.num_tokens, true)
                            : pre ? make_operand_map(d.codes8, d.num_tokens, false)
                                  : CUtensorMap{};
-  auto go = [&](auto kernel, int smem_bytes) {
+  auto go = [&](auto plain, auto twin_kernel, int smem_bytes) {
+    auto kernel = twin ? twin_kernel : plain;
     check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes), "set tc smem");
     kernel<<<grid, tc::kThreads, smem_bytes, stream>>>(prm, tmap);
   };
+  using LayoutF16 = tc::Layout<true, true>;
+#define MSB_TC_GO(TS, PRE, F16, DIG, LAYOUT) \
+  go(tc::tc_scan_kernel<TS, PRE, F16, DIG, false>, tc::tc_scan_kernel<TS, PRE, F16, DIG, true>, LAYOUT::bytes)
   if (digits) {
     if (d.token_scale) {
-      if (pre) go(tc::tc_scan_kernel<true, true, false, true>, tc::Layout<true>::bytes);
-      else go(tc::tc_scan_kernel<true, false, false, true>, tc::Layout<false>::bytes);
+      if (pre) MSB_TC_GO(true, true, false, true, tc::Layout<true>);
+      else MSB_TC_GO(true, false, false, true, tc::Layout<false>);
     } else {
-      if (pre) go(tc::tc_scan_kernel<false, true, false, true>, tc::Layout<true>::bytes);
-      else go(tc::tc_scan_kernel<false, false, false, true>, tc::Layout<false>::bytes);
+      if (pre) MSB_TC_GO(false, true, false, true, tc::Layout<true>);
+      else MSB_TC_GO(false, false, false, true, tc::Layout<false>);
     }
   } else if (d.token_scale) {
-    if (f16) go(tc::tc_scan_kernel<true, true, true>, tc::Layout<true, true>::bytes);
-    else if (pre) go(tc::tc_scan_kernel<true, true, false>, tc::Layout<true>::bytes);
-    else go(tc::tc_scan_kernel<true, false, false>, tc::Layout<false>::bytes);
+    if (f16) MSB_TC_GO(true, true, true, false, LayoutF16);
+    else if (pre) MSB_TC_GO(true, true, false, false, tc::Layout<true>);
+    else MSB_TC_GO(true, false, false, false, tc::Layout<false>);
   } else {
-    if (pre) go(tc::tc_scan_kernel<false, true, false>, tc::Layout<true>::bytes);
-    else go(tc::tc_scan_kernel<false, false, false>, tc::Layout<false>::bytes);
+    if (pre) MSB_TC_GO(false, true, false, false, tc::Layout<true>);
+    else MSB_TC_GO(false, false, false, false, tc::Layout<false>);
   }
+#undef MSB_TC_GO
   count_launch();
   check(cudaGetLastError(), "launch tensor-core scan kernel");
 }
