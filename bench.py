@@ -50,10 +50,10 @@ SEED = 20260713
 CHUNK_PAGES = 2_000
 # DRAM bytes (read + write) of one tc_scan_kernel launch per corpus page, from one ncu capture of a
 # 2,000-page case of the same workload (profiles/tc_scan_kernel_2000pages_full.txt: 272.32 MB read +
-# 4.21 MB written).  The kernel streams the resident int8 copy of the codes (128 B per token, twice
+# 4.56 MB written).  The kernel streams the resident int8 copy of the codes (128 B per token, twice
 # the int4 bytes) plus the token scales once per launch and the score matrix grows with the pages,
 # so traffic scales with the pages a rank holds.
-TC_DRAM_BYTES_PER_PAGE = (272.315136e6 + 4.212480e6) / 2000
+TC_DRAM_BYTES_PER_PAGE = (272.316416e6 + 4.558080e6) / 2000
 WORKLOAD = ("C4: 100,000 pages x 1,030 tokens (dim 128) per-token int4 (6.59 GB codes + 0.41 GB scales); "
             "1,024 queries x 24 tokens int8, batch 64, full-scan top-10")
 
