@@ -18,7 +18,7 @@ namespace msb {
 void launch_simt_scan(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, bool, float*,
                       cudaStream_t);
 void launch_quantize_rows(const float*, int64_t, int, int8_t*, float*, int32_t*, int32_t*, bool, cudaStream_t);
-void launch_split_query_digits(const float*, int64_t, int32_t*, float*, cudaStream_t);
+void launch_split_query_digits(const float*, int64_t, int32_t*, float*, const float*, int, int, cudaStream_t);
 void launch_topk_rows(const float*, int64_t, int, int64_t, int, const int64_t*, bool, float*, int64_t*, cudaStream_t);
 void launch_pack_int4(const float*, int64_t, int, bool, uint8_t*, float*, float*, void*, cudaStream_t);
 void launch_pack_signs(const float*, int64_t, int, uint8_t*, float*, cudaStream_t);
@@ -354,7 +354,10 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
       // fp32 queries: three int8 digit planes and a power-of-two scale per row
       h->w_qwords.ensure(static_cast<size_t>(rows) * 3 * h->dim, "cudaMalloc query digit planes");
       h->w_qscale.ensure(static_cast<size_t>(rows) * sizeof(float), "cudaMalloc query digit scales");
-      launch_split_query_digits(d_query, rows, h->w_qwords.as<int32_t>(), h->w_qscale.as<float>(), stream);
+      const bool weighted = r.red.reducer == kWeighted;
+      launch_split_query_digits(d_query, rows, h->w_qwords.as<int32_t>(), h->w_qscale.as<float>(),
+                                weighted ? r.red.weights : nullptr, qtok, weighted ? r.red.weights_batched : 0,
+                                stream);
       qv.i8_words = h->w_qwords.as<int32_t>();
       qv.row_scale = h->w_qscale.as<float>();
     }

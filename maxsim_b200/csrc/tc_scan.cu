@@ -1175,9 +1175,13 @@ __global__ void expand_binary8_kernel(const uint8_t* __restrict__ in, int64_t n_
 // the even dims' bytes, then the odd dims'), plane k at words + k * rows * 32.  The scan's dot of plane
 // k with a token is an exact int32; the three combine to the exact dot of q, and qscale = 2^-S (a power
 // of two, exact) brings it back to the query's scale.  A row of zeros has S = 0; a row holding a
-// non-finite value gets qscale NaN, so its scores are NaN.
+// non-finite value gets qscale NaN, so its scores are NaN.  Weighted MaxSim folds the row's weight in:
+// qscale = w * 2^-S is exact (a power-of-two scaling of w, unless it leaves the normal range), so the
+// epilogue's fl(best' * qscale), best' = best * 2^S, is fl(best * w).  weights: [qtok], or [rows] when
+// weights_batched, or nullptr.
 __global__ void split_query_digits_kernel(const float* __restrict__ q, int64_t rows, int32_t* __restrict__ words,
-                                          float* __restrict__ qscale) {
+                                          float* __restrict__ qscale, const float* __restrict__ weights, int qtok,
+                                          int weights_batched) {
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -1218,15 +1222,19 @@ __global__ void split_query_digits_kernel(const float* __restrict__ q, int64_t r
     const uint32_t odd = __byte_perm(first, second, 0x7531);
     words[(static_cast<int64_t>(k) * rows + row) * 32 + lane] = static_cast<int32_t>((lane & 1) ? odd : even);
   }
-  if (lane == 0) qscale[row] = finite ? ldexpf(1.0F, -S) : __int_as_float(0x7FC00000);
+  if (lane == 0) {
+    const float w = weights ? weights[weights_batched ? row : row % qtok] : 1.0F;
+    qscale[row] = finite ? ldexpf(w, -S) : __int_as_float(0x7FC00000);
+  }
 }
 }  // namespace tc
 
-void launch_split_query_digits(const float* q, int64_t rows, int32_t* words, float* qscale, cudaStream_t stream) {
+void launch_split_query_digits(const float* q, int64_t rows, int32_t* words, float* qscale, const float* weights,
+                               int qtok, int weights_batched, cudaStream_t stream) {
   if (rows <= 0) return;
   const int64_t threads = rows * 32;
-  tc::split_query_digits_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(q, rows, words,
-                                                                                                  qscale);
+  tc::split_query_digits_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+      q, rows, words, qscale, weights, qtok, weights_batched);
   count_launch();
   check(cudaGetLastError(), "launch query digit-split kernel");
 }
@@ -1294,7 +1302,9 @@ bool tc_scan_supported(const DocsView& d, const QueryView& q, const ReduceView& 
                            : (q.mode == kQueryF32 && q.qtok <= 32 && (reinterpret_cast<uintptr_t>(q.f32) & 15) == 0);
   // binary corpora: a scalar document scale (the epilogue's one factor), read from the resident +-1 copy
   const bool format_ok = d.format == kFormatInt4 || (d.format == kFormatBinary && d.doc_scale == nullptr);
-  return !residual && format_ok && d.dim == 128 && mode_ok && r.reducer == kMaxSim && tg.ids == nullptr &&
+  // weighted MaxSim of fp32 queries: the weights fold into the digit planes' row scales
+  const bool reducer_ok = r.reducer == kMaxSim || (r.reducer == kWeighted && q.mode == kQueryF32);
+  return !residual && format_ok && d.dim == 128 && mode_ok && reducer_ok && tg.ids == nullptr &&
          q.qtok >= 1 && q.batch >= 1 && d.num_docs <= 0x7FFFFFFF && d.host_offsets != nullptr;
 }
 

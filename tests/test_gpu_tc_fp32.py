@@ -41,10 +41,14 @@ def _digits(q):
     return np.stack([d0, d1, d2]), np.ldexp(np.float32(1), -s).astype(np.float32)
 
 
-def _digit_model(query, values, offsets, scale, token_scale):
-    """The engine's arithmetic for [B, Q, 128] fp32 queries against int4 values [N, 128]."""
+def _digit_model(query, values, offsets, scale, token_scale, weights=None):
+    """The engine's arithmetic for [B, Q, 128] fp32 queries against int4 values [N, 128]; weighted
+    MaxSim folds each row's weight into its power-of-two scale (exact)."""
     B, Q, _ = query.shape
     digits, qscale = _digits(query.reshape(-1, 128))
+    if weights is not None:
+        w = np.broadcast_to(np.asarray(weights, np.float32), (B, Q)).reshape(-1)
+        qscale = np.ldexp(w, np.frexp(qscale)[1] - 1).astype(np.float32)  # w * 2^-S
     vals = values.astype(np.int64)
     dots = np.einsum("kri,ti->krt", digits, vals)  # exact integers
     lo = (dots[0] + 256 * dots[1]).astype(np.float32)
@@ -93,6 +97,37 @@ def test_digit_planes_bit_exact_and_within_oracle(engine, gran, batch, qtok):
     s, i = m.topk_int4_maxsim(q, dev, 10)
     for row in range(batch):
         np.testing.assert_array_equal(s[row], np.sort(got[row])[::-1][:10])
+
+
+@pytest.mark.parametrize("batched", [False, True])
+@pytest.mark.parametrize("binary", [False, True])
+def test_weighted_maxsim_on_digit_planes(engine, batched, binary):
+    """Weighted MaxSim of fp32 queries: the row weights fold into the digit planes' row scales."""
+    import maxsim_b200 as m
+
+    docs, off = _corpus(200, 240, seed=31)
+    q = ref.clustered_queries(docs, off, 3, 24, seed=32)
+    rng = np.random.default_rng(33)
+    w = rng.uniform(0.25, 2.0, size=(3, 24) if batched else 24).astype(np.float32)
+    if binary:
+        packed, h = _binary(docs, off, True)
+        values = ref.unpack_signs(packed.data, 128).astype(np.int64)
+        ts, scale = np.asarray(packed.token_scale, np.float32), 1.0
+        run = lambda: h.score_batch(q, reducer="weighted_maxsim", query_weights=w, use_token_scale=True)
+        exact = ref.score_binary_fp32(q, packed.data, 128, off, token_scale=ts, reducer="weighted_maxsim", weights=w)
+    else:
+        packed = m.pack_int4_symmetric(docs, off, scale_granularity="token")
+        dev = m.int4_to_device(packed)
+        values, ts, scale = packed.values, packed.token_scale, packed.scale
+        run = lambda: m.int4_maxsim(q, dev, reducer="weighted_maxsim", query_weights=w)
+        exact = ref.score_int4_fp32(q, packed.values, off, scale=scale, token_scale=ts, reducer="weighted_maxsim",
+                                    weights=w)
+    engine.set_engine(2)
+    got = run()
+    np.testing.assert_array_equal(got, _digit_model(q, values, off, scale, ts, weights=w))
+    np.testing.assert_allclose(got, exact, rtol=2e-6, atol=2e-6 * np.abs(exact).max())
+    engine.set_engine(1)
+    np.testing.assert_allclose(run(), got, rtol=1e-5, atol=1e-5 * np.abs(exact).max())
 
 
 def test_digit_planes_extreme_row_magnitudes(engine):
