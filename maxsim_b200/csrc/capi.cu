@@ -145,6 +145,10 @@ struct msb_docs {
   // hold the exact integer dot, so the epilogue converts nothing.
   DeviceBuf codes16;
   bool codes16_failed = false;
+  // The residual stream's int4 codes expanded like codes8, for the tensor-core residual scan; released
+  // whenever the residual stream is replaced or cleared.
+  DeviceBuf codes2_8;
+  bool codes2_8_failed = false;
   // Streaming upload (msb_docs_create_for_upload .. msb_docs_upload_finish): scoring is refused while
   // open; each queued copy records an event in a small ring that its ticket names.
   static constexpr int kUploadEvents = 16;
@@ -156,8 +160,8 @@ struct msb_docs {
 
   size_t bytes_per_token() const { return format == kFormatInt4 ? dim / 2 : dim / 8; }
   int64_t resident_bytes() const {
-    return static_cast<int64_t>(codes.cap + codes8.cap + codes16.cap + offsets.cap + token_scale.cap + doc_scale.cap + residual_codes.cap +
-                                residual_token_scale.cap);
+    return static_cast<int64_t>(codes.cap + codes8.cap + codes16.cap + codes2_8.cap + offsets.cap + token_scale.cap +
+                                doc_scale.cap + residual_codes.cap + residual_token_scale.cap);
   }
   int64_t workspace_bytes() const {
     return static_cast<int64_t>(w_query.cap + w_qcodes.cap + w_qwords.cap + w_qscale.cap + w_qsum.cap +
@@ -172,7 +176,7 @@ struct msb_docs {
     DeviceBuf* all[] = {&codes,   &offsets,  &token_scale, &doc_scale, &residual_codes, &residual_token_scale,
                         &w_query, &w_qcodes, &w_qwords,    &w_qscale,  &w_qsum,         &w_scores,
                         &w_cands, &w_weights, &w_top_s,    &w_top_i,   &w_override,     &w_fine,
-                        &w_tc,    &codes8,   &codes16,   &w_check};
+                        &w_tc,    &codes8,   &codes16,   &w_check,        &codes2_8};
     for (DeviceBuf* b : all) b->release();
     for (cudaEvent_t& e : upload_events)
       if (e) cudaEventDestroy(e);
@@ -296,7 +300,8 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
     // the int8 copy (int4 expanded, or +-1 for sign codes).  int4 corpora fall back to expanding per
     // tile when there is no memory for a copy; binary corpora fall back to the SIMT engine.
     const bool binary = h->format == kFormatBinary;
-    if (!binary && g_tc_f16_cache.load() && !h->codes16_failed && dv.token_scale && tc_int8_cache_supported(dv)) {
+    if (!binary && !r.residual && g_tc_f16_cache.load() && !h->codes16_failed && dv.token_scale &&
+        tc_int8_cache_supported(dv)) {
       if (!h->codes16.ptr) {
         const size_t bytes = static_cast<size_t>(h->num_tokens) * 256;
         void* p = nullptr;
@@ -312,7 +317,8 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
       }
       if (h->codes16.ptr) dv.codes16 = static_cast<const uint16_t*>(h->codes16.ptr);
     }
-    if (!dv.codes16 && (binary || g_tc_int8_cache.load()) && !h->codes8_failed && tc_int8_cache_supported(dv)) {
+    if (!dv.codes16 && (binary || r.residual || g_tc_int8_cache.load()) && !h->codes8_failed &&
+        tc_int8_cache_supported(dv)) {
       if (!h->codes8.ptr) {
         const size_t bytes = static_cast<size_t>(h->num_tokens) * 128;
         void* p = nullptr;
@@ -331,6 +337,26 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
     if (binary && !dv.codes8) {
       if (engine == 2) throw NotSupported("no device memory for the tensor-core engine's int8 copy of the sign codes");
       use_tc = false;
+    }
+    if (r.residual) {
+      // the fused residual stream reads int8 copies of both streams; without them, the SIMT engine
+      if (dv.codes8 && !h->codes2_8.ptr && !h->codes2_8_failed) {
+        const size_t bytes = static_cast<size_t>(h->num_tokens) * 128;
+        void* p = nullptr;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) {
+          (void)cudaGetLastError();
+          h->codes2_8_failed = true;
+        } else {
+          h->codes2_8.ptr = p;
+          h->codes2_8.cap = bytes;
+          launch_expand_codes8(h->residual_codes.as<uint8_t>(), h->num_tokens, h->codes2_8.as<uint8_t>(), stream);
+        }
+      }
+      if (h->codes2_8.ptr) dv.codes2_8 = h->codes2_8.as<uint8_t>();
+      if (!dv.codes8 || !dv.codes2_8) {
+        if (engine == 2) throw NotSupported("no device memory for the tensor-core engine's int8 copies of the streams");
+        use_tc = false;
+      }
     }
   }
   const int64_t rows = static_cast<int64_t>(batch) * qtok;
@@ -680,7 +706,7 @@ int msb_docs_set_residual(msb_docs* h, const uint8_t* codes, int64_t num_tokens,
     const size_t cbytes = static_cast<size_t>(h->dim / 2) * static_cast<size_t>(num_tokens);  // int4 residual
     const size_t sbytes = sizeof(float) * static_cast<size_t>(num_tokens);
     h->residual_codes.ensure(cbytes > 0 ? cbytes : 4, "cudaMalloc resident int4 residual data");
-    h->residual_token_scale.ensure(sbytes > 0 ? sbytes : 4, "cudaMalloc resident int4 residual token scales");
+    h->residual_token_scale.ensure(sbytes + kTailPad, "cudaMalloc resident int4 residual token scales");
     if (cbytes)
       check(cudaMemcpyAsync(h->residual_codes.ptr, codes, cbytes, cudaMemcpyHostToDevice, h->stream),
             "copy int4 residual data to device");
@@ -689,6 +715,8 @@ int msb_docs_set_residual(msb_docs* h, const uint8_t* codes, int64_t num_tokens,
             "copy int4 residual token scales to device");
     check(cudaStreamSynchronize(h->stream), "synchronize residual upload");
     h->residual_scale = scale;
+    h->codes2_8.release();  // the int8 copy of the previous residual stream
+    h->codes2_8_failed = false;
     h->has_residual = true;
   });
 }
@@ -716,7 +744,7 @@ int msb_docs_create_for_upload(int32_t format, int32_t dim, int64_t num_tokens, 
       if (flags & MSB_UPLOAD_RESIDUAL) {
         const size_t rbytes = static_cast<size_t>(dim / 2) * n;
         h->residual_codes.ensure(rbytes > 0 ? rbytes : 4, "cudaMalloc resident int4 residual data");
-        h->residual_token_scale.ensure(n > 0 ? sizeof(float) * n : 4, "cudaMalloc resident int4 residual token scales");
+        h->residual_token_scale.ensure(sizeof(float) * n + kTailPad, "cudaMalloc resident int4 residual token scales");
       }
       for (cudaEvent_t& e : h->upload_events)
         check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "create upload event");
@@ -818,6 +846,8 @@ int msb_docs_upload_finish(msb_docs* h, float residual_scale) {
     h->has_token_scale = (h->upload_flags & MSB_UPLOAD_TOKEN_SCALES) != 0;
     if (residual) {
       h->residual_scale = residual_scale;
+      h->codes2_8.release();  // the int8 copy of the previous residual stream
+      h->codes2_8_failed = false;
       h->has_residual = true;
     }
     h->upload_open = false;
@@ -842,6 +872,8 @@ int msb_pinned_free(void* ptr) {
 int msb_docs_clear_residual(msb_docs* h) {
   return guarded([&] {
     if (!h) throw InvalidArgument("handle is NULL");
+    h->codes2_8.release();  // the int8 copy of the previous residual stream
+    h->codes2_8_failed = false;
     h->has_residual = false;
   });
 }

@@ -52,6 +52,7 @@ struct DocsView {
   uint64_t corpus_id;          // unique per resident corpus (keys host-side caches)
   const uint8_t* codes8;       // int4 codes expanded to int8 in scan K order [N, 128], or nullptr
   const uint16_t* codes16;     // the same as f16 values [N, 128], or nullptr (tensor-core f16 operands)
+  const uint8_t* codes2_8;     // the residual stream expanded to int8 like codes8, or nullptr
   int64_t num_docs;
   int64_t num_tokens;
   int dim;

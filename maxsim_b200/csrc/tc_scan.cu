@@ -93,7 +93,10 @@ struct Params {
   int batch;
   int qtok;
   int qpt;                    // queries per tile
-  float scale;                // tensor scale applied to the document score
+  float scale;                // tensor scale applied to the document score (1 for the residual stream)
+  const float* token_scale2;  // residual stream (kRes): per-token scales of the second stream
+  float res_scale1;           // residual stream: the prefix's and the residual's scalar scales
+  float res_scale2;
   int64_t num_docs;           // output row stride
   float* out;                 // [B, num_docs]
   int* error;                 // set to a non-zero code on timeout
@@ -127,26 +130,31 @@ constexpr int kRowBytes = kSegGroup * kG * 128 * 4;    // [group][query tile][ro
 // bound by DRAM latency (few query tiles, so little work per tile).
 // With f16 operands (kF16, from the resident f16 copy) each operand tile is twice as large (two 128-byte
 // swizzled K halves of 64 values) and the query tiles are single-buffered to keep 4 B stages.
-template <bool kPre, bool kF16 = false>
+// With the residual stream (kRes) each B stage holds two operand tiles (prefix, then residual), the raw
+// ring two scale vectors, and a second scale array per meta slot sits after the meta ring.
+template <bool kPre, bool kF16 = false, bool kRes = false>
 struct Layout {
-  static constexpr int stages = kF16 ? 4 : (kPre ? 8 : 4);  // B ring, released by the MMA commit
+  static constexpr int stages = (kF16 || kRes) ? 4 : (kPre ? 8 : 4);  // B ring, released by the MMA commit
   static constexpr int a_tile = kF16 ? 2 * kATileBytes : kATileBytes;
-  static constexpr int b_tile = kF16 ? 2 * kBTileBytes : kBTileBytes;
-  static constexpr int a_bufs = kF16 ? 1 : 2;
+  static constexpr int b_tile = (kF16 || kRes) ? 2 * kBTileBytes : kBTileBytes;
+  static constexpr int a_bufs = (kF16 || kRes) ? 1 : 2;
   static constexpr int raw_code_bytes = kPre ? 0 : kRawCodeBytes;
-  static constexpr int raw_bytes = ((raw_code_bytes + kRawScaleFloats * 4 + 127) / 128) * 128;
+  static constexpr int raw_scale_bytes = kRawScaleFloats * 4;  // one vector (16-byte multiple)
+  static constexpr int raw_bytes = ((raw_code_bytes + (kRes ? 2 : 1) * raw_scale_bytes + 127) / 128) * 128;
   static constexpr int off_a = 0;                        // [a_bufs][kG] query tiles
   static constexpr int off_b = off_a + a_bufs * kG * a_tile;
   static constexpr int off_raw = off_b + stages * b_tile;
   static constexpr int off_meta = off_raw + kRaw * raw_bytes;
-  static constexpr int off_uoff = off_meta + kMeta * kMetaBytes;
+  static constexpr int off_scale2 = off_meta + kMeta * kMetaBytes;  // [kMeta][160] (kRes)
+  static constexpr int off_uoff = off_scale2 + (kRes ? kMeta * 160 * 4 : 0);
   static constexpr int off_row = off_uoff + 2 * kUoffEntries * 8;
   static constexpr int off_bar = off_row + kRowBytes + 128;  // + per-group doc ids
   static constexpr int num_bars = 2 * stages + 2 * kMeta + 2 * kRaw + kAccBufs + 10;
   static constexpr int bytes = off_bar + num_bars * 8 + 64 + 1024;  // + alignment slack
   static_assert(bytes <= 227 * 1024, "shared memory budget");
   static_assert(off_b % 1024 == 0 && b_tile % 1024 == 0 && a_tile % 1024 == 0, "128-byte-swizzled operand tiles");
-  static_assert(off_uoff % 16 == 0 && off_raw % 16 == 0 && raw_bytes % 16 == 0, "bulk-copy alignment");
+  static_assert(off_uoff % 16 == 0 && off_raw % 16 == 0 && raw_bytes % 16 == 0 && raw_scale_bytes % 16 == 0,
+                "bulk-copy alignment");
 };
 
 // ---------------------------------------------------------------------------
@@ -384,9 +392,17 @@ __device__ __forceinline__ Step step_of(const Item& it, int64_t i) {
 // one epilogue thread holds, which combines them to d0 + 256 d1 + 65536 d2 before the scale and maximum.
 // kTwin: the pass has one query tile and runs in twin mode (see Item); a template parameter, so that the
 // passes with several query tiles compile to the plain one-unit loop.
-template <bool kTokenScale, bool kPre, bool kF16, bool kDigits = false, bool kTwin = false>
-__global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap) {
-  using L = Layout<kPre, kF16>;
+// kRes: the fused two-stream residual (fp32 queries as digit planes, per-token scales on both streams):
+// per token tile the prefix tile (tmap) and the residual tile (tmap2) each get an accumulator per query
+// tile, so one accumulator buffer fills the 512 TMEM columns; the epilogue forms
+// fl(fl(fl(v1 * scale1) * s1) + fl(fl(v2 * scale2) * s2)) before the maximum.
+template <bool kTokenScale, bool kPre, bool kF16, bool kDigits = false, bool kTwin = false, bool kRes = false>
+__global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap,
+                                                              const __grid_constant__ CUtensorMap tmap2) {
+  using L = Layout<kPre, kF16, kRes>;
+  static_assert(!kRes || (kPre && kDigits && kTokenScale && !kF16), "the residual stream reads both int8 copies");
+  constexpr int kAcc = kRes ? 1 : kAccBufs;         // accumulator buffers
+  constexpr int kStreams = kRes ? 2 : 1;            // accumulators per query tile
   static_assert(!kF16 || (kPre && kTokenScale), "f16 operands come from the resident copy, with token scales");
   static_assert(!(kF16 && kDigits), "digit-plane queries use int8 operands");
   constexpr bool kFloat = kTokenScale || kDigits;  // row maxima in fp32; int32 for the tensor-scale dots
@@ -494,6 +510,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               tma_load_2d(bdst, &tmap, 0, static_cast<int>(t0), &full[stg.idx]);
               // f16: the second K half (values 64..127, byte 128 of each row: x * 2 B is 16-byte aligned)
               if (kF16) tma_load_2d(bdst + kBTileBytes, &tmap, 64, static_cast<int>(t0), &full[stg.idx]);
+              // residual stream: the same tokens of the residual int8 copy
+              if (kRes) tma_load_2d(bdst + kBTileBytes, &tmap2, 0, static_cast<int>(t0), &full[stg.idx]);
             } else {
               mbar_arrive(&full[stg.idx]);  // an empty tile: nothing to load
             }
@@ -505,9 +523,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           uint32_t scale_bytes = 0;
           const int64_t s_first = t0 & ~3LL;
           if (kTokenScale && valid > 0) scale_bytes = static_cast<uint32_t>(((t0 + valid - s_first + 3) & ~3LL) * 4);
-          mbar_expect_tx(&raw_full[raw.idx], code_bytes + scale_bytes);
+          mbar_expect_tx(&raw_full[raw.idx], code_bytes + (kRes ? 2 : 1) * scale_bytes);
           if (code_bytes) bulk_g2s(rb, p.codes + t0 * 64, code_bytes, &raw_full[raw.idx]);
           if (scale_bytes) bulk_g2s(rb + L::raw_code_bytes, p.token_scale + s_first, scale_bytes, &raw_full[raw.idx]);
+          if (kRes && scale_bytes)
+            bulk_g2s(rb + L::raw_code_bytes + L::raw_scale_bytes, p.token_scale2 + s_first, scale_bytes,
+                     &raw_full[raw.idx]);
           raw.next<kRaw>();
         }
       }
@@ -600,6 +621,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         if (kPre && kTokenScale) {
           const float* rs = reinterpret_cast<const float*>(rb + L::raw_code_bytes);
           for (int r = xtid; r < valid; r += kXWarps * 32) meta->scale[scale_slot(r)] = rs[(t0 & 3) + r];
+          if (kRes) {
+            const float* rs2 = reinterpret_cast<const float*>(rb + L::raw_code_bytes + L::raw_scale_bytes);
+            float* sc2 = reinterpret_cast<float*>(smem + L::off_scale2 + mst.idx * 160 * 4);
+            for (int r = xtid; r < valid; r += kXWarps * 32) sc2[scale_slot(r)] = rs2[(t0 & 3) + r];
+          }
         }
 #pragma unroll 1
         for (int r = xtid; r < (kPre ? 0 : valid); r += kXWarps * 32) {  // tokens of the tile
@@ -709,7 +735,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           const int g_first = kTwin ? st.side : 0;
           const int g_end = kTwin ? (st.valid > 0 ? st.side + 1 : st.side) : n_tiles;
           for (int g = g_first; g < g_end; ++g) {
-            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((acc.idx * kG + g) * kTileN);
+            // accumulator of (query tile g, stream 0); the residual stream's follows it
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((acc.idx * kG + g) * kStreams * kTileN);
             const uint32_t ag = a_addr + static_cast<uint32_t>((kTwin ? 0 : g) * L::a_tile);
             if (kF16) {
               // 8 steps of K = 16 f16 (32 bytes): 4 per 128-byte K half, the halves 16 KB apart
@@ -722,10 +749,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               }
             } else {
 #pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const uint64_t ad = umma_desc(ag + 32u * k, 16u, 1024u);
-                const uint64_t bd = umma_desc(b_addr + 32u * k, 16u, 1024u);
-                mma_i8(d_tmem, ad, bd, idesc, k > 0 ? 1u : 0u);
+              for (int sm = 0; sm < kStreams; ++sm) {  // prefix tile; residual tile 16 KB after it
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const uint64_t ad = umma_desc(ag + 32u * k, 16u, 1024u);
+                  const uint64_t bd = umma_desc(b_addr + static_cast<uint32_t>(sm * kBTileBytes) + 32u * k, 16u, 1024u);
+                  mma_i8(d_tmem + static_cast<uint32_t>(sm * kTileN), ad, bd, idesc, k > 0 ? 1u : 0u);
+                }
               }
             }
           }
@@ -733,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         }
         __syncwarp();
         stg.next<L::stages>();
-        if (!kTwin || st.side == 1) acc.next<kAccBufs>();
+        if (!kTwin || st.side == 1) acc.next<kAcc>();
       }
       if (lane == 0) mma_commit(&a_empty[abuf]);
       __syncwarp();
@@ -791,7 +821,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         if (kTwin && st.side != g) {
           // the other group's tile: keep the rings in step without touching its barriers
           stg.next<L::stages>();
-          if (st.side == 1) acc.next<kAccBufs>();
+          if (st.side == 1) acc.next<kAcc>();
           mst.next<kMeta>();
           continue;
         }
@@ -804,7 +834,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         const int valid = meta->valid;
         const int nseg = meta->nseg;
         const bool last_tile = st.last;
-        const uint32_t tbase = tmem_base + lane_base + static_cast<uint32_t>((acc.idx * kG + g) * kTileN);
+        const uint32_t tbase =
+            tmem_base + lane_base + static_cast<uint32_t>((acc.idx * kG + g) * kStreams * kTileN);
         int sgi = 0;
         bool released = false;
 #pragma unroll
@@ -814,18 +845,40 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           const int c1 = min(c0 + 64, valid);  // this chunk's valid columns [c0, c1)
           uint32_t ra[32], rb[32];              // lanes +0..15 (rows i = 0, 1) and +16..31 (rows i = 2, 3)
           if (tile_live) {
-            float2 sc[8];
+            float2 sc[8], sc2[8];
             if (kTokenScale) {
+              const float* s2base = reinterpret_cast<const float*>(smem + L::off_scale2 + mst.idx * 160 * 4);
 #pragma unroll
               for (int k4 = 0; k4 < 4; ++k4) {
                 const float4 x = *reinterpret_cast<const float4*>(meta->scale + (c0 >> 6) * 80 + tc * 20 + 4 * k4);
                 sc[2 * k4] = make_float2(x.x, x.y);
                 sc[2 * k4 + 1] = make_float2(x.z, x.w);
+                if (kRes) {  // the residual stream's scales, in the same slots
+                  const float4 y = *reinterpret_cast<const float4*>(s2base + (c0 >> 6) * 80 + tc * 20 + 4 * k4);
+                  sc2[2 * k4] = make_float2(y.x, y.y);
+                  sc2[2 * k4 + 1] = make_float2(y.z, y.w);
+                }
               }
             }
             tmem_ld16x256b_x8(tbase + c0, ra);
             tmem_ld16x256b_x8(tbase + (16u << 16) + c0, rb);
             tmem_wait_ld();
+            float v1[16];  // residual stream: the prefix's combined digit dots of this thread's row
+            if (kRes) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+#pragma unroll
+                for (int b2 = 0; b2 < 2; ++b2) {
+                  const int32_t d0 = static_cast<int32_t>(ra[4 * j + b2]);
+                  const int32_t d1 = static_cast<int32_t>(ra[4 * j + 2 + b2]);
+                  const int32_t d2 = static_cast<int32_t>(rb[4 * j + b2]);
+                  v1[2 * j + b2] = __fmaf_rn(__int2float_rn(d2), 65536.0F, __int2float_rn(d0 + 256 * d1));
+                }
+              }
+              tmem_ld16x256b_x8(tbase + kTileN + c0, ra);  // the residual stream's accumulator
+              tmem_ld16x256b_x8(tbase + kTileN + (16u << 16) + c0, rb);
+              tmem_wait_ld();
+            }
             if (c0 + 64 >= valid) {
               // last chunk of the tile is in registers: hand the accumulators back to the MMA now
               tc_fence_before();
@@ -844,7 +897,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                   const int32_t d1 = static_cast<int32_t>(ra[4 * j + 2 + b2]);
                   const int32_t d2 = static_cast<int32_t>(rb[4 * j + b2]);
                   float v = __fmaf_rn(__int2float_rn(d2), 65536.0F, __int2float_rn(d0 + 256 * d1));
-                  if (kTokenScale) v = __fmul_rn(v, b2 ? sc[j].y : sc[j].x);
+                  if (kRes) {
+                    // fl(fl(fl(v1 * scale1) * s1) + fl(fl(v2 * scale2) * s2)), as the SIMT kernel orders it
+                    const float a = __fmul_rn(__fmul_rn(v1[2 * j + b2], p.res_scale1), b2 ? sc[j].y : sc[j].x);
+                    const float b = __fmul_rn(__fmul_rn(v, p.res_scale2), b2 ? sc2[j].y : sc2[j].x);
+                    v = __fadd_rn(a, b);
+                  } else if (kTokenScale) {
+                    v = __fmul_rn(v, b2 ? sc[j].y : sc[j].x);
+                  }
                   ra[4 * j + b2] = __float_as_uint(v);
                 }
               }
@@ -1031,7 +1091,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           mbar_arrive(&m_empty[mst.idx]);
         }
         stg.next<L::stages>();
-        if (!kTwin || st.side == 1) acc.next<kAccBufs>();
+        if (!kTwin || st.side == 1) acc.next<kAcc>();
         mst.next<kMeta>();
       }
     }
@@ -1304,7 +1364,10 @@ bool tc_scan_supported(const DocsView& d, const QueryView& q, const ReduceView& 
   const bool format_ok = d.format == kFormatInt4 || (d.format == kFormatBinary && d.doc_scale == nullptr);
   // weighted MaxSim of fp32 queries: the weights fold into the digit planes' row scales
   const bool reducer_ok = r.reducer == kMaxSim || (r.reducer == kWeighted && q.mode == kQueryF32);
-  return !residual && format_ok && d.dim == 128 && mode_ok && reducer_ok && tg.ids == nullptr &&
+  // the fused residual stream: int4 prefix and residual with per-token scales, fp32 queries
+  const bool residual_ok = !residual || (d.format == kFormatInt4 && q.mode == kQueryF32 && d.token_scale != nullptr &&
+                                         d.codes2 != nullptr && d.token_scale2 != nullptr);
+  return residual_ok && format_ok && d.dim == 128 && mode_ok && reducer_ok && tg.ids == nullptr &&
          q.qtok >= 1 && q.batch >= 1 && d.num_docs <= 0x7FFFFFFF && d.host_offsets != nullptr;
 }
 
@@ -1393,7 +1456,12 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   prm.batch = q.batch;
   prm.qtok = q.qtok;
   prm.qpt = pl.qpt;
-  prm.scale = d.scale;
+  // the fused residual stream applies its scalar scales per token, not to the document score
+  const bool res = d.codes2 != nullptr;
+  prm.scale = res ? 1.0F : d.scale;
+  prm.token_scale2 = d.token_scale2;
+  prm.res_scale1 = d.scale;
+  prm.res_scale2 = d.scale2;
   prm.num_docs = d.num_docs;
   prm.out = out;
   prm.error = err;
@@ -1401,20 +1469,28 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   const bool digits = q.mode == kQueryF32;
   const bool f16 = !digits && d.format == kFormatInt4 && d.codes16 != nullptr && d.token_scale != nullptr;
   const bool pre = f16 || d.codes8 != nullptr;
-  // the expanding path decodes int4 rows: binary corpora need their +-1 copy
+  // the expanding path decodes int4 rows: binary corpora need their +-1 copy, the residual stream both
+  // int8 copies
   if (d.format == kFormatBinary && !d.codes8) throw CudaFailure("binary tensor-core scan without the int8 copy");
+  if (res && !(digits && d.token_scale && d.token_scale2 && d.codes8 && d.codes2_8))
+    throw CudaFailure("residual tensor-core scan without its int8 copies");
   const CUtensorMap tmap = f16   ? make_operand_map(d.codes16, d.num_tokens, true)
                            : pre ? make_operand_map(d.codes8, d.num_tokens, false)
                                  : CUtensorMap{};
+  const CUtensorMap tmap2 = res ? make_operand_map(d.codes2_8, d.num_tokens, false) : CUtensorMap{};
   auto go = [&](auto plain, auto twin_kernel, int smem_bytes) {
     auto kernel = twin ? twin_kernel : plain;
     check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes), "set tc smem");
-    kernel<<<grid, tc::kThreads, smem_bytes, stream>>>(prm, tmap);
+    kernel<<<grid, tc::kThreads, smem_bytes, stream>>>(prm, tmap, tmap2);
   };
   using LayoutF16 = tc::Layout<true, true>;
 #define MSB_TC_GO(TS, PRE, F16, DIG, LAYOUT) \
   go(tc::tc_scan_kernel<TS, PRE, F16, DIG, false>, tc::tc_scan_kernel<TS, PRE, F16, DIG, true>, LAYOUT::bytes)
-  if (digits) {
+  using LayoutRes = tc::Layout<true, false, true>;
+  if (res) {
+    go(tc::tc_scan_kernel<true, true, false, true, false, true>, tc::tc_scan_kernel<true, true, false, true, true, true>,
+       LayoutRes::bytes);
+  } else if (digits) {
     if (d.token_scale) {
       if (pre) MSB_TC_GO(true, true, false, true, tc::Layout<true>);
       else MSB_TC_GO(true, false, false, true, tc::Layout<false>);

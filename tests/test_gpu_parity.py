@@ -146,7 +146,11 @@ def test_reducers_match_reference_golden(engine, golden, reducer):
     cand = m.residual_score(q, res, reducer=reducer, candidate_indices=cands, **kw)
     np.testing.assert_allclose(full, g[f"residual_{reducer}_full"], rtol=RTOL, atol=3e-4)
     np.testing.assert_allclose(cand, g[f"residual_{reducer}_cand"], rtol=RTOL, atol=3e-4)
-    np.testing.assert_array_equal(cand, np.take(full, cands, axis=-1))
+    if engine == 0 and reducer in ("maxsim", "weighted_maxsim"):
+        # the full scan runs on the tensor-core digit planes, candidate lists on fp32 FMA chains
+        np.testing.assert_allclose(cand, np.take(full, cands, axis=-1), rtol=2e-6, atol=2e-6 * np.abs(full).max())
+    else:
+        np.testing.assert_array_equal(cand, np.take(full, cands, axis=-1))
 
 
 @pytest.mark.parametrize("gran", ["tensor", "token"])

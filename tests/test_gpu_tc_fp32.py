@@ -249,3 +249,96 @@ def test_binary_document_scales_stay_simt(engine):
     want = h.score_batch(q, use_scale_vector=True)
     engine.set_engine(0)
     np.testing.assert_array_equal(h.score_batch(q, use_scale_vector=True), want)
+
+
+# ---------------------------------------------------------------------------
+# The fused residual stream: both int4 streams' int8 copies, two accumulators per query tile
+# ---------------------------------------------------------------------------
+
+def _digit_values(query, values):
+    """Combined digit dots fl(65536 d2 + fl(d0 + 256 d1)) of every query row with every token [R, N],
+    and the rows' power-of-two scales."""
+    digits, qscale = _digits(query.reshape(-1, 128))
+    dots = np.einsum("kri,ti->krt", digits, values.astype(np.int64))
+    lo = (dots[0] + 256 * dots[1]).astype(np.float32)
+    return (dots[2].astype(np.float64) * 65536.0 + lo.astype(np.float64)).astype(np.float32), qscale
+
+
+def _residual_model(query, res, offsets, weights=None):
+    B, Q, _ = query.shape
+    v1, qscale = _digit_values(query, res["prefix_values"])
+    v2, _ = _digit_values(query, res["residual_values"])
+    f32 = np.float32
+    a = (v1 * f32(res["prefix_scale"])) * np.asarray(res["prefix_token_scale"], f32)[None, :]
+    b = (v2 * f32(res["residual_scale"])) * np.asarray(res["residual_token_scale"], f32)[None, :]
+    sim = a + b  # every step a float32 operation, rounded once
+    if weights is not None:
+        w = np.broadcast_to(np.asarray(weights, f32), (B, Q)).reshape(-1)
+        qscale = np.ldexp(w, np.frexp(qscale)[1] - 1).astype(f32)
+    out = np.zeros((B, offsets.shape[0] - 1), f32)
+    for d in range(offsets.shape[0] - 1):
+        lo, hi = offsets[d], offsets[d + 1]
+        if lo == hi:
+            continue
+        best = sim[:, lo:hi].max(axis=1) * qscale
+        for bi in range(B):
+            acc = f32(0)
+            for r in range(Q):
+                acc = f32(acc + best[bi * Q + r])
+            out[bi, d] = acc
+    return out
+
+
+def _residual_corpus(num_docs, max_len, seed):
+    import maxsim_b200 as m
+
+    docs, off = _corpus(num_docs, max_len, seed)
+    packed = m.pack_residual_int4(docs, off)
+    res = {k: getattr(packed, k) for k in ("prefix_scale", "prefix_token_scale", "residual_scale",
+                                            "residual_token_scale")}
+    res["prefix_values"] = ref.unpack_nibbles(packed.prefix_data, 128)
+    res["residual_values"] = ref.unpack_nibbles(packed.residual_data, 128)
+    return docs, off, packed, res, m.residual_int4_to_device(packed)
+
+
+@pytest.mark.parametrize("batch,qtok", [(1, 32), (4, 32), (3, 9)])
+@pytest.mark.parametrize("weighted", [False, True])
+def test_residual_stream_on_digit_planes(engine, batch, qtok, weighted):
+    import maxsim_b200 as m
+
+    docs, off, packed, res, dev = _residual_corpus(260, 250, seed=41 + qtok)
+    q = ref.clustered_queries(docs, off, batch, qtok, seed=42)
+    kw, w = {}, None
+    if weighted:
+        w = np.random.default_rng(43).uniform(0.5, 1.5, size=qtok).astype(np.float32)
+        kw = {"reducer": "weighted_maxsim", "query_weights": w}
+    engine.set_engine(2)
+    got = m.residual_score(q, dev, **kw)
+    np.testing.assert_array_equal(got, _residual_model(q, res, off, weights=w))
+    oracle = {"prefix_values": res["prefix_values"], "prefix_scale": res["prefix_scale"],
+              "prefix_token_scale": res["prefix_token_scale"], "residual_values": res["residual_values"],
+              "residual_scale": res["residual_scale"], "residual_token_scale": res["residual_token_scale"]}
+    exact = ref.score_residual(q, oracle, off, **({"reducer": "weighted_maxsim", "weights": w} if weighted else {}))
+    np.testing.assert_allclose(got, exact, rtol=2e-6, atol=2e-6 * np.abs(exact).max())
+    engine.set_engine(1)
+    np.testing.assert_allclose(m.residual_score(q, dev, **kw), got, rtol=1e-5, atol=1e-5 * np.abs(exact).max())
+
+
+def test_residual_stream_replaced_on_the_handle(engine):
+    """Replacing or clearing a handle's residual stream drops its int8 copy: the next scan reads the new one."""
+    import maxsim_b200 as m
+
+    docs, off, packed, res, dev = _residual_corpus(150, 120, seed=51)
+    q = ref.clustered_queries(docs, off, 2, 16, seed=52)
+    h = dev.prefix_data
+    engine.set_engine(2)
+    first = h.score_residual_batch(q)
+    np.testing.assert_array_equal(first, _residual_model(q, res, off))
+    other = m.pack_residual_int4(docs[::-1].copy(), off)
+    h.set_residual_int4(other.residual_data, float(other.residual_scale), other.residual_token_scale)
+    res2 = dict(res, residual_values=ref.unpack_nibbles(other.residual_data, 128), residual_scale=other.residual_scale,
+                residual_token_scale=other.residual_token_scale)
+    np.testing.assert_array_equal(h.score_residual_batch(q), _residual_model(q, res2, off))
+    h.clear_residual_int4()
+    with pytest.raises(ValueError, match="residual"):
+        h.score_residual_batch(q)
