@@ -20,6 +20,7 @@ void launch_simt_scan(const DocsView&, const QueryView&, const ReduceView&, cons
 void launch_quantize_rows(const float*, int64_t, int, int8_t*, float*, int32_t*, int32_t*, bool, cudaStream_t);
 void launch_split_query_digits(const float*, int64_t, int32_t*, float*, const float*, int, int, cudaStream_t);
 void launch_topk_rows(const float*, int64_t, int, int64_t, int, const int64_t*, bool, float*, int64_t*, cudaStream_t);
+void launch_gather_scores(const float*, int64_t, int, const int64_t*, int64_t, bool, float*, cudaStream_t);
 void launch_pack_int4(const float*, int64_t, int, bool, uint8_t*, float*, float*, void*, cudaStream_t);
 void launch_pack_signs(const float*, int64_t, int, uint8_t*, float*, cudaStream_t);
 void launch_check_positive_finite(const float*, int64_t, unsigned int*, cudaStream_t);
@@ -133,7 +134,8 @@ struct msb_docs {
   DeviceBuf codes, offsets, token_scale, doc_scale, residual_codes, residual_token_scale;
   // Workspace (grows monotonically, reused across calls).
   DeviceBuf w_query, w_qcodes, w_qwords, w_qscale, w_qsum, w_scores, w_cands, w_weights, w_top_s, w_top_i,
-      w_override, w_fine, w_tc;
+      w_override, w_fine, w_tc,
+      w_full;  // full-scan scores that candidate lists are gathered from
   std::vector<int64_t> host_offsets;
   bool tc_used = false;  // the tensor-core engine ran since the last error check
   uint64_t serial = 0;   // unique corpus id for caches keyed on a corpus
@@ -166,7 +168,7 @@ struct msb_docs {
   int64_t workspace_bytes() const {
     return static_cast<int64_t>(w_query.cap + w_qcodes.cap + w_qwords.cap + w_qscale.cap + w_qsum.cap +
                                 w_scores.cap + w_cands.cap + w_weights.cap + w_top_s.cap + w_top_i.cap +
-                                w_override.cap + w_fine.cap + w_tc.cap + w_check.cap);
+                                w_override.cap + w_fine.cap + w_tc.cap + w_check.cap + w_full.cap);
   }
   ~msb_docs() {
     int prev = -1;
@@ -176,7 +178,7 @@ struct msb_docs {
     DeviceBuf* all[] = {&codes,   &offsets,  &token_scale, &doc_scale, &residual_codes, &residual_token_scale,
                         &w_query, &w_qcodes, &w_qwords,    &w_qscale,  &w_qsum,         &w_scores,
                         &w_cands, &w_weights, &w_top_s,    &w_top_i,   &w_override,     &w_fine,
-                        &w_tc,    &codes8,   &codes16,   &w_check,        &codes2_8};
+                        &w_tc,    &codes8,   &codes16,   &w_check,        &codes2_8,  &w_full};
     for (DeviceBuf* b : all) b->release();
     for (cudaEvent_t& e : upload_events)
       if (e) cudaEventDestroy(e);
@@ -276,6 +278,29 @@ Resolved resolve(msb_docs* h, const msb_score_opts* o, int batch, int qtok, cons
   return r;
 }
 
+void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, int qtok, const TargetsView& tg,
+              float* d_out, cudaStream_t stream);
+
+// Candidate lists (shared or per row) that name at least one document in 16 are scored faster by a full
+// tensor-core scan whose scores are then gathered: per (document, query) that scan costs a few percent
+// of the SIMT rescoring of a candidate.  Returns false (nothing done) when the list is shorter, the SIMT
+// engine is forced, or the tensor-core engine does not support the full scan.  (If a binary corpus or
+// the residual stream cannot get its int8 copy, the full scan runs on the SIMT engine: correct, slower.)
+bool scan_targets_via_full_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, int qtok,
+                                const TargetsView& tg, float* d_out, cudaStream_t stream) {
+  if (!tg.ids || g_engine.load() == 1 || tg.count * 16 < h->num_docs || batch <= 0 || qtok <= 0) return false;
+  QueryView qv{};
+  qv.f32 = d_query;
+  qv.batch = batch;
+  qv.qtok = qtok;
+  qv.mode = r.mode;
+  if (!tc_scan_supported(r.docs, qv, r.red, TargetsView{}, r.residual)) return false;
+  h->w_full.ensure(sizeof(float) * static_cast<size_t>(batch) * h->num_docs, "cudaMalloc full score cache");
+  run_scan(h, r, d_query, batch, qtok, TargetsView{}, h->w_full.as<float>(), stream);
+  launch_gather_scores(h->w_full.as<float>(), h->num_docs, batch, tg.ids, tg.count, tg.per_row != 0, d_out, stream);
+  return true;
+}
+
 // Run one scan into d_out [B, T].  d_query is a device pointer.
 void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, int qtok, const TargetsView& tg,
               float* d_out, cudaStream_t stream) {
@@ -285,6 +310,7 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
     check(cudaMemsetAsync(d_out, 0, sizeof(float) * static_cast<size_t>(batch) * T, stream), "zero scores");
     return;
   }
+  if (scan_targets_via_full_scan(h, r, d_query, batch, qtok, tg, d_out, stream)) return;
   QueryView qv{};
   qv.f32 = d_query;
   qv.batch = batch;
@@ -990,9 +1016,11 @@ int msb_docs_cascade_topk(msb_docs* h, const float* query, int32_t batch, int32_
       tg.ids = h->w_cands.as<int64_t>();
       tg.count = m;
       tg.per_row = 1;
-      // Rescoring of per-row candidate lists always runs on the SIMT engine.
-      launch_simt_scan(rf.docs, QueryView{d_q, nullptr, nullptr, nullptr, nullptr, batch, qtok, kQueryF32}, rf.red,
-                       tg, true, h->w_fine.as<float>(), s);
+      // Rescoring of per-row candidate lists: from the full tensor-core residual scan when the lists are
+      // long enough, else on the SIMT engine.
+      if (!scan_targets_via_full_scan(h, rf, d_q, batch, qtok, tg, h->w_fine.as<float>(), s))
+        launch_simt_scan(rf.docs, QueryView{d_q, nullptr, nullptr, nullptr, nullptr, batch, qtok, kQueryF32}, rf.red,
+                         tg, true, h->w_fine.as<float>(), s);
       launch_topk_rows(h->w_fine.as<float>(), m, batch, m, k, h->w_cands.as<int64_t>(), true,
                        h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
     }

@@ -10,6 +10,8 @@
 //   * long rows: 4-pass 8-bit radix select of the k-th largest ordered key,
 //     then collection of everything above it plus the lowest-index ties, and
 //     a bitonic sort of the k survivors.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace msb {
@@ -205,6 +207,29 @@ void launch_topk_rows(const float* scores, int64_t ld, int rows, int64_t T, int 
   topk_select_kernel<<<rows, kTopkThreads, smem, stream>>>(scores, ld, T, k, out_s, out_id);
   count_launch();
   check(cudaGetLastError(), "launch top-k select kernel");
+}
+
+// out[b, j] = scores[b, ids[j]] (shared list) or scores[b, ids[b * count + j]] (per-row lists): the scores
+// of candidate lists read out of a full scan.
+__global__ void gather_scores_kernel(const float* __restrict__ scores, int64_t ld, int rows,
+                                     const int64_t* __restrict__ ids, int64_t count, int per_row,
+                                     float* __restrict__ out) {
+  const int64_t n = static_cast<int64_t>(rows) * count;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < n;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t b = e / count, j = e - b * count;
+    out[e] = scores[b * ld + ids[per_row ? e : j]];
+  }
+}
+
+void launch_gather_scores(const float* scores, int64_t ld, int rows, const int64_t* ids, int64_t count, bool per_row,
+                          float* out, cudaStream_t stream) {
+  const int64_t n = static_cast<int64_t>(rows) * count;
+  if (n <= 0) return;
+  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 148LL * 8));
+  gather_scores_kernel<<<blocks, 256, 0, stream>>>(scores, ld, rows, ids, count, per_row ? 1 : 0, out);
+  count_launch();
+  check(cudaGetLastError(), "launch candidate score gather kernel");
 }
 
 }  // namespace msb

@@ -342,3 +342,30 @@ def test_residual_stream_replaced_on_the_handle(engine):
     h.clear_residual_int4()
     with pytest.raises(ValueError, match="residual"):
         h.score_residual_batch(q)
+
+
+def test_candidate_lists_long_enough_read_the_full_scan(engine):
+    """A candidate list naming at least one document in 16 is read out of the full tensor-core scan, so its
+    scores equal the full scan's columns exactly; a shorter list is rescored on the SIMT engine."""
+    import maxsim_b200 as m
+
+    docs, off, packed, res, dev = _residual_corpus(320, 90, seed=61)
+    q = ref.clustered_queries(docs, off, 3, 20, seed=62)
+    rng = np.random.default_rng(63)
+    long_list = rng.integers(0, 320, size=40).astype(np.int64)   # 40 * 16 >= 320
+    short_list = rng.integers(0, 320, size=15).astype(np.int64)  # 15 * 16 < 320
+    int4 = m.int4_to_device(m.pack_int4_symmetric(docs, off, scale_granularity="token"))
+    _, binh = _binary(docs, off, True)
+    cases = [
+        (lambda c=None: m.int4_maxsim(q, int4, candidate_indices=c)),
+        (lambda c=None: m.residual_score(q, dev, candidate_indices=c)),
+        (lambda c=None: binh.score_batch(q, use_token_scale=True) if c is None
+         else binh.score_candidates_batch(q, c, use_token_scale=True)),
+    ]
+    for run in cases:
+        engine.set_engine(0)
+        full = run()
+        np.testing.assert_array_equal(run(long_list), full[:, long_list])
+        got_short = run(short_list)
+        engine.set_engine(1)
+        np.testing.assert_array_equal(got_short, run(short_list))
