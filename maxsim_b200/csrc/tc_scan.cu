@@ -1364,9 +1364,11 @@ bool tc_scan_supported(const DocsView& d, const QueryView& q, const ReduceView& 
   const bool format_ok = d.format == kFormatInt4 || (d.format == kFormatBinary && d.doc_scale == nullptr);
   // weighted MaxSim of fp32 queries: the weights fold into the digit planes' row scales
   const bool reducer_ok = r.reducer == kMaxSim || (r.reducer == kWeighted && q.mode == kQueryF32);
-  // the fused residual stream: int4 prefix and residual with per-token scales, fp32 queries
-  const bool residual_ok = !residual || (d.format == kFormatInt4 && q.mode == kQueryF32 && d.token_scale != nullptr &&
-                                         d.codes2 != nullptr && d.token_scale2 != nullptr);
+  // the fused residual stream: an int4 or sign-code prefix and an int4 residual, per-token scales on both,
+  // fp32 queries (a sign-code prefix has scale 1, so its term is fl(v1 * s1) as in the SIMT kernel)
+  const bool residual_ok = !residual || ((d.format == kFormatInt4 || d.format == kFormatBinary) &&
+                                         q.mode == kQueryF32 && d.token_scale != nullptr && d.codes2 != nullptr &&
+                                         d.token_scale2 != nullptr);
   return residual_ok && format_ok && d.dim == 128 && mode_ok && reducer_ok && tg.ids == nullptr &&
          q.qtok >= 1 && q.batch >= 1 && d.num_docs <= 0x7FFFFFFF && d.host_offsets != nullptr;
 }

@@ -41,7 +41,11 @@ def test_fused_scores_and_candidates(corpus, reducer):
     np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
     cands = np.array([7, 0, 299, 150, 7], np.int64)
     got_c = m.binary_residual_score(q, dev, candidate_indices=cands, **kw)
-    np.testing.assert_array_equal(got_c, got[:, cands])  # candidate scores equal the full scan exactly
+    if reducer in ("maxsim", "weighted_maxsim"):
+        # the full scan runs on the tensor-core digit planes, a short candidate list on fp32 FMA chains
+        np.testing.assert_allclose(got_c, got[:, cands], rtol=2e-6, atol=2e-6 * np.abs(got).max())
+    else:
+        np.testing.assert_array_equal(got_c, got[:, cands])  # both on the SIMT engine: identical
 
 
 def test_prefix_scores_are_the_scaled_sign_scan(corpus):

@@ -369,3 +369,24 @@ def test_candidate_lists_long_enough_read_the_full_scan(engine):
         got_short = run(short_list)
         engine.set_engine(1)
         np.testing.assert_array_equal(got_short, run(short_list))
+
+
+@pytest.mark.parametrize("batch,qtok", [(1, 32), (3, 16)])
+def test_binary_prefix_residual_on_digit_planes(engine, batch, qtok):
+    """Sign-code prefix (scale 1, per-token mean |x|) + int4 residual: the same residual kernel, reading
+    the +-1 copy as the prefix stream."""
+    from maxsim_b200 import cascade as casc
+
+    docs, off = _corpus(240, 200, seed=71)
+    q = ref.clustered_queries(docs, off, batch, qtok, seed=72)
+    packed = casc.pack_binary_residual_int4(docs, off)
+    dev = casc.binary_residual_to_device(packed)
+    res = {"prefix_values": ref.unpack_signs(packed.prefix_data, 128).astype(np.int64), "prefix_scale": 1.0,
+           "prefix_token_scale": packed.prefix_token_scale, "residual_values": ref.unpack_nibbles(packed.residual_data, 128),
+           "residual_scale": 1.0, "residual_token_scale": packed.residual_token_scale}
+    engine.set_engine(2)
+    got = casc.binary_residual_score(q, dev)
+    np.testing.assert_array_equal(got, _residual_model(q, res, off))
+    engine.set_engine(1)
+    simt = casc.binary_residual_score(q, dev)
+    np.testing.assert_allclose(got, simt, rtol=1e-5, atol=1e-5 * np.abs(simt).max())
