@@ -103,7 +103,12 @@ int64_t msb_launch_count(void);
  * dim 128, scalar document scale), and use the SIMT engine when there is no
  * memory for it.  fp32 queries of up to 32 tokens run on the tensor-core
  * engine as three int8 digit planes of each row's 23-bit fixed-point value
- * (exact integer dots, one rounding).  "tc_f16_cache": 1 keeps an f16
+ * (exact integer dots, one rounding), for MaxSim and weighted MaxSim.  The
+ * fused residual stream (use_residual) runs there too, reading a second int8
+ * copy of the residual codes (128 B per token, dropped when the residual is
+ * replaced or cleared).  Candidate lists that name at least one document in
+ * 16 are scored by a full tensor-core scan whose [batch, num_docs] scores
+ * (workspace) are then gathered.  "tc_f16_cache": 1 keeps an f16
  * copy instead (256 B per token, per-token-scale corpora) and runs kind::f16
  * MMAs whose fp32 accumulators hold the exact integer dots, so the epilogue
  * converts nothing; 0 (default) because its doubled MMA and operand traffic
