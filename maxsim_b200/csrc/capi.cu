@@ -295,7 +295,18 @@ bool scan_targets_via_full_scan(msb_docs* h, const Resolved& r, const float* d_q
   qv.qtok = qtok;
   qv.mode = r.mode;
   if (!tc_scan_supported(r.docs, qv, r.red, TargetsView{}, r.residual)) return false;
-  h->w_full.ensure(sizeof(float) * static_cast<size_t>(batch) * h->num_docs, "cudaMalloc full score cache");
+  const size_t bytes = sizeof(float) * static_cast<size_t>(batch) * h->num_docs;
+  if (bytes > h->w_full.cap) {
+    // no room for the full score matrix: rescore the list instead (the shorter output of the SIMT engine)
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return false;
+    }
+    h->w_full.release();
+    h->w_full.ptr = p;
+    h->w_full.cap = bytes;
+  }
   run_scan(h, r, d_query, batch, qtok, TargetsView{}, h->w_full.as<float>(), stream);
   launch_gather_scores(h->w_full.as<float>(), h->num_docs, batch, tg.ids, tg.count, tg.per_row != 0, d_out, stream);
   return true;
