@@ -337,7 +337,8 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
     // the int8 copy (int4 expanded, or +-1 for sign codes).  int4 corpora fall back to expanding per
     // tile when there is no memory for a copy; binary corpora fall back to the SIMT engine.
     const bool binary = h->format == kFormatBinary;
-    if (!binary && !r.residual && g_tc_f16_cache.load() && !h->codes16_failed && dv.token_scale &&
+    const bool topk = r.red.reducer == kTopK2 || r.red.reducer == kTopK4;  // its kernels read the int8 copy
+    if (!binary && !r.residual && !topk && g_tc_f16_cache.load() && !h->codes16_failed && dv.token_scale &&
         tc_int8_cache_supported(dv)) {
       if (!h->codes16.ptr) {
         const size_t bytes = static_cast<size_t>(h->num_tokens) * 256;
@@ -354,7 +355,7 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
       }
       if (h->codes16.ptr) dv.codes16 = static_cast<const uint16_t*>(h->codes16.ptr);
     }
-    if (!dv.codes16 && (binary || r.residual || g_tc_int8_cache.load()) && !h->codes8_failed &&
+    if (!dv.codes16 && (binary || r.residual || topk || g_tc_int8_cache.load()) && !h->codes8_failed &&
         tc_int8_cache_supported(dv)) {
       if (!h->codes8.ptr) {
         const size_t bytes = static_cast<size_t>(h->num_tokens) * 128;
@@ -371,8 +372,8 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
       }
       if (h->codes8.ptr) dv.codes8 = h->codes8.as<uint8_t>();
     }
-    if (binary && !dv.codes8) {
-      if (engine == 2) throw NotSupported("no device memory for the tensor-core engine's int8 copy of the sign codes");
+    if ((binary || topk) && !dv.codes8) {
+      if (engine == 2) throw NotSupported("no device memory for the tensor-core engine's int8 copy of the codes");
       use_tc = false;
     }
     if (r.residual) {

@@ -305,6 +305,19 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 
 // Maximum of row s (0 or 1) of a 16x256b chunk half X (its 16 values X[4j + 2s], X[4j + 2s + 1]) folded
 // into R: four independent chains of three-input maxima.
+// Insertion of x into a descending list of K values (the SIMT reducer's order: equal values keep their
+// places, so sums over the list do not depend on the insertion order of ties).
+template <int K>
+__device__ __forceinline__ void topk_insert(float (&v)[K], float x) {
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    const float cur = v[i];
+    const bool take = x > cur;
+    v[i] = take ? x : cur;
+    x = take ? cur : x;
+  }
+}
+
 __device__ __forceinline__ float row_max16(const uint32_t* X, int s, float R) {
   float m0 = fmax3(__uint_as_float(X[2 * s]), __uint_as_float(X[2 * s + 1]), __uint_as_float(X[16 + 2 * s]));
   float m1 = fmax3(__uint_as_float(X[4 + 2 * s]), __uint_as_float(X[4 + 2 * s + 1]), __uint_as_float(X[20 + 2 * s]));
@@ -396,11 +409,18 @@ __device__ __forceinline__ Step step_of(const Item& it, int64_t i) {
 // per token tile the prefix tile (tmap) and the residual tile (tmap2) each get an accumulator per query
 // tile, so one accumulator buffer fills the 512 TMEM columns; the epilogue forms
 // fl(fl(fl(v1 * scale1) * s1) + fl(fl(v2 * scale2) * s2)) before the maximum.
-template <bool kTokenScale, bool kPre, bool kF16, bool kDigits = false, bool kTwin = false, bool kRes = false>
+// kTopK (2 or 4): the TopK reducers of digit-plane queries: each thread keeps a descending list of its
+// columns' largest values per row and a token count; at a document end the four threads holding the row
+// merge lists and counts, and the row value is the mean of the top min(K, tokens) values (summed in
+// descending order), as the SIMT reducer forms it.
+template <bool kTokenScale, bool kPre, bool kF16, bool kDigits = false, bool kTwin = false, bool kRes = false,
+          int kTopK = 0>
 __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap,
                                                               const __grid_constant__ CUtensorMap tmap2) {
   using L = Layout<kPre, kF16, kRes>;
   static_assert(!kRes || (kPre && kDigits && kTokenScale && !kF16), "the residual stream reads both int8 copies");
+  static_assert(kTopK == 0 || (kTopK <= 4 && kPre && kDigits && !kRes), "TopK: digit-plane queries, int8 copies");
+  constexpr int kTk = kTopK > 0 ? kTopK : 1;
   constexpr int kAcc = kRes ? 1 : kAccBufs;         // accumulator buffers
   constexpr int kStreams = kRes ? 2 : 1;            // accumulators per query tile
   static_assert(!kF16 || (kPre && kTokenScale), "f16 operands come from the resident copy, with token scales");
@@ -814,6 +834,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       const int nq1 = kTwin ? 0 : max(0, min(p.qpt, p.batch - (unit.qpair * kG + 1) * p.qpt));
       const int nq = nq0 + nq1;
       float run[4] = {kLowest, kLowest, kLowest, kLowest};                // open document, per row
+      float tk[kTk];                                                      // TopK: open document's list
+      int tk_cnt = 0;                                                     // TopK: its tokens in my columns
+#pragma unroll
+      for (int i = 0; i < kTk; ++i) tk[i] = kLowest;
       int32_t run_i[4] = {INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN};    // tensor-scale variant
       int pending = 0;
       for (int64_t si = 0; si < it.nsteps; ++si) {
@@ -929,7 +953,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               }
             }
           }
-          if (nseg == 0 && tile_live && c1 == c0 + 64) {
+          if (!kTopK && nseg == 0 && tile_live && c1 == c0 + 64) {
             // no document ends in this tile and the open document covers the whole chunk: no walk
             if (kFloat) {
               run[0] = row_max16(ra, 0, run[0]);
@@ -952,7 +976,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           while (true) {
             const int e = nseg == 0 ? 0x7FFF : (sgi < nseg ? meta->seg_end[sgi] : 0x7FFF);
             const int bnd = min(e, c1);
-            const bool split = kFloat && tile_live && a == c0 && c1 == c0 + 64 && e > c0 && e < c1 &&
+            const bool split = !kTopK && kFloat && tile_live && a == c0 && c1 == c0 + 64 && e > c0 && e < c1 &&
                                (sgi + 1 < nseg ? meta->seg_end[sgi + 1] : 0x7FFF) > c1;
             if (split) {
               // Exactly one document ends strictly inside the chunk: one pass sends each value to the
@@ -984,7 +1008,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               carry = true;
               a = e;
             } else if (bnd > a && tile_live) {
-              if (a == c0 && bnd == c0 + 64) {
+              if (kTopK) {
+                // columns [a, bnd) of the open document into this thread's list
+                const int la = a - c0 - 2 * tc, lb = bnd - c0 - 2 * tc;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+#pragma unroll
+                  for (int b2 = 0; b2 < 2; ++b2) {
+                    const int cc = 8 * j + b2;
+                    if (cc >= la && cc < lb) {
+                      topk_insert<kTk>(tk, __uint_as_float(ra[4 * j + b2]));
+                      ++tk_cnt;
+                    }
+                  }
+                }
+              } else if (a == c0 && bnd == c0 + 64) {
                 // whole chunk inside one document: two independent chains per row
                 if (kFloat) {
                   run[0] = row_max16(ra, 0, run[0]);
@@ -1029,7 +1067,24 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             // document meta->seg_doc[sgi] ends: complete each row's maximum across the four threads
             // holding it, stage the row value scaled by the query scale, flush finished documents.
             float best;
-            if (kFloat) {
+            if (kTopK) {
+              // merge the four threads' lists and counts, then the mean of the top min(K, tokens)
+#pragma unroll
+              for (int delta = 1; delta <= 2; delta <<= 1) {
+                float other[kTk];
+#pragma unroll
+                for (int i = 0; i < kTk; ++i) other[i] = __shfl_xor_sync(0xFFFFFFFFu, tk[i], delta);
+                tk_cnt += __shfl_xor_sync(0xFFFFFFFFu, tk_cnt, delta);
+#pragma unroll
+                for (int i = 0; i < kTk; ++i) topk_insert<kTk>(tk, other[i]);
+              }
+              const int c = min(kTk, tk_cnt);
+              float total = 0.0F;
+#pragma unroll
+              for (int i = 0; i < kTk; ++i)
+                if (i < c) total = __fadd_rn(total, tk[i]);
+              best = c > 0 ? __fdiv_rn(total, static_cast<float>(c)) : 0.0F;
+            } else if (kFloat) {
 #pragma unroll
               for (int i = 0; i < kRows; ++i) {
                 run[i] = fmaxf(run[i], __shfl_xor_sync(0xFFFFFFFFu, run[i], 1));
@@ -1052,6 +1107,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               run[i] = carry ? carry_max[i] : kLowest;
               run_i[i] = INT32_MIN;
             }
+#pragma unroll
+            for (int i = 0; i < kTk; ++i) tk[i] = kLowest;
+            tk_cnt = 0;
             if (carry) {
               carry = false;
               a = c1;
@@ -1363,7 +1421,9 @@ bool tc_scan_supported(const DocsView& d, const QueryView& q, const ReduceView& 
   // binary corpora: a scalar document scale (the epilogue's one factor), read from the resident +-1 copy
   const bool format_ok = d.format == kFormatInt4 || (d.format == kFormatBinary && d.doc_scale == nullptr);
   // weighted MaxSim of fp32 queries: the weights fold into the digit planes' row scales
-  const bool reducer_ok = r.reducer == kMaxSim || (r.reducer == kWeighted && q.mode == kQueryF32);
+  // TopK2 / TopK4 of fp32 queries: per-row lists in the epilogue (not with the residual stream)
+  const bool reducer_ok = r.reducer == kMaxSim || (r.reducer == kWeighted && q.mode == kQueryF32) ||
+                          ((r.reducer == kTopK2 || r.reducer == kTopK4) && q.mode == kQueryF32 && !residual);
   // the fused residual stream: an int4 or sign-code prefix and an int4 residual, per-token scales on both,
   // fp32 queries (a sign-code prefix has scale 1, so its term is fl(v1 * s1) as in the SIMT kernel)
   const bool residual_ok = !residual || ((d.format == kFormatInt4 || d.format == kFormatBinary) &&
@@ -1389,7 +1449,7 @@ struct UnitCacheKey {
   }
 };
 
-void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, const TargetsView&, float* out, void* ws,
+void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red, const TargetsView&, float* out, void* ws,
                     size_t ws_bytes, cudaStream_t stream) {
   // The unit table depends only on the corpus and the query tiling; it is
   // built once per (workspace, corpus, tiling) and kept in the workspace.
@@ -1476,6 +1536,8 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   if (d.format == kFormatBinary && !d.codes8) throw CudaFailure("binary tensor-core scan without the int8 copy");
   if (res && !(digits && d.token_scale && d.token_scale2 && d.codes8 && d.codes2_8))
     throw CudaFailure("residual tensor-core scan without its int8 copies");
+  const int topk = red.reducer == kTopK2 ? 2 : (red.reducer == kTopK4 ? 4 : 0);
+  if (topk && !(digits && d.codes8 && !res)) throw CudaFailure("TopK tensor-core scan without the int8 copy");
   const CUtensorMap tmap = f16   ? make_operand_map(d.codes16, d.num_tokens, true)
                            : pre ? make_operand_map(d.codes8, d.num_tokens, false)
                                  : CUtensorMap{};
@@ -1492,6 +1554,18 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView&, co
   if (res) {
     go(tc::tc_scan_kernel<true, true, false, true, false, true>, tc::tc_scan_kernel<true, true, false, true, true, true>,
        LayoutRes::bytes);
+  } else if (topk) {
+#define MSB_TC_TOPK(TS, K) \
+  go(tc::tc_scan_kernel<TS, true, false, true, false, false, K>, tc::tc_scan_kernel<TS, true, false, true, true, false, K>, \
+     tc::Layout<true>::bytes)
+    if (d.token_scale) {
+      if (topk == 2) MSB_TC_TOPK(true, 2);
+      else MSB_TC_TOPK(true, 4);
+    } else {
+      if (topk == 2) MSB_TC_TOPK(false, 2);
+      else MSB_TC_TOPK(false, 4);
+    }
+#undef MSB_TC_TOPK
   } else if (digits) {
     if (d.token_scale) {
       if (pre) MSB_TC_GO(true, true, false, true, tc::Layout<true>);

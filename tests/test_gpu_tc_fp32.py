@@ -390,3 +390,59 @@ def test_binary_prefix_residual_on_digit_planes(engine, batch, qtok):
     engine.set_engine(1)
     simt = casc.binary_residual_score(q, dev)
     np.testing.assert_allclose(got, simt, rtol=1e-5, atol=1e-5 * np.abs(simt).max())
+
+
+def _topk_model(query, values, offsets, scale, token_scale, K):
+    """TopK reducers on digit planes: per row, the mean of the top min(K, tokens) values summed in
+    descending order (one float32 division), times the row's power-of-two scale; rows summed in order."""
+    B, Q, _ = query.shape
+    v, qscale = _digit_values(query, values)
+    if token_scale is not None:
+        v = v * np.asarray(token_scale, np.float32)[None, :]
+    f32 = np.float32
+    out = np.zeros((B, offsets.shape[0] - 1), f32)
+    for d in range(offsets.shape[0] - 1):
+        lo, hi = offsets[d], offsets[d + 1]
+        if lo == hi:
+            continue
+        top = -np.sort(-v[:, lo:hi], axis=1)[:, :min(K, hi - lo)]
+        for bi in range(B):
+            acc = f32(0)
+            for r in range(Q):
+                row = bi * Q + r
+                total = f32(0)
+                for x in top[row]:
+                    total = f32(total + x)
+                acc = f32(acc + f32(f32(total / f32(top.shape[1])) * qscale[row]))
+            out[bi, d] = f32(acc * f32(scale))
+    return out
+
+
+@pytest.mark.parametrize("K", [2, 4])
+@pytest.mark.parametrize("kind", ["token", "tensor", "binary"])
+@pytest.mark.parametrize("batch,qtok", [(1, 24), (5, 16)])
+def test_topk_reducers_on_digit_planes(engine, K, kind, batch, qtok):
+    import maxsim_b200 as m
+
+    docs, off = _corpus(220, 150, seed=81 + K)
+    q = ref.clustered_queries(docs, off, batch, qtok, seed=82)
+    reducer = f"topk{K}"
+    if kind == "binary":
+        packed, h = _binary(docs, off, True)
+        values = ref.unpack_signs(packed.data, 128).astype(np.int64)
+        ts, scale = np.asarray(packed.token_scale, np.float32), 1.0
+        run = lambda: h.score_batch(q, reducer=reducer, use_token_scale=True)
+        exact = ref.score_binary_fp32(q, packed.data, 128, off, token_scale=ts, reducer=reducer)
+    else:
+        packed = m.pack_int4_symmetric(docs, off, scale_granularity=kind)
+        dev = m.int4_to_device(packed)
+        values, ts, scale = packed.values, packed.token_scale, packed.scale
+        run = lambda: m.int4_maxsim(q, dev, reducer=reducer)
+        exact = ref.score_int4_fp32(q, values, off, scale=scale, token_scale=ts, reducer=reducer)
+    assert (np.diff(off) == 1).any()  # documents shorter than K: the mean is over their tokens
+    engine.set_engine(2)
+    got = run()
+    np.testing.assert_array_equal(got, _topk_model(q, values, off, scale, ts, K))
+    np.testing.assert_allclose(got, exact, rtol=2e-6, atol=2e-6 * np.abs(exact).max())
+    engine.set_engine(1)
+    np.testing.assert_allclose(run(), got, rtol=1e-5, atol=1e-5 * np.abs(exact).max())
