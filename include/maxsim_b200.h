@@ -103,7 +103,8 @@ int64_t msb_launch_count(void);
  * dim 128, scalar document scale), and use the SIMT engine when there is no
  * memory for it.  fp32 queries of up to 32 tokens run on the tensor-core
  * engine as three int8 digit planes of each row's 23-bit fixed-point value
- * (exact integer dots, one rounding), for MaxSim and weighted MaxSim.  The
+ * (exact integer dots, one rounding), for MaxSim, weighted MaxSim and TopK2 /
+ * TopK4.  The
  * fused residual stream (use_residual) runs there too, reading a second int8
  * copy of the residual codes (128 B per token, dropped when the residual is
  * replaced or cleared).  Candidate lists that name at least one document in

@@ -1,11 +1,11 @@
 // SIMT scan engine: every format x query mode x reducer, any dim (dim % 8 == 0).
 //
 // This engine is the general path: odd dims, queries of more than 32 tokens
-// with fp32 values, the TopK and SmoothSim reducers, candidate lists naming
-// fewer than one document in 16.  Dim-128 MaxSim and weighted MaxSim full
-// scans (int8 queries, fp32 queries as digit planes, the fused residual
-// streams), and the longer candidate lists gathered from them, run on the
-// tcgen05 engine (tc_scan.cu).
+// with fp32 values, SmoothSim (and TopK of the residual streams), candidate
+// lists naming fewer than one document in 16.  Dim-128 MaxSim, weighted
+// MaxSim and TopK full scans (int8 queries, fp32 queries as digit planes, the
+// fused residual streams), and the longer candidate lists gathered from them,
+// run on the tcgen05 engine (tc_scan.cu).
 //
 // Semantics follow the reference kernels:
 //   int4 fp32     cpp/maxsim/cuda_extension.cu:1268-1323 and :757-844
