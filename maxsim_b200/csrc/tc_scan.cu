@@ -1,4 +1,5 @@
-// Tensor-core (tcgen05) MaxSim scan for dim-128 corpora, int8 queries.
+// Tensor-core (tcgen05) MaxSim scan for dim-128 corpora: int8 queries, and fp32 queries as int8 digit
+// planes.
 //
 // D[query row, token] = sum_k A[row, k] * B[token, k] runs on the 5th-gen
 // tensor cores (tcgen05.mma kind::i8, int32 accumulators in TMEM); the
@@ -44,6 +45,17 @@
 //     and reads its 16 token scales with four 16-byte loads from a permuted
 //     layout; a row's maximum is completed with two butterfly shuffles when a
 //     document ends, and tiles without document ends skip the walk.
+//
+// Variants (template parameters of tc_scan_kernel)
+//   * kDigits: fp32 query rows as three int8 digit planes of their 23-bit fixed-point values, on four
+//     TMEM lanes per row; the epilogue combines the planes' exact dots before the token scale.  Weighted
+//     MaxSim folds the weights into the rows' power-of-two scales.
+//   * Sign-code corpora read a resident +-1 int8 copy through the same TMA path.
+//   * kTwin: passes with one query tile let the two epilogue groups take two document ranges in turn.
+//   * kRes: the fused two-stream residual (int4 or sign-code prefix + int4 residual), two accumulators
+//     per query tile.
+//   * kTopK: the TopK2 / TopK4 reducers, per-thread lists merged across a row's four threads.
+//
 // Every mbarrier wait is bounded (%globaltimer); on timeout the kernel raises
 // an error flag, drains, frees its TMEM and returns.
 #include <cuda.h>
