@@ -102,3 +102,20 @@ def test_cpu_device_requests_fail_loudly():
     idx = m.Index.from_embeddings(["a", "b"], np.ones((2, 128), np.float32), np.array([0, 1, 2]), mode="int4")
     with pytest.raises(NotImplementedError, match="GPU only"):
         m.Reranker(idx, device="cpu")
+
+
+def test_score_options_take_host_arrays_or_tensor_pointers():
+    """The option struct carries a numpy array's address for the synchronous calls and a tensor's
+    data_ptr for the *_device calls (which need device memory there)."""
+    import numpy as np
+    import torch
+
+    from maxsim_b200._maxsim_cuda import _opts
+
+    w = np.arange(4, dtype=np.float32)
+    t = torch.arange(4, dtype=torch.float32)
+    assert _opts(reducer=1, weights=w).weights == w.ctypes.data
+    assert _opts(reducer=1, weights=t).weights == t.data_ptr()
+    assert _opts(override=t).doc_scale_override == t.data_ptr()
+    o = _opts()
+    assert not o.weights and not o.doc_scale_override
