@@ -7,6 +7,11 @@ multiply-add), multiplies by the token scale, takes the maxima, scales them back
 rows in order.  ``_digit_model`` restates that arithmetic in numpy, so the engine must match it bit for
 bit; against the reference's fp32 scoring (the float64 oracle) the only error is the query's rounding
 to 23 bits and the one rounding of each dot, far inside the fp32 paths' 1e-4 tolerance.
+
+The same holds, each with its own restatement, for sign-code corpora (a +-1 int8 copy), weighted
+MaxSim (weights folded into the row scales), the fused residual streams (two accumulators per query
+tile, int4 or sign-code prefix), the TopK2 / TopK4 reducers (per-row lists merged across threads),
+and candidate lists long enough to be gathered from a full scan.
 """
 
 import numpy as np
