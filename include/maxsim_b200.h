@@ -219,6 +219,18 @@ int msb_docs_topk_device(msb_docs* docs, const float* query, int32_t batch, int3
 int msb_topk_rows_device(const float* scores, int64_t ld, int32_t rows, int64_t count, int32_t k,
                          const int64_t* tie_ids, int32_t tie_batched, float* out_scores, int64_t* out_ids,
                          void* stream);
+/* Merge of per-shard top-k lists after one all-gather (multi-GPU search; the
+ * reference is single-GPU, so this replaces its host-side
+ * `np.lexsort`-style top-k of src/maxsim/_api.py:732-735 over the union of
+ * the shards' candidates).  `gathered` holds `world` blocks of
+ * 16 * batch * k bytes in rank order: a rank's [batch, k] fp32 scores at byte
+ * 0 of its block and its [batch, k] int64 local document ids at byte
+ * 8 * batch * k, each row ordered (score desc, id asc); a local id of
+ * INT64_MAX pads a shard with fewer than k documents.  Global id = local id +
+ * first_doc[rank] ([world] int64, device).  Output [batch, k] in the
+ * single-GPU order (score desc, global id asc).  world <= 1024. */
+int msb_merge_shard_topk_device(const void* gathered, int32_t world, int32_t batch, int32_t k,
+                                const int64_t* first_doc, float* out_scores, int64_t* out_ids, void* stream);
 /* Kernel-formula int8 query quantisation (reference :1455-1492):
  * codes [rows, dim] int8, scales [rows] fp32. */
 int msb_quantize_query_int8_device(const float* query, int64_t rows, int32_t dim, int8_t* codes, float* scales,

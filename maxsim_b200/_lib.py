@@ -104,6 +104,7 @@ SIGNATURES = {
     "msb_docs_topk_device_noalloc": (ctypes.c_int, [_vp, _vp, _i32, _i32, _i32, ctypes.POINTER(ScoreOpts), _vp, _vp,
                                                      _vp]),
     "msb_topk_rows_device": (ctypes.c_int, [_vp, _i64, _i32, _i64, _i32, _vp, _i32, _vp, _vp, _vp]),
+    "msb_merge_shard_topk_device": (ctypes.c_int, [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp]),
     "msb_quantize_query_int8_device": (ctypes.c_int, [_vp, _i64, _i32, _vp, _vp, _vp]),
     "msb_pack_int4_device": (ctypes.c_int, [_vp, _i64, _i32, _i32, _vp, _vp, ctypes.POINTER(_f32), _vp]),
     "msb_pack_signs_device": (ctypes.c_int, [_vp, _i64, _i32, _vp, _vp, _vp]),

@@ -20,11 +20,13 @@ void launch_simt_scan(const DocsView&, const QueryView&, const ReduceView&, cons
 void launch_quantize_rows(const float*, int64_t, int, int8_t*, float*, int32_t*, int32_t*, bool, cudaStream_t);
 void launch_split_query_digits(const float*, int64_t, int32_t*, float*, const float*, int, int, cudaStream_t);
 void launch_topk_rows(const float*, int64_t, int, int64_t, int, const int64_t*, bool, float*, int64_t*, cudaStream_t);
+void launch_merge_shard_topk(const void*, int, int, int, const int64_t*, float*, int64_t*, cudaStream_t);
 void launch_gather_scores(const float*, int64_t, int, const int64_t*, int64_t, bool, float*, cudaStream_t);
 void launch_pack_int4(const float*, int64_t, int, bool, uint8_t*, float*, float*, void*, cudaStream_t);
 void launch_pack_signs(const float*, int64_t, int, uint8_t*, float*, cudaStream_t);
 void launch_check_positive_finite(const float*, int64_t, unsigned int*, cudaStream_t);
 void launch_check_int4_codes(const uint8_t*, int64_t, unsigned int*, cudaStream_t);
+void launch_check_scale_range(const float*, int64_t, unsigned int*, cudaStream_t);
 bool tc_scan_supported(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, bool residual);
 void launch_tc_scan(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, float*, void* ws,
                     size_t ws_bytes, cudaStream_t);
@@ -128,6 +130,9 @@ struct msb_docs {
   float scale = 1.0F;
   float residual_scale = 1.0F;
   bool has_token_scale = false;
+  // Whether every finite token scale is below 2^104 in magnitude (the tensor-core scan's biased
+  // accumulators stage s * 2^23): -1 until checked, on first use after the token scales change.
+  int token_scale_small = -1;
   bool has_doc_scale = false;
   bool has_residual = false;
   cudaStream_t stream = nullptr;
@@ -312,6 +317,22 @@ bool scan_targets_via_full_scan(msb_docs* h, const Resolved& r, const float* d_q
   return true;
 }
 
+// Whether the handle's token scales are all below 2^104 in magnitude (non-finite values aside): a
+// device check, run once after the scales change.
+int token_scales_small(msb_docs* h, const float* d_scales, cudaStream_t stream) {
+  if (h->token_scale_small < 0) {
+    h->w_check.ensure(8 * sizeof(unsigned int), "cudaMalloc scale range flag");
+    unsigned int* flag = static_cast<unsigned int*>(h->w_check.ptr) + 4;
+    check(cudaMemsetAsync(flag, 0, sizeof(unsigned int), stream), "clear scale range flag");
+    launch_check_scale_range(d_scales, h->num_tokens, flag, stream);
+    unsigned int big = 0;
+    check(cudaMemcpyAsync(&big, flag, sizeof(big), cudaMemcpyDeviceToHost, stream), "read scale range flag");
+    check(cudaStreamSynchronize(stream), "synchronize scale range check");
+    h->token_scale_small = big == 0 ? 1 : 0;
+  }
+  return h->token_scale_small;
+}
+
 // Run one scan into d_out [B, T].  d_query is a device pointer.
 void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, int qtok, const TargetsView& tg,
               float* d_out, cudaStream_t stream) {
@@ -397,6 +418,7 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
       }
     }
   }
+  if (use_tc && r.mode == kQueryI8 && dv.token_scale) dv.token_scale_small = token_scales_small(h, dv.token_scale, stream);
   const int64_t rows = static_cast<int64_t>(batch) * qtok;
   if (r.mode == kQueryI8) {
     h->w_qcodes.ensure(static_cast<size_t>(rows) * h->dim, "cudaMalloc int8 query codes");
@@ -681,6 +703,7 @@ int msb_docs_set_token_scales(msb_docs* h, const float* scales, int64_t count, i
       check(cudaStreamSynchronize(h->stream), "synchronize token scale upload");
     }
     h->has_token_scale = true;
+    h->token_scale_small = -1;
   });
 }
 
@@ -697,6 +720,7 @@ int msb_docs_set_token_scales_device(msb_docs* h, const float* scales, int64_t c
       check(cudaStreamSynchronize(h->stream), "synchronize token scale upload");
     }
     h->has_token_scale = true;
+    h->token_scale_small = -1;
   });
 }
 
@@ -882,6 +906,7 @@ int msb_docs_upload_finish(msb_docs* h, float residual_scale) {
     if (flags[2]) throw InvalidArgument("residual int4 codes must be symmetric int4 values in [-7, 7]");
     if (flags[3]) throw InvalidArgument("residual token scales must be finite and > 0");
     h->has_token_scale = (h->upload_flags & MSB_UPLOAD_TOKEN_SCALES) != 0;
+    h->token_scale_small = -1;
     if (residual) {
       h->residual_scale = residual_scale;
       h->codes2_8.release();  // the int8 copy of the previous residual stream
@@ -1097,6 +1122,15 @@ int msb_topk_rows_device(const float* scores, int64_t ld, int32_t rows, int64_t 
   });
 }
 
+int msb_merge_shard_topk_device(const void* gathered, int32_t world, int32_t batch, int32_t k,
+                                const int64_t* first_doc, float* out_scores, int64_t* out_ids, void* stream) {
+  return guarded([&] {
+    if (!gathered || !first_doc || !out_scores || !out_ids) throw InvalidArgument("NULL argument");
+    launch_merge_shard_topk(gathered, world, batch, k, first_doc, out_scores, out_ids,
+                            static_cast<cudaStream_t>(stream));
+  });
+}
+
 int msb_quantize_query_int8_device(const float* query, int64_t rows, int32_t dim, int8_t* codes, float* scales,
                                    void* stream) {
   return guarded([&] {
@@ -1177,15 +1211,11 @@ extern "C" int msb_docs_topk_device_noalloc(msb_docs* h, const float* query, int
     check_query(h, query, batch, qtok);
     DeviceGuard g(h->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // (the pointer checks are host queries, made when the stream is not being captured into a graph)
-    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
-    check(cudaStreamIsCapturing(s, &capturing), "query stream capture status");
-    if (capturing == cudaStreamCaptureStatusNone) {
-      if (static_cast<int64_t>(batch) * qtok > 0) require_device_accessible(query, "query");
-      require_device_accessible(out_scores, "out_scores");
-      require_device_accessible(out_ids, "out_ids");
-      require_device_opts(opts);
-    }
+    // Pointers the kernels dereference must be device-accessible: checked on every call (host queries).
+    if (static_cast<int64_t>(batch) * qtok > 0) require_device_accessible(query, "query");
+    require_device_accessible(out_scores, "out_scores");
+    require_device_accessible(out_ids, "out_ids");
+    require_device_opts(opts);
     Resolved r = resolve(h, opts, batch, qtok, opts ? opts->weights : nullptr, opts ? opts->doc_scale_override : nullptr);
     if (batch == 0) return;
     // Scratch layout: scores [batch, num_docs] fp32, then (int8 queries) codes,

@@ -59,6 +59,7 @@ struct DocsView {
   int format;
   float scale;                 // int4 tensor scale or binary scalar doc scale
   float scale2;                // residual tensor scale
+  int token_scale_small;       // every finite token scale is below 2^104 in magnitude (s * 2^23 is exact)
 };
 
 struct QueryView {

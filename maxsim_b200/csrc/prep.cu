@@ -154,6 +154,26 @@ void launch_check_int4_codes(const uint8_t* codes, int64_t bytes, unsigned int* 
   check(cudaGetLastError(), "launch int4 code check kernel");
 }
 
+// Sets *big to 1 when any finite value has magnitude >= 2^104 (too large for the tensor-core scan's
+// exact s * 2^23 staging of token scales).
+__global__ void check_scale_range_kernel(const float* __restrict__ x, int64_t n, unsigned int* __restrict__ big) {
+  bool small = true;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float a = fabsf(x[i]);
+    small = small && !(isfinite(a) && a >= 0x1p104F);
+  }
+  if (__any_sync(0xFFFFFFFFu, !small) && (threadIdx.x & 31) == 0) atomicOr(big, 1u);
+}
+
+void launch_check_scale_range(const float* x, int64_t n, unsigned int* big, cudaStream_t stream) {
+  if (n <= 0) return;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 16);
+  check_scale_range_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, n, big);
+  count_launch();
+  check(cudaGetLastError(), "launch scale range check kernel");
+}
+
 void launch_check_positive_finite(const float* x, int64_t n, unsigned int* bad, cudaStream_t stream) {
   if (n <= 0) return;
   const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 16);

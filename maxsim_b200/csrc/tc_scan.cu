@@ -85,6 +85,12 @@ constexpr int kSegGroup = 8;      // finished documents per epilogue flush
 constexpr int kMaxRangeDocs = 512;
 constexpr uint32_t kTmemCols = kAccBufs * kG * kTileN;        // 512
 constexpr uint64_t kTimeoutNs = 4000000000ull;                // 4 s per wait
+// Biased accumulators (int8 queries, per-token scales): one extra K = 32 MMA of two constant 0x7F
+// operands opens every accumulator at kBiasValue = 32 * 127 * 127, so a finished accumulator holds
+// dot + kBiasValue in (0, 2^23): read as a float it is the subnormal (dot + kBiasValue) * 2^-149, which
+// one fused multiply-add maps exactly to dot * 2^-23 (see bias_scale2).
+constexpr int kBiasBytes = 128 * 32;
+constexpr int32_t kBiasValue = 32 * 127 * 127;  // 516,128 > |dot| <= 127 * 7 * 128 = 113,792
 
 struct Unit {
   int64_t d_lo, d_hi;    // documents [d_lo, d_hi), at most kMaxRangeDocs
@@ -144,9 +150,10 @@ constexpr int kRowBytes = kSegGroup * kG * 128 * 4;    // [group][query tile][ro
 // swizzled K halves of 64 values) and the query tiles are single-buffered to keep 4 B stages.
 // With the residual stream (kRes) each B stage holds two operand tiles (prefix, then residual), the raw
 // ring two scale vectors, and a second scale array per meta slot sits after the meta ring.
-template <bool kPre, bool kF16 = false, bool kRes = false>
+// With biased accumulators (kBias) a 4 KB constant operand follows the B ring, which has one stage less.
+template <bool kPre, bool kF16 = false, bool kRes = false, bool kBias = false>
 struct Layout {
-  static constexpr int stages = (kF16 || kRes) ? 4 : (kPre ? 8 : 4);  // B ring, released by the MMA commit
+  static constexpr int stages = (kF16 || kRes) ? 4 : (kPre ? (kBias ? 7 : 8) : 4);  // B ring, freed by the MMA commit
   static constexpr int a_tile = kF16 ? 2 * kATileBytes : kATileBytes;
   static constexpr int b_tile = (kF16 || kRes) ? 2 * kBTileBytes : kBTileBytes;
   static constexpr int a_bufs = (kF16 || kRes) ? 1 : 2;
@@ -155,7 +162,8 @@ struct Layout {
   static constexpr int raw_bytes = ((raw_code_bytes + (kRes ? 2 : 1) * raw_scale_bytes + 127) / 128) * 128;
   static constexpr int off_a = 0;                        // [a_bufs][kG] query tiles
   static constexpr int off_b = off_a + a_bufs * kG * a_tile;
-  static constexpr int off_raw = off_b + stages * b_tile;
+  static constexpr int off_bias = off_b + stages * b_tile;  // kBias: 128 rows x 32 bytes of 0x7F
+  static constexpr int off_raw = off_bias + (kBias ? kBiasBytes : 0);
   static constexpr int off_meta = off_raw + kRaw * raw_bytes;
   static constexpr int off_scale2 = off_meta + kMeta * kMetaBytes;  // [kMeta][160] (kRes)
   static constexpr int off_uoff = off_scale2 + (kRes ? kMeta * 160 * 4 : 0);
@@ -228,6 +236,38 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
   // matrices along K, SBO between 8-row groups; version 1 (bits 46-47).
   return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
          (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);  // SWIZZLE_128B
+}
+// K-major, no swizzle (layout type 0): the constant bias operand, 128 rows x 32 bytes in 8-row x 16-byte
+// core matrices, LBO 128 bytes between the two K core matrices, SBO 256 bytes between 8-row groups.
+// Every byte is 0x7F, so the product does not depend on how rows map to addresses inside the 4 KB.
+__device__ __forceinline__ uint64_t umma_desc_plain(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(128u >> 4) << 16) |
+         (static_cast<uint64_t>(256u >> 4) << 32) | (1ull << 46);
+}
+// Two biased accumulators of adjacent columns (as float bits: subnormals (dot + kBiasValue) * 2^-149)
+// to fl(dot * s) for their token scales, given as s * 2^23: the packed FMA forms
+// (dot + kBiasValue) * 2^-23 - kBiasValue * 2^-23 = dot * 2^-23 exactly (|dot| < 2^17; subnormal
+// inputs are kept, no flush to zero), and the packed product dot * 2^-23 * (s * 2^23) is rounded once,
+// to the same float as fl(float(dot) * s).  Two instructions per two values, both on the FMA pipe.
+__device__ __forceinline__ uint64_t pack_f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+struct BiasConsts {
+  uint64_t mul, add;  // {2^126, 2^126}, {-kBiasValue * 2^-23, same}
+  __device__ __forceinline__ BiasConsts()
+      : mul(pack_f2(0x1p126F, 0x1p126F)),
+        add(pack_f2(-static_cast<float>(kBiasValue) / 8388608.0F, -static_cast<float>(kBiasValue) / 8388608.0F)) {}
+};
+__device__ __forceinline__ void bias_scale2(uint32_t& x0, uint32_t& x1, const BiasConsts& k, float2 s23) {
+  asm("{\n .reg .b64 v;\n"
+      " mov.b64 v, {%0, %1};\n"
+      " fma.rn.f32x2 v, v, %2, %3;\n"
+      " mul.rn.f32x2 v, v, %4;\n"
+      " mov.b64 {%0, %1}, v;\n}"
+      : "+r"(x0), "+r"(x1)
+      : "l"(k.mul), "l"(k.add), "l"(pack_f2(s23.x, s23.y)));
 }
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
@@ -425,11 +465,17 @@ __device__ __forceinline__ Step step_of(const Item& it, int64_t i) {
 // columns' largest values per row and a token count; at a document end the four threads holding the row
 // merge lists and counts, and the row value is the mean of the top min(K, tokens) values (summed in
 // descending order), as the SIMT reducer forms it.
+// kBias: biased accumulators (kBiasValue, int8 queries with per-token scales): the epilogue converts and
+// scales two values with two packed FMA-pipe instructions (bias_scale2) instead of an int32 -> fp32
+// conversion and a product per value; the token scales are staged as s * 2^23 (the host keeps this
+// variant for corpora whose token scales are below 2^104, so that s * 2^23 is exact).
 template <bool kTokenScale, bool kPre, bool kF16, bool kDigits = false, bool kTwin = false, bool kRes = false,
-          int kTopK = 0>
+          int kTopK = 0, bool kBias = false>
 __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap,
                                                               const __grid_constant__ CUtensorMap tmap2) {
-  using L = Layout<kPre, kF16, kRes>;
+  using L = Layout<kPre, kF16, kRes, kBias>;
+  static_assert(!kBias || (kTokenScale && !kDigits && !kF16 && !kRes && kTopK == 0),
+                "biased accumulators: int8 queries with per-token scales");
   static_assert(!kRes || (kPre && kDigits && kTokenScale && !kF16), "the residual stream reads both int8 copies");
   static_assert(kTopK == 0 || (kTopK <= 4 && kPre && kDigits && !kRes), "TopK: digit-plane queries, int8 copies");
   constexpr int kTk = kTopK > 0 ? kTopK : 1;
@@ -493,6 +539,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (kBias) {
+    // the constant bias operand, made visible to the tensor core (async proxy) before the first MMA
+    for (int i = threadIdx.x; i < kBiasBytes / 16; i += kThreads)
+      reinterpret_cast<uint4*>(smem + L::off_bias)[i] = make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
+    fence_proxy_async();
   }
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -652,7 +704,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         const int valid = st.valid;
         if (kPre && kTokenScale) {
           const float* rs = reinterpret_cast<const float*>(rb + L::raw_code_bytes);
-          for (int r = xtid; r < valid; r += kXWarps * 32) meta->scale[scale_slot(r)] = rs[(t0 & 3) + r];
+          // biased accumulators take s * 2^23 (exact: the host checked s < 2^104)
+          for (int r = xtid; r < valid; r += kXWarps * 32)
+            meta->scale[scale_slot(r)] = kBias ? __fmul_rn(rs[(t0 & 3) + r], 8388608.0F) : rs[(t0 & 3) + r];
           if (kRes) {
             const float* rs2 = reinterpret_cast<const float*>(rb + L::raw_code_bytes + L::raw_scale_bytes);
             float* sc2 = reinterpret_cast<float*>(smem + L::off_scale2 + mst.idx * 160 * 4);
@@ -685,7 +739,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           }
           if (kTokenScale) {
             const float* rs = reinterpret_cast<const float*>(rb + L::raw_code_bytes);
-            meta->scale[scale_slot(r)] = rs[(t0 & 3) + r];
+            meta->scale[scale_slot(r)] = kBias ? __fmul_rn(rs[(t0 & 3) + r], 8388608.0F) : rs[(t0 & 3) + r];
           }
         }
         // Documents ending inside (t0, t0 + valid]: expander warp 0 walks the unit's offsets in smem.
@@ -780,13 +834,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 mma_f16(d_tmem, ad, bd, idesc16, k > 0 ? 1u : 0u);
               }
             } else {
+              if (kBias) {  // every accumulator opens at kBiasValue: constant x constant, K = 32
+                const uint64_t cd = umma_desc_plain(smem_u32(smem + L::off_bias));
+                mma_i8(d_tmem, cd, cd, idesc, 0u);
+              }
 #pragma unroll
               for (int sm = 0; sm < kStreams; ++sm) {  // prefix tile; residual tile 16 KB after it
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                   const uint64_t ad = umma_desc(ag + 32u * k, 16u, 1024u);
                   const uint64_t bd = umma_desc(b_addr + static_cast<uint32_t>(sm * kBTileBytes) + 32u * k, 16u, 1024u);
-                  mma_i8(d_tmem + static_cast<uint32_t>(sm * kTileN), ad, bd, idesc, k > 0 ? 1u : 0u);
+                  mma_i8(d_tmem + static_cast<uint32_t>(sm * kTileN), ad, bd, idesc, (kBias || k > 0) ? 1u : 0u);
                 }
               }
             }
@@ -943,6 +1001,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                   }
                   ra[4 * j + b2] = __float_as_uint(v);
                 }
+              }
+            } else if (kBias) {
+              // (dot + kBiasValue) bits -> fl(dot * s_t): two packed instructions per two columns
+              const BiasConsts kc;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                bias_scale2(ra[4 * j], ra[4 * j + 1], kc, sc[j]);
+                bias_scale2(ra[4 * j + 2], ra[4 * j + 3], kc, sc[j]);
+                bias_scale2(rb[4 * j], rb[4 * j + 1], kc, sc[j]);
+                bias_scale2(rb[4 * j + 2], rb[4 * j + 3], kc, sc[j]);
               }
             } else if (kTokenScale) {
               // exact int32 dot -> float (all 64 first), then fl(dot * s_t); f16 operands accumulate the
@@ -1587,9 +1655,16 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
       else MSB_TC_GO(false, false, false, true, tc::Layout<false>);
     }
   } else if (d.token_scale) {
+    // biased accumulators unless a token scale is too large for the exact s * 2^23
+#define MSB_TC_BIAS(PRE)                                                                          \
+  go(tc::tc_scan_kernel<true, PRE, false, false, false, false, 0, true>,                          \
+     tc::tc_scan_kernel<true, PRE, false, false, true, false, 0, true>, tc::Layout<PRE, false, false, true>::bytes)
     if (f16) MSB_TC_GO(true, true, true, false, LayoutF16);
+    else if (pre && d.token_scale_small) MSB_TC_BIAS(true);
     else if (pre) MSB_TC_GO(true, true, false, false, tc::Layout<true>);
+    else if (d.token_scale_small) MSB_TC_BIAS(false);
     else MSB_TC_GO(true, false, false, false, tc::Layout<false>);
+#undef MSB_TC_BIAS
   } else {
     if (pre) MSB_TC_GO(false, true, false, false, tc::Layout<true>);
     else MSB_TC_GO(false, false, false, false, tc::Layout<false>);

@@ -209,6 +209,88 @@ void launch_topk_rows(const float* scores, int64_t ld, int rows, int64_t T, int 
   check(cudaGetLastError(), "launch top-k select kernel");
 }
 
+// Merge of per-shard top-k lists (multi-GPU search).  `gathered` holds `world` blocks of 16 * batch * k
+// bytes, one per rank in rank order, as one all-gather leaves them: the rank's [batch, k] fp32 scores at
+// byte 0 of its block and its [batch, k] int64 local document ids at byte 8 * batch * k.  Each rank's
+// row is ordered (score desc, id asc); global id = local id + first_doc[rank] (a local id of INT64_MAX
+// pads a shard holding fewer than k documents and stays INT64_MAX).  One warp per query row repeats k
+// times: every lane offers the best head among its ranks (lane, lane + 32, ...), a butterfly reduction
+// picks the winner in the single-GPU order (ordered score key desc, global id asc), and the winning
+// rank advances.  Shards are disjoint, so the result equals the top-k of the whole corpus.
+constexpr int kMergeWarps = 4;
+constexpr int kMergeMaxWorld = 1024;
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_shard_topk_kernel(
+    const unsigned char* __restrict__ gathered, int world, int batch, int k, const int64_t* __restrict__ first_doc,
+    float* __restrict__ out_s, int64_t* __restrict__ out_id) {
+  __shared__ int pos_all[kMergeWarps][kMergeMaxWorld];
+  const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kMergeWarps + wib;
+  if (row >= batch) return;
+  int* pos = pos_all[wib];
+  for (int r = lane; r < world; r += 32) pos[r] = 0;
+  __syncwarp();
+  const size_t blk = 16ull * static_cast<size_t>(batch) * k;
+  const size_t row_off = static_cast<size_t>(row) * k;
+  auto head = [&](int r, uint32_t& key, int64_t& gid) {
+    const int p = pos[r];
+    const unsigned char* b = gathered + static_cast<size_t>(r) * blk;
+    key = float_to_ordered(reinterpret_cast<const float*>(b)[row_off + p]);
+    const int64_t lid = reinterpret_cast<const int64_t*>(b + 8ull * batch * k)[row_off + p];
+    gid = lid == INT64_MAX ? INT64_MAX : lid + first_doc[r];
+  };
+  for (int j = 0; j < k; ++j) {
+    bool have = false;
+    uint32_t bk = 0;
+    int64_t bg = INT64_MAX;
+    int br = -1;
+    for (int r = lane; r < world; r += 32) {
+      if (pos[r] >= k) continue;
+      uint32_t key;
+      int64_t gid;
+      head(r, key, gid);
+      if (!have || key > bk || (key == bk && gid < bg)) {
+        have = true;
+        bk = key;
+        bg = gid;
+        br = r;
+      }
+    }
+#pragma unroll
+    for (int delta = 16; delta > 0; delta >>= 1) {
+      const int oh = __shfl_xor_sync(0xFFFFFFFFu, have ? 1 : 0, delta);
+      const uint32_t ok = __shfl_xor_sync(0xFFFFFFFFu, bk, delta);
+      const int64_t og = __shfl_xor_sync(0xFFFFFFFFu, bg, delta);
+      const int orr = __shfl_xor_sync(0xFFFFFFFFu, br, delta);
+      if (oh && (!have || ok > bk || (ok == bk && (og < bg || (og == bg && orr < br))))) {
+        have = true;
+        bk = ok;
+        bg = og;
+        br = orr;
+      }
+    }
+    // every lane now holds the winner (ties between lanes resolved by rank, identically everywhere)
+    if (lane == 0) {
+      out_s[row_off + j] = have ? ordered_to_float(bk) : -INFINITY;
+      out_id[row_off + j] = bg;
+    }
+    if (have && lane == (br & 31)) ++pos[br];
+    __syncwarp();
+  }
+}
+
+void launch_merge_shard_topk(const void* gathered, int world, int batch, int k, const int64_t* first_doc,
+                             float* out_s, int64_t* out_id, cudaStream_t stream) {
+  if (world < 1 || world > kMergeMaxWorld) throw InvalidArgument("world must be between 1 and 1024");
+  if (k < 1) throw InvalidArgument("k must be >= 1");
+  if (batch < 0) throw InvalidArgument("batch must be >= 0");
+  if (batch == 0) return;
+  const int blocks = (batch + kMergeWarps - 1) / kMergeWarps;
+  merge_shard_topk_kernel<<<blocks, kMergeWarps * 32, 0, stream>>>(static_cast<const unsigned char*>(gathered), world,
+                                                                   batch, k, first_doc, out_s, out_id);
+  count_launch();
+  check(cudaGetLastError(), "launch shard merge kernel");
+}
+
 // out[b, j] = scores[b, ids[j]] (shared list) or scores[b, ids[b * count + j]] (per-row lists): the scores
 // of candidate lists read out of a full scan.
 __global__ void gather_scores_kernel(const float* __restrict__ scores, int64_t ld, int rows,

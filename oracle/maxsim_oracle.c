@@ -17,6 +17,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #ifdef _OPENMP
@@ -94,6 +95,73 @@ int oracle_int4_int8q_scores(const int8_t* qcodes, const float* qscales, int bat
     }
   }
   return 0;
+}
+
+/* The same scores as oracle_int4_int8q_scores (exact integer dots, then the identical fp32 epilogue
+ * sequence per (query, document)), organised for large corpora: threads take documents, each
+ * document's tokens are unpacked to int8 once and shared by every query row, and the integer dot is
+ * a plain loop the compiler vectorises (integer sums do not depend on their order). */
+int oracle_int4_int8q_scores_docs(const int8_t* qcodes, const float* qscales, int batch, int qtok, int dim,
+                                  const uint8_t* packed, const float* token_scale, float scale,
+                                  const int64_t* offsets, int64_t num_docs, const int64_t* targets,
+                                  int64_t num_targets, float* out, int threads) {
+  const int64_t T = targets ? num_targets : num_docs;
+  const int half = dim / 2;
+  int failed = 0;
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+#pragma omp parallel
+#endif
+  {
+    int8_t* buf = NULL;
+    int64_t cap = 0;
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 1)
+#endif
+    for (int64_t j = 0; j < T; ++j) {
+      int64_t d = targets ? targets[j] : j;
+      int64_t s = offsets[d], e = offsets[d + 1], n = e - s;
+      if (n > cap) {
+        free(buf);
+        buf = (int8_t*)malloc((size_t)n * (size_t)dim);
+        cap = buf ? n : 0;
+        if (!buf) {
+          failed = 1;
+          continue;
+        }
+      }
+      for (int64_t t = 0; t < n; ++t) {
+        const uint8_t* row = packed + (s + t) * half;
+        for (int i = 0; i < half; ++i) {
+          buf[t * dim + 2 * i] = (int8_t)nibble(row[i], 0);
+          buf[t * dim + 2 * i + 1] = (int8_t)nibble(row[i], 1);
+        }
+      }
+      for (int b = 0; b < batch; ++b) {
+        float acc = 0.0f;
+        if (n > 0 && qtok > 0) {
+          for (int r = 0; r < qtok; ++r) {
+            const int8_t* qc = qcodes + ((int64_t)b * qtok + r) * dim;
+            float best = -3.402823466e+38f;
+            for (int64_t t = 0; t < n; ++t) {
+              const int8_t* tok = buf + t * dim;
+              int32_t dot = 0;
+              for (int i = 0; i < dim; ++i) dot += (int32_t)qc[i] * (int32_t)tok[i];
+              volatile float v = (float)dot;
+              if (token_scale) v = v * token_scale[s + t];
+              best = v > best ? v : best;
+            }
+            volatile float c = best * qscales[(int64_t)b * qtok + r];
+            acc = acc + c;
+          }
+        }
+        volatile float res = acc * scale;
+        out[(int64_t)b * T + j] = res;
+      }
+    }
+    free(buf);
+  }
+  return failed ? -1 : 0;
 }
 
 /* Exact binary x int8 scores: dot = sum_i (bit_i ? q_i : -q_i). */

@@ -80,3 +80,43 @@ def test_two_gpu_sharded_search_equals_single_gpu(tmp_path, k, split):
     np.testing.assert_array_equal(got["i"], got["want_i"])
     np.testing.assert_array_equal(got["s"], got["want_s"])
     assert any(3 in row and 300 in row for row in got["i"])  # the cross-shard tie is inside the top-k
+
+
+@pytest.mark.parametrize("world,batch,k", [(2, 3, 10), (8, 64, 10), (40, 5, 7), (3, 2, 700)])
+def test_merge_kernel_equals_host_statement(world, batch, k):
+    """msb_merge_shard_topk_device on one GPU, fed a gathered buffer as the all-gather leaves it: ranks with
+    ties inside and across shards, a short shard padded with (-inf, INT64_MAX), more ranks than a warp has
+    lanes, and long lists; equal to the host statement of the merge."""
+    import ctypes
+
+    import torch
+
+    from maxsim_b200 import _lib
+    from maxsim_b200.sharded import merge_shard_topk_host, pack_shard_block
+
+    rng = np.random.default_rng(world * 100 + k)
+    sizes = rng.integers(k // 2, 3 * k, size=world)
+    sizes[0] = max(1, k // 3)  # a shard with fewer than k documents
+    first = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.int64)
+    blocks = []
+    for r in range(world):
+        # coarse scores so that ties are common, within and across shards
+        full = rng.integers(-20, 20, size=(batch, int(sizes[r]))).astype(np.float32) * np.float32(0.25)
+        s = np.full((batch, k), -np.inf, np.float32)
+        i = np.full((batch, k), np.iinfo(np.int64).max, np.int64)
+        for b in range(batch):
+            order = np.lexsort((np.arange(sizes[r]), -full[b]))[:k]
+            s[b, :len(order)], i[b, :len(order)] = full[b][order], order
+        blocks.append(pack_shard_block(s, i))
+    gathered = np.concatenate(blocks)
+    want_s, want_i = merge_shard_topk_host(gathered, world, batch, k, first)
+    g = torch.from_numpy(gathered).cuda()
+    fd = torch.from_numpy(first).cuda()
+    out_s = torch.empty((batch, k), dtype=torch.float32, device="cuda")
+    out_i = torch.empty((batch, k), dtype=torch.int64, device="cuda")
+    _lib.check(_lib.lib.msb_merge_shard_topk_device(ctypes.c_void_p(g.data_ptr()), world, batch, k,
+                                                    ctypes.c_void_p(fd.data_ptr()), ctypes.c_void_p(out_s.data_ptr()),
+                                                    ctypes.c_void_p(out_i.data_ptr()), None))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out_i.cpu().numpy(), want_i)
+    np.testing.assert_array_equal(out_s.cpu().numpy(), want_s)

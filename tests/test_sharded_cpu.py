@@ -1,12 +1,13 @@
 """Document-sharded search on CPU ranks (gloo): shard planning and the merge protocol.
 
 The GPU path (``ShardedReranker.search_device``) scans a contiguous document
-shard per rank, keeps a local top-k with global ids padded to exactly k
-entries with (-inf, INT64_MAX), all-gathers the ``[B, k]`` lists and merges
-them in (score desc, id asc) order.  These tests run that protocol with two
-gloo ranks, local scores from the oracle, and check that the merged result is
-identical to the single-process top-k over the whole corpus, including ties
-across the shard boundary and a shard holding fewer than k documents.
+shard per rank, writes its local top-k (local ids, padded to exactly k entries
+with (-inf, INT64_MAX)) into one send block, all-gathers the blocks and merges
+them in (score desc, global id asc) order.  These tests run that protocol with
+two gloo ranks, local scores from the oracle and the host statement of the
+merge kernel, and check that the merged result is identical to the
+single-process top-k over the whole corpus, including ties across the shard
+boundary and a shard holding fewer than k documents.
 """
 
 import os
@@ -15,7 +16,8 @@ import socket
 import numpy as np
 import pytest
 
-from maxsim_b200.sharded import merge_topk_host, shard_bounds, shard_offsets
+from maxsim_b200.sharded import (merge_shard_topk_host, merge_topk_host, pack_shard_block, shard_bounds,
+                                 shard_offsets)
 from oracle import reference_cpu as ref
 
 
@@ -58,6 +60,16 @@ def test_merge_orders_ties_by_global_id_and_skips_padding():
     np.testing.assert_array_equal(s, [[3.0, 3.0, 2.0]])
 
 
+def test_shard_block_merge_adds_first_documents_and_keeps_padding():
+    neg = np.float32(-np.inf)
+    big = np.iinfo(np.int64).max
+    b0 = pack_shard_block(np.array([[3.0, 1.0, neg]], np.float32), np.array([[7, 2, big]], np.int64))
+    b1 = pack_shard_block(np.array([[3.0, 2.0, 1.0]], np.float32), np.array([[0, 5, 6]], np.int64))
+    s, i = merge_shard_topk_host(np.concatenate([b0, b1]), 2, 1, 3, [0, 4])
+    np.testing.assert_array_equal(i, [[4, 7, 9]])
+    np.testing.assert_array_equal(s, [[3.0, 3.0, 2.0]])
+
+
 def _corpus(seed=11):
     rng = np.random.default_rng(seed)
     off = _offsets(rng, 23, 0, 30)
@@ -90,12 +102,11 @@ def _rank_main(rank, world, port, k, bounds, result_path):
         s, i = ref.topk_rows(loc_scores, k_local)
         pad_s = np.full((q.shape[0], k), -np.inf, np.float32)
         pad_i = np.full((q.shape[0], k), np.iinfo(np.int64).max, np.int64)
-        pad_s[:, :k_local], pad_i[:, :k_local] = s, i + lo
-        all_s = [torch.empty((q.shape[0], k), dtype=torch.float32) for _ in range(world)]
-        all_i = [torch.empty((q.shape[0], k), dtype=torch.int64) for _ in range(world)]
-        dist.all_gather(all_s, torch.from_numpy(pad_s))
-        dist.all_gather(all_i, torch.from_numpy(pad_i))
-        ms, mi = merge_topk_host(torch.stack(all_s).numpy(), torch.stack(all_i).numpy(), k)
+        pad_s[:, :k_local], pad_i[:, :k_local] = s, i  # local ids; the merge adds the rank's first document
+        send = torch.from_numpy(pack_shard_block(pad_s, pad_i))
+        blocks = [torch.empty_like(send) for _ in range(world)]
+        dist.all_gather(blocks, send)
+        ms, mi = merge_shard_topk_host(torch.cat(blocks).numpy(), world, q.shape[0], k, bounds[:-1])
         if rank == 0:
             np.savez(result_path, s=ms, i=mi)
     finally:

@@ -121,3 +121,31 @@ def test_noalloc_rejects_work_beyond_its_scratch():
     with pytest.raises(ValueError, match="fixed scratch"):
         _topk(_lib.lib.msb_docs_topk_device_noalloc, h, q, 5, _opts(query_mode=_lib.QUERY_I8),
               torch.cuda.Stream())
+
+
+def test_noalloc_refuses_host_pointers():
+    """A pageable host buffer given as an output (or as the query) is refused before anything is queued:
+    the kernels would otherwise dereference it on the GPU."""
+    import torch
+
+    from maxsim_b200 import _lib
+
+    rng = np.random.default_rng(8)
+    h = _handle_int4(rng, 300)
+    q = torch.from_numpy(rng.standard_normal((2, 8, 128)).astype(np.float32)).cuda()
+    s = torch.empty((2, 5), dtype=torch.float32, device="cuda")
+    i = torch.empty((2, 5), dtype=torch.int64, device="cuda")
+    host_s = np.empty((2, 5), np.float32)
+    host_q = np.zeros((2, 8, 128), np.float32)
+    stream = torch.cuda.Stream()
+    opts = _opts(query_mode=_lib.QUERY_I8)
+    fn = _lib.lib.msb_docs_topk_device_noalloc
+    with pytest.raises(ValueError, match="host pointer|not a CUDA pointer"):
+        _lib.check(fn(h.device_handle, ctypes.c_void_p(q.data_ptr()), 2, 8, 5, ctypes.byref(opts),
+                      ctypes.c_void_p(host_s.ctypes.data), ctypes.c_void_p(i.data_ptr()),
+                      ctypes.c_void_p(stream.cuda_stream)))
+    with pytest.raises(ValueError, match="host pointer|not a CUDA pointer"):
+        _lib.check(fn(h.device_handle, ctypes.c_void_p(host_q.ctypes.data), 2, 8, 5, ctypes.byref(opts),
+                      ctypes.c_void_p(s.data_ptr()), ctypes.c_void_p(i.data_ptr()),
+                      ctypes.c_void_p(stream.cuda_stream)))
+    stream.synchronize()
