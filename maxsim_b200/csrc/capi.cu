@@ -32,13 +32,17 @@ void launch_tc_scan(const DocsView&, const QueryView&, const ReduceView&, const 
                     size_t ws_bytes, cudaStream_t);
 size_t tc_scan_workspace_bytes(const DocsView&, const QueryView&, const TargetsView&);
 bool tc_int8_cache_supported(const DocsView&);
+bool popc_scan_supported(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, bool residual);
+size_t popc_scan_workspace_bytes(const QueryView&);
+void launch_popc_scan(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, float*, void* ws,
+                      size_t ws_bytes, cudaStream_t);
 void launch_expand_codes8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t);
 void launch_expand_binary8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t);
 void launch_expand_codes16(const uint8_t* codes, int64_t num_tokens, uint16_t* out, cudaStream_t);
 
 static std::atomic<int64_t> g_launches{0};
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
-static std::atomic<int> g_engine{0};  // 0 auto, 1 SIMT, 2 tensor core
+static std::atomic<int> g_engine{0};  // 0 auto, 1 SIMT, 2 tensor core, 3 popcount (sign codes)
 static std::atomic<int> g_tc_int8_cache{1};  // keep an int8-expanded copy of int4 corpora for the tc engine
 static std::atomic<int> g_tc_f16_cache{0};   // keep an f16 copy instead (per-token scales): no conversion in the
                                              // epilogue, but twice the MMAs and operand bytes; measured slower
@@ -139,7 +143,7 @@ struct msb_docs {
   DeviceBuf codes, offsets, token_scale, doc_scale, residual_codes, residual_token_scale;
   // Workspace (grows monotonically, reused across calls).
   DeviceBuf w_query, w_qcodes, w_qwords, w_qscale, w_qsum, w_scores, w_cands, w_weights, w_top_s, w_top_i,
-      w_override, w_fine, w_tc,
+      w_override, w_fine, w_tc, w_popc,
       w_full;  // full-scan scores that candidate lists are gathered from
   std::vector<int64_t> host_offsets;
   bool tc_used = false;  // the tensor-core engine ran since the last error check
@@ -173,7 +177,8 @@ struct msb_docs {
   int64_t workspace_bytes() const {
     return static_cast<int64_t>(w_query.cap + w_qcodes.cap + w_qwords.cap + w_qscale.cap + w_qsum.cap +
                                 w_scores.cap + w_cands.cap + w_weights.cap + w_top_s.cap + w_top_i.cap +
-                                w_override.cap + w_fine.cap + w_tc.cap + w_check.cap + w_full.cap);
+                                w_override.cap + w_fine.cap + w_tc.cap + w_check.cap + w_full.cap +
+                                w_popc.cap);
   }
   ~msb_docs() {
     int prev = -1;
@@ -183,7 +188,7 @@ struct msb_docs {
     DeviceBuf* all[] = {&codes,   &offsets,  &token_scale, &doc_scale, &residual_codes, &residual_token_scale,
                         &w_query, &w_qcodes, &w_qwords,    &w_qscale,  &w_qsum,         &w_scores,
                         &w_cands, &w_weights, &w_top_s,    &w_top_i,   &w_override,     &w_fine,
-                        &w_tc,    &codes8,   &codes16,   &w_check,        &codes2_8,  &w_full};
+                        &w_tc,    &codes8,   &codes16,   &w_check,        &codes2_8,  &w_full, &w_popc};
     for (DeviceBuf* b : all) b->release();
     for (cudaEvent_t& e : upload_events)
       if (e) cudaEventDestroy(e);
@@ -349,6 +354,26 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
   qv.qtok = qtok;
   qv.mode = r.mode;
   const int engine = g_engine.load();
+  if (engine == 3) {
+    // AND + popcount over the sign codes (forced; see popc_scan.cu)
+    if (!popc_scan_supported(r.docs, qv, r.red, tg, r.residual))
+      throw NotSupported("the popcount engine does not support this scan");
+    const int64_t rows = static_cast<int64_t>(batch) * qtok;
+    if (r.mode == kQueryI8) {
+      h->w_qcodes.ensure(static_cast<size_t>(rows) * h->dim, "cudaMalloc int8 query codes");
+      h->w_qwords.ensure(static_cast<size_t>(rows) * h->dim, "cudaMalloc int8 query words");
+      h->w_qscale.ensure(static_cast<size_t>(rows) * sizeof(float), "cudaMalloc int8 query scales");
+      h->w_qsum.ensure(static_cast<size_t>(rows) * sizeof(int32_t), "cudaMalloc int8 query sums");
+      launch_quantize_rows(d_query, rows, h->dim, h->w_qcodes.as<int8_t>(), h->w_qscale.as<float>(),
+                           h->w_qsum.as<int32_t>(), h->w_qwords.as<int32_t>(), false, stream);
+      qv.i8 = h->w_qcodes.as<int8_t>();
+      qv.row_scale = h->w_qscale.as<float>();
+    }
+    const size_t ws = popc_scan_workspace_bytes(qv);
+    h->w_popc.ensure(ws, "cudaMalloc popcount scan workspace");
+    launch_popc_scan(r.docs, qv, r.red, tg, d_out, h->w_popc.ptr, h->w_popc.cap, stream);
+    return;
+  }
   const bool tc_ok = tc_scan_supported(r.docs, qv, r.red, tg, r.residual);
   if (engine == 2 && !tc_ok) throw NotSupported("the tensor-core engine does not support this scan");
   bool use_tc = tc_ok && engine != 1;
@@ -567,7 +592,8 @@ int msb_set_option(const char* name, int64_t value) {
   return guarded([&] {
     if (!name) throw InvalidArgument("option name is NULL");
     if (std::strcmp(name, "engine") == 0) {
-      if (value < 0 || value > 2) throw InvalidArgument("engine must be 0 (auto), 1 (SIMT) or 2 (tensor core)");
+      if (value < 0 || value > 3)
+        throw InvalidArgument("engine must be 0 (auto), 1 (SIMT), 2 (tensor core) or 3 (popcount, sign codes)");
       g_engine.store(static_cast<int>(value));
       return;
     }

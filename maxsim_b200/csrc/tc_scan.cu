@@ -517,7 +517,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       mbar_init(&tile_done[s], 1);
     }
     for (int s = 0; s < kMeta; ++s) {
-      mbar_init(&m_full[s], kXWarps);
+      // kPre: the expanders' metadata and the MMA warp's commit of the tile's products (kXWarps + 1)
+      mbar_init(&m_full[s], kPre ? kXWarps + 1 : kXWarps);
       mbar_init(&m_empty[s], kTwin ? kEpiWarps / 2 : kEpiWarps);  // twin: only the owning group reads a tile
     }
     for (int s = 0; s < kRaw; ++s) {
@@ -779,10 +780,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           if (!kPre) mbar_arrive(&full[stg.idx]);
           mbar_arrive(&raw_empty[raw.idx]);
         }
-        // With TMA operand tiles, expander warp 0 also waits for the tile's MMAs, so that m_full tells the
-        // epilogue both that the metadata is written and that the accumulators are ready: one barrier
-        // wait per tile on the epilogue's critical path instead of two.
-        if (kPre && xwarp == 0 && !mbar_wait(&tile_done[stg.idx], stg.phase, abort_flag, p.error, 16)) goto done;
+        // With TMA operand tiles the MMA warp also commits the tile's products to m_full, so that one
+        // barrier tells the epilogue both that the metadata is written and that the accumulators are
+        // ready: one wait per tile on the epilogue's critical path, and no relay through this warp.
         if (lane == 0) mbar_arrive(&m_full[mst.idx]);
         raw.next<kRaw>();
         stg.next<L::stages>();
@@ -799,7 +799,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                                (static_cast<uint32_t>(128 >> 4) << 24);
     constexpr uint32_t idesc16 = (1u << 4) | (static_cast<uint32_t>(kTileN >> 3) << 17) |
                                  (static_cast<uint32_t>(128 >> 4) << 24);
-    Ring stg, acc;
+    Ring stg, acc, mst;
     int iter = 0;
     for (int w = blockIdx.x; w < p.num_items; w += gridDim.x, ++iter) {
       const Item it = load_item<kTwin>(p, w);
@@ -850,9 +850,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             }
           }
           mma_commit(&tile_done[stg.idx]);
+          if (kPre) mma_commit(&m_full[mst.idx]);  // the accumulators are ready for the epilogue
         }
         __syncwarp();
         stg.next<L::stages>();
+        mst.next<kMeta>();
         if (!kTwin || st.side == 1) acc.next<kAcc>();
       }
       if (lane == 0) mma_commit(&a_empty[abuf]);
@@ -921,7 +923,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         }
         if (!kPre && !mbar_wait(&tile_done[stg.idx], stg.phase, abort_flag, p.error, 31)) goto done;
         // Acquire the expanders' metadata writes for this tile (meta ring slot) and, with TMA operand
-        // tiles, the completion of its MMAs (observed by expander warp 0 before it arrives).
+        // tiles, the completion of its MMAs (the MMA warp's commit is the slot's last arrival).
         if (!mbar_wait(&m_full[mst.idx], mst.phase, abort_flag, p.error, 32)) goto done;
         tc_fence_after();
         const StageMeta* meta = reinterpret_cast<const StageMeta*>(smem + L::off_meta + mst.idx * kMetaBytes);

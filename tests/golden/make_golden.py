@@ -27,6 +27,7 @@ The fixtures are committed; the GPU box never needs the reference.
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.util
 import json
 import sys
@@ -71,8 +72,11 @@ def _ragged(num_docs, seed, dim=128, lo=1, hi=9, empty_at=2):
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", default=os.environ.get("MAXSIM_REFERENCE"),
+                        help="path of the reference source tree (or set MAXSIM_REFERENCE)")
     args = parser.parse_args()
+    if not args.reference:
+        parser.error("give --reference or set MAXSIM_REFERENCE")
     ref_root = Path(args.reference)
     ms = _load_reference(ref_root)
     from maxsim import cascade, experimental  # reference modules
