@@ -208,9 +208,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
                                           int code) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = global_ns();
-  // Roles other than the epilogue (codes < 30 or >= 40) back off so their
-  // waiting does not take issue slots from the epilogue warps.
-  const bool backoff = code < 30 || code >= 40;
+  // The loader and expander warps (codes < 20 or >= 40) back off so their waiting does not take issue
+  // slots from the epilogue warps; the MMA warp (20-29) and the epilogue (30-39) rely on try_wait's own
+  // suspension, so they resume as soon as the phase completes.
+  const bool backoff = code < 20 || code >= 40;
   uint32_t sleep_ns = 32;
   for (uint32_t it = 0;; ++it) {
     if (mbar_try(bar, parity)) return true;
@@ -249,25 +250,13 @@ __device__ __forceinline__ uint64_t umma_desc_plain(uint32_t saddr) {
 // (dot + kBiasValue) * 2^-23 - kBiasValue * 2^-23 = dot * 2^-23 exactly (|dot| < 2^17; subnormal
 // inputs are kept, no flush to zero), and the packed product dot * 2^-23 * (s * 2^23) is rounded once,
 // to the same float as fl(float(dot) * s).  Two instructions per two values, both on the FMA pipe.
-__device__ __forceinline__ uint64_t pack_f2(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-struct BiasConsts {
-  uint64_t mul, add;  // {2^126, 2^126}, {-kBiasValue * 2^-23, same}
-  __device__ __forceinline__ BiasConsts()
-      : mul(pack_f2(0x1p126F, 0x1p126F)),
-        add(pack_f2(-static_cast<float>(kBiasValue) / 8388608.0F, -static_cast<float>(kBiasValue) / 8388608.0F)) {}
-};
-__device__ __forceinline__ void bias_scale2(uint32_t& x0, uint32_t& x1, const BiasConsts& k, float2 s23) {
-  asm("{\n .reg .b64 v;\n"
-      " mov.b64 v, {%0, %1};\n"
-      " fma.rn.f32x2 v, v, %2, %3;\n"
-      " mul.rn.f32x2 v, v, %4;\n"
-      " mov.b64 {%0, %1}, v;\n}"
-      : "+r"(x0), "+r"(x1)
-      : "l"(k.mul), "l"(k.add), "l"(pack_f2(s23.x, s23.y)));
+__device__ __forceinline__ void bias_scale2(uint32_t& x0, uint32_t& x1, float2 s23) {
+  constexpr float kNeg = -static_cast<float>(kBiasValue) / 8388608.0F;  // -kBiasValue * 2^-23 (exact)
+  const float2 v = __fmul2_rn(__ffma2_rn(make_float2(__uint_as_float(x0), __uint_as_float(x1)),
+                                         make_float2(0x1p126F, 0x1p126F), make_float2(kNeg, kNeg)),
+                              s23);
+  x0 = __float_as_uint(v.x);
+  x1 = __float_as_uint(v.y);
 }
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
@@ -799,6 +788,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                                (static_cast<uint32_t>(128 >> 4) << 24);
     constexpr uint32_t idesc16 = (1u << 4) | (static_cast<uint32_t>(kTileN >> 3) << 17) |
                                  (static_cast<uint32_t>(128 >> 4) << 24);
+    // Descriptors are formed once: their start-address field is the shared-memory address / 16, so an
+    // operand offset of 32 bytes along K adds 2 and a stage offset adds stage * b_tile / 16 (addresses stay
+    // below 2^18, so the 14-bit field never carries into the next one).
+    const uint64_t b_desc0 = umma_desc(smem_u32(smem + L::off_b), 16u, 1024u);
+    const uint64_t c_desc = kBias ? umma_desc_plain(smem_u32(smem + L::off_bias)) : 0ull;
     Ring stg, acc, mst;
     int iter = 0;
     for (int w = blockIdx.x; w < p.num_items; w += gridDim.x, ++iter) {
@@ -834,18 +828,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 mma_f16(d_tmem, ad, bd, idesc16, k > 0 ? 1u : 0u);
               }
             } else {
-              if (kBias) {  // every accumulator opens at kBiasValue: constant x constant, K = 32
-                const uint64_t cd = umma_desc_plain(smem_u32(smem + L::off_bias));
-                mma_i8(d_tmem, cd, cd, idesc, 0u);
-              }
+              // every accumulator opens at kBiasValue: constant x constant, K = 32
+              if (kBias) mma_i8(d_tmem, c_desc, c_desc, idesc, 0u);
+              const uint64_t ad0 = umma_desc(ag, 16u, 1024u);
+              const uint64_t bd0 = b_desc0 + static_cast<uint64_t>((stg.idx * L::b_tile) >> 4);
 #pragma unroll
               for (int sm = 0; sm < kStreams; ++sm) {  // prefix tile; residual tile 16 KB after it
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  const uint64_t ad = umma_desc(ag + 32u * k, 16u, 1024u);
-                  const uint64_t bd = umma_desc(b_addr + static_cast<uint32_t>(sm * kBTileBytes) + 32u * k, 16u, 1024u);
-                  mma_i8(d_tmem + static_cast<uint32_t>(sm * kTileN), ad, bd, idesc, (kBias || k > 0) ? 1u : 0u);
-                }
+                for (int k = 0; k < 4; ++k)
+                  mma_i8(d_tmem + static_cast<uint32_t>(sm * kTileN), ad0 + 2u * k,
+                         bd0 + static_cast<uint64_t>((sm * kBTileBytes) >> 4) + 2u * k, idesc,
+                         (kBias || k > 0) ? 1u : 0u);
               }
             }
           }
@@ -1006,13 +999,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               }
             } else if (kBias) {
               // (dot + kBiasValue) bits -> fl(dot * s_t): two packed instructions per two columns
-              const BiasConsts kc;
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                bias_scale2(ra[4 * j], ra[4 * j + 1], kc, sc[j]);
-                bias_scale2(ra[4 * j + 2], ra[4 * j + 3], kc, sc[j]);
-                bias_scale2(rb[4 * j], rb[4 * j + 1], kc, sc[j]);
-                bias_scale2(rb[4 * j + 2], rb[4 * j + 3], kc, sc[j]);
+                bias_scale2(ra[4 * j], ra[4 * j + 1], sc[j]);
+                bias_scale2(ra[4 * j + 2], ra[4 * j + 3], sc[j]);
+                bias_scale2(rb[4 * j], rb[4 * j + 1], sc[j]);
+                bias_scale2(rb[4 * j + 2], rb[4 * j + 3], sc[j]);
               }
             } else if (kTokenScale) {
               // exact int32 dot -> float (all 64 first), then fl(dot * s_t); f16 operands accumulate the
