@@ -95,12 +95,40 @@ def _queries(rng, cent, batch, qtok, dim=DIM):
     return (q / np.linalg.norm(q, axis=2, keepdims=True)).astype(np.float32)
 
 
-def configs_bench(args):
-    """C0-C3 shapes of the reference's benchmarks (seeded synthetic data with their sizes and distributions),
+REF_CUDA_DIR = REPO / "baseline" / "_ref_cuda"
+
+
+def _reference_cuda_package():
+    """The reference package with its own CUDA extension, built for sm_100a from its sources into
+    baseline/_ref_cuda (``MAXSIM_BUILD_CUDA=1 MAXSIM_CUDA_ARCH=100a pip install --no-deps --target
+    baseline/_ref_cuda <reference>``); None when it is not installed."""
+    if not list((REF_CUDA_DIR / "maxsim").glob("_maxsim_cuda*.so")):
+        return None
+    sys.path.insert(0, str(REF_CUDA_DIR))
+    import maxsim  # the reference package
+
+    if maxsim._api._maxsim_cuda is None:
+        raise RuntimeError("the reference CUDA extension in baseline/_ref_cuda did not load")
+    return maxsim
+
+
+def configs_bench(args, impl="ours"):
+    """C0-C4 shapes of the reference's benchmarks (seeded synthetic data with their sizes and distributions),
     timed like the reference's harness: 5 warm-up calls, then 20 timed synchronous calls with host inputs
-    and outputs; median and p95 in ms."""
-    from maxsim_b200 import _api, cascade as casc, experimental as ex
-    from maxsim_b200.sdk import Index, Reranker
+    and outputs; median and p95 in ms.  ``impl="reference"`` runs the same calls through the reference's
+    own package and CUDA extension (built for sm_100a), on the same box; its test-only
+    ``streaming_topk_batch`` (a spin lock on a global flag) is never called."""
+    if impl == "reference":
+        mx = _reference_cuda_package()
+        if mx is None:
+            print(json.dumps({"configs": "all", "impl": "reference", "unavailable":
+                              "reference CUDA extension not installed in baseline/_ref_cuda"}), flush=True)
+            return
+        from maxsim import cascade as casc, experimental as ex
+        from maxsim.sdk import Index, Reranker
+    else:
+        from maxsim_b200 import cascade as casc, experimental as ex
+        from maxsim_b200.sdk import Index, Reranker
 
     def timed(fn, reps=20, warm=5):
         for _ in range(warm):
@@ -115,58 +143,95 @@ def configs_bench(args):
 
     def emit(cfg, op, p50, p95, note=""):
         ref = REF_4090_MS.get((cfg, op))
-        print(json.dumps({"configs": cfg, "op": op, "p50_ms": round(p50, 4), "p95_ms": round(p95, 4),
-                          "reference_rtx4090_p50_ms": ref, "speedup_vs_rtx4090": None if ref is None else round(ref / p50, 2),
-                          "note": note}), flush=True)
+        print(json.dumps({"configs": cfg, "impl": impl, "op": op, "p50_ms": round(p50, 4), "p95_ms": round(p95, 4),
+                          "reference_rtx4090_p50_ms": ref, "note": note}), flush=True)
 
+    only = set(args.configs_only.split(",")) if args.configs_only else None
     rng = np.random.default_rng(SEED ^ 0x51A7)
     # C0 / C3: 4,096 docs of U[64, 192] tokens, query [4, 32, 128] from 4 target docs
     docs, off, cent = _clustered(rng, 4096, 64, 192)
     q = _queries(rng, cent, 4, 32)
-    tok = ex.int4_to_device(ex.pack_int4_symmetric(docs, off, scale_granularity="token")).data
-    ten = ex.int4_to_device(ex.pack_int4_symmetric(docs, off, scale_granularity="tensor")).data
-    emit("C0", "int4 per-token full scan, fp32 query", *timed(lambda: tok.maxsim_batch(q)))
-    emit("C0", "int4 per-token full scan, int8 query", *timed(lambda: tok.maxsim_batch_int8q(q)))
-    emit("C0", "int4 per-token top-10, fp32 query", *timed(lambda: tok.topk_batch(q, 10)))
-    emit("C0", "int4 per-token top-10, int8 query", *timed(lambda: tok.topk_batch_int8q(q, 10)))
-    emit("C0", "int4 tensor-scale top-10, fp32 query", *timed(lambda: ten.topk_batch(q, 10)))
-    emit("C0", "int4 tensor-scale top-10, int8 query", *timed(lambda: ten.topk_batch_int8q(q, 10)))
-    cand = np.sort(rng.choice(4096, size=512, replace=False)).astype(np.int64)
-    emit("C0", "int4 per-token candidates fp32, M=512", *timed(lambda: tok.score_candidates_batch(q, cand)))
-    res = casc.residual_int4_to_device(casc.pack_residual_int4(docs, off)).prefix_data
-    emit("C0", "int4 residual fused full scan", *timed(lambda: res.score_residual_batch(q)))
-    emit("C0", "int4 residual candidates, M=512", *timed(lambda: res.score_residual_candidates_batch(q, cand)))
-    for m in (512, 1024, 2048):
-        emit("C3", f"int4-prefix cascade top-10, M={m}", *timed(lambda m=m: res.cascade_topk_batch(q, 10, m)))
-    bres = casc.binary_residual_to_device(casc.pack_binary_residual_int4(docs, off))
-    for m in (512, 1024, 2048):
-        emit("C3", f"binary-prefix cascade top-10, M={m}",
-             *timed(lambda m=m: casc.binary_cascade_topk(q, bres, 10, candidates=m, device="cuda")),
-             note="binary sign prefix + per-token int4 residual (no reference counterpart)")
-    del docs, tok, ten, res, bres
+    if only is None or "C0" in only or "C3" in only:
+        tok = ex.int4_to_device(ex.pack_int4_symmetric(docs, off, scale_granularity="token")).data
+        ten = ex.int4_to_device(ex.pack_int4_symmetric(docs, off, scale_granularity="tensor")).data
+        emit("C0", "int4 per-token full scan, fp32 query", *timed(lambda: tok.maxsim_batch(q)))
+        emit("C0", "int4 per-token full scan, int8 query", *timed(lambda: tok.maxsim_batch_int8q(q)))
+        emit("C0", "int4 per-token top-10, fp32 query", *timed(lambda: tok.topk_batch(q, 10)))
+        emit("C0", "int4 per-token top-10, int8 query", *timed(lambda: tok.topk_batch_int8q(q, 10)))
+        emit("C0", "int4 tensor-scale top-10, fp32 query", *timed(lambda: ten.topk_batch(q, 10)))
+        emit("C0", "int4 tensor-scale top-10, int8 query", *timed(lambda: ten.topk_batch_int8q(q, 10)))
+        cand = np.sort(rng.choice(4096, size=512, replace=False)).astype(np.int64)
+        emit("C0", "int4 per-token candidates fp32, M=512", *timed(lambda: tok.score_candidates_batch(q, cand)))
+        resp = casc.residual_int4_to_device(casc.pack_residual_int4(docs, off))
+        res = resp.prefix_data
+        emit("C0", "int4 residual fused full scan", *timed(lambda: res.score_residual_batch(q)))
+        emit("C0", "int4 residual candidates, M=512", *timed(lambda: res.score_residual_candidates_batch(q, cand)))
+        for m in (512, 1024, 2048):
+            emit("C3", f"int4-prefix cascade top-10, M={m}",
+                 *timed(lambda m=m: casc.cascade_topk(q, resp, 10, candidates=m, device="cuda")))
+        if impl == "ours":
+            bres = casc.binary_residual_to_device(casc.pack_binary_residual_int4(docs, off))
+            for m in (512, 1024, 2048):
+                emit("C3", f"binary-prefix cascade top-10, M={m}",
+                     *timed(lambda m=m: casc.binary_cascade_topk(q, bres, 10, candidates=m, device="cuda")),
+                     note="binary sign prefix + per-token int4 residual (no reference counterpart)")
+            del bres
+        del tok, ten, res, resp
+    del docs
     # C1 / C2: 10,171 docs of U[400, 800] tokens, 256 queries x 20 tokens
     docs, off, cent = _clustered(rng, 10171, 400, 800)
     q256 = _queries(rng, cent, 256, 20)
     ids = [f"d{i}" for i in range(10171)]
-    rr = Reranker(Index.from_embeddings(ids, docs, off, mode="int4"), device="cuda", int4_query="int8")
-    emit("C1", "SDK search, tensor int4 + int8 query, 256 queries one by one",
-         *timed(lambda: [rr.search(q256[i], k=10) for i in range(256)], reps=3, warm=1))
-    h1 = rr.corpus.int4_packed.data
-    emit("C1", "tensor int4 top-10, int8 query, 8 batches of 32",
-         *timed(lambda: [h1.topk_batch_int8q(q256[i:i + 32], 10) for i in range(0, 256, 32)], reps=5, warm=2))
-    del rr, h1
-    for mode, label in (("binary", "binary (max_speed)"), ("binary_token_scale", "binary + fp16 token scale (balanced)")):
-        rb = Reranker(Index.from_embeddings(ids, docs, off, mode=mode), device="cuda")
-        emit("C2", f"SDK search, {label}, 256 queries one by one",
-             *timed(lambda: [rb.search(q256[i], k=10) for i in range(256)], reps=3, warm=1))
-        hb = rb.corpus.packed.data
-        w = rng.uniform(0.5, 1.5, size=20).astype(np.float32)
-        use_ts = mode == "binary_token_scale"
-        for red, kw in (("maxsim", {}), ("weighted_maxsim", {"query_weights": w}), ("topk2", {}), ("topk4", {}),
-                        ("smoothsim", {"temperature": 0.1})):
-            emit("C2", f"{label} full scan, reducer {red}, 256 queries in one batch",
-                 *timed(lambda red=red, kw=kw: hb.score_batch(q256, reducer=red, use_token_scale=use_ts, **kw), reps=5, warm=2))
-        del rb, hb
+    if only is None or "C1" in only:
+        rr = Reranker(Index.from_embeddings(ids, docs, off, mode="int4"), device="cuda", int4_query="int8")
+        emit("C1", "SDK search, tensor int4 + int8 query, 256 queries one by one",
+             *timed(lambda: [rr.search(q256[i], k=10) for i in range(256)], reps=3, warm=1))
+        h1 = rr.corpus.int4_packed.data
+        emit("C1", "tensor int4 top-10, int8 query, 8 batches of 32",
+             *timed(lambda: [h1.topk_batch_int8q(q256[i:i + 32], 10) for i in range(0, 256, 32)], reps=5, warm=2))
+        del rr, h1
+    if only is None or "C2" in only:
+        for mode, label in (("binary", "binary (max_speed)"),
+                            ("binary_token_scale", "binary + fp16 token scale (balanced)")):
+            rb = Reranker(Index.from_embeddings(ids, docs, off, mode=mode), device="cuda")
+            emit("C2", f"SDK search, {label}, 256 queries one by one",
+                 *timed(lambda: [rb.search(q256[i], k=10) for i in range(256)], reps=3, warm=1))
+            hb = rb.corpus.packed.data
+            w = rng.uniform(0.5, 1.5, size=20).astype(np.float32)
+            use_ts = mode == "binary_token_scale"
+            for red, kw in (("maxsim", {}), ("weighted_maxsim", {"query_weights": w}), ("topk2", {}), ("topk4", {}),
+                            ("smoothsim", {"temperature": 0.1})):
+                emit("C2", f"{label} full scan, reducer {red}, 256 queries in one batch",
+                     *timed(lambda red=red, kw=kw: hb.score_batch(q256, reducer=red, use_token_scale=use_ts, **kw),
+                            reps=5, warm=2))
+            del rb, hb
+    del docs
+    if only is None or "C4" in only:
+        # C4: the bench corpus (100,000 pages x 1,030 tokens, per-token int4), host arrays into each
+        # implementation's handle, one 64-query batch of make_queries, int8 queries, top-10
+        import torch
+
+        from maxsim_b200 import _lib  # corpus generation only (the device packer, bit-exact with the reference's)
+
+        dev = torch.device("cuda", 0)
+        codes_d, scales_d = build_shard(torch, _lib, 0, NUM_PAGES, dev)
+        codes_h, scales_h = codes_d.cpu().numpy(), scales_d.cpu().numpy()
+        del codes_d, scales_d
+        torch.cuda.empty_cache()
+        qd, _ = make_queries(torch, dev)
+        q64 = qd[:BATCH].cpu().numpy()
+        offs = np.arange(NUM_PAGES + 1, dtype=np.int64) * PAGE_TOKENS
+        if impl == "reference":
+            h = mx._api._maxsim_cuda.CudaInt4PackedDocs(codes_h, offs, DIM, 1.0)
+        else:
+            from maxsim_b200 import _maxsim_cuda as mc
+
+            h = mc.CudaInt4PackedDocs(codes_h, offs, DIM, 1.0)
+        h.set_token_scale_vector(scales_h)
+        del codes_h, scales_h
+        emit("C4", "int4 per-token top-10, int8 query, one batch of 64 x 24 (100,000 pages)",
+             *timed(lambda: h.topk_batch_int8q(q64, 10), reps=5, warm=2))
+        del h
 
 
 def batch_sweep(args, torch, _lib, handle, queries, device):
@@ -467,6 +532,9 @@ def main() -> None:
     ap.add_argument("--engine", type=int, default=0, help="0 auto, 1 SIMT, 2 tensor core")
     ap.add_argument("--pages", type=int, default=NUM_PAGES,
                     help="corpus pages (default: the C4 workload; smaller values are for profiling captures)")
+    ap.add_argument("--configs-impl", choices=["ours", "reference"], default="ours",
+                    help="--configs through this library or through the reference's own CUDA build (baseline/_ref_cuda)")
+    ap.add_argument("--configs-only", default=None, help="comma-separated subset of C0,C1,C2,C3,C4 for --configs")
     ap.add_argument("--configs", action="store_true",
                     help="time the reference's smaller benchmark shapes (C0-C3) through the handle and SDK calls "
                          "the reference's own benchmarks time, one JSON line per operation, instead of the bench line")
@@ -495,7 +563,7 @@ def main() -> None:
     if args.configs:
         if rank == 0:
             torch.cuda.set_device(local_rank)
-            configs_bench(args)
+            configs_bench(args, args.configs_impl)
         return
 
     _lib.set_engine(args.engine)

@@ -80,6 +80,8 @@ def _prefix_view(packed: ResidualInt4PackedDocs) -> Int4PackedDocs:
 def _validate_residual_packed(packed: ResidualInt4PackedDocs, *, verify_packed_values: bool = False) -> None:
     if not isinstance(packed, ResidualInt4PackedDocs):
         raise TypeError("packed must be a ResidualInt4PackedDocs instance")
+    if packed.device == "cuda" and getattr(packed, "_msb_validated", False):
+        return  # a resident corpus is immutable once validated: no O(N) host checks per call
     prefix = _prefix_view(packed)
     _validate_int4_packed(prefix)
     if verify_packed_values:
@@ -145,11 +147,14 @@ def residual_int4_to_device(packed: ResidualInt4PackedDocs, device: str = "cuda"
     prefix.data.set_residual_int4(np.ascontiguousarray(packed.residual_data, dtype=np.uint8),
                                   float(packed.residual_scale),
                                   np.ascontiguousarray(packed.residual_token_scale, dtype=np.float32))
-    return ResidualInt4PackedDocs(
+    resident = ResidualInt4PackedDocs(
         prefix_data=prefix.data, prefix_values=None, prefix_scale=prefix.scale, prefix_token_scale=prefix.token_scale,
         residual_data=prefix.data, residual_values=None, residual_scale=packed.residual_scale,
         residual_token_scale=packed.residual_token_scale.copy(), doc_offsets=packed.doc_offsets.copy(),
         dim=packed.dim, num_docs=packed.num_docs, device="cuda")
+    _validate_residual_packed(resident)
+    object.__setattr__(resident, "_msb_validated", True)
+    return resident
 
 
 def _normalize_query(query_tokens, dim: int):

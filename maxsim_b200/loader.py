@@ -300,6 +300,7 @@ def load_resident_corpus(path, *, doc_range: tuple[int, int] | None = None, chun
             residual_data=handle, residual_values=None, residual_scale=residual_scale,
             residual_token_scale=residual_token_scale, doc_offsets=local_offsets, dim=dim,
             num_docs=len(local_ids), device="cuda")
+        object.__setattr__(payload, "_msb_validated", True)  # checked on the device and from the headers
     else:
         payload = Int4PackedDocs(data=handle, values=None, doc_offsets=local_offsets, dim=dim,
                                  num_docs=len(local_ids), scale=prefix_scale, device="cuda",
