@@ -383,7 +383,8 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
     // the int8 copy (int4 expanded, or +-1 for sign codes).  int4 corpora fall back to expanding per
     // tile when there is no memory for a copy; binary corpora fall back to the SIMT engine.
     const bool binary = h->format == kFormatBinary;
-    const bool topk = r.red.reducer == kTopK2 || r.red.reducer == kTopK4;  // its kernels read the int8 copy
+    // TopK and SmoothSim kernels read the int8 copy
+    const bool topk = r.red.reducer == kTopK2 || r.red.reducer == kTopK4 || r.red.reducer == kSmooth;
     if (!binary && !r.residual && !topk && g_tc_f16_cache.load() && !h->codes16_failed && dv.token_scale &&
         tc_int8_cache_supported(dv)) {
       if (!h->codes16.ptr) {

@@ -55,6 +55,7 @@
 //   * kRes: the fused two-stream residual (int4 or sign-code prefix + int4 residual), two accumulators
 //     per query tile.
 //   * kTopK: the TopK2 / TopK4 reducers, per-thread lists merged across a row's four threads.
+//   * kSmooth: the SmoothSim reducer, a running log-sum-exp per thread merged across a row's four threads.
 //
 // Every mbarrier wait is bounded (%globaltimer); on timeout the kernel raises
 // an error flag, drains, frees its TMEM and returns.
@@ -118,6 +119,8 @@ struct Params {
   int64_t num_docs;           // output row stride
   float* out;                 // [B, num_docs]
   int* error;                 // set to a non-zero code on timeout
+  float smooth_scale;         // SmoothSim: the document scale applied to every value before the reduction
+  float temperature;          // SmoothSim: the temperature (> 0)
 };
 
 // Shared-memory layout (bytes, from a 1024-aligned base).
@@ -459,7 +462,7 @@ __device__ __forceinline__ Step step_of(const Item& it, int64_t i) {
 // conversion and a product per value; the token scales are staged as s * 2^23 (the host keeps this
 // variant for corpora whose token scales are below 2^104, so that s * 2^23 is exact).
 template <bool kTokenScale, bool kPre, bool kF16, bool kDigits = false, bool kTwin = false, bool kRes = false,
-          int kTopK = 0, bool kBias = false>
+          int kTopK = 0, bool kBias = false, bool kSmooth = false>
 __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap,
                                                               const __grid_constant__ CUtensorMap tmap2) {
   using L = Layout<kPre, kF16, kRes, kBias>;
@@ -467,6 +470,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 "biased accumulators: int8 queries with per-token scales");
   static_assert(!kRes || (kPre && kDigits && kTokenScale && !kF16), "the residual stream reads both int8 copies");
   static_assert(kTopK == 0 || (kTopK <= 4 && kPre && kDigits && !kRes), "TopK: digit-plane queries, int8 copies");
+  static_assert(!kSmooth || (kTopK == 0 && kPre && kDigits && !kRes), "SmoothSim: digit-plane queries, int8 copies");
+  constexpr bool kList = kTopK > 0 || kSmooth;     // reducers that take the per-segment path in every chunk
   constexpr int kTk = kTopK > 0 ? kTopK : 1;
   constexpr int kAcc = kRes ? 1 : kAccBufs;         // accumulator buffers
   constexpr int kStreams = kRes ? 2 : 1;            // accumulators per query tile
@@ -901,6 +906,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       float run[4] = {kLowest, kLowest, kLowest, kLowest};                // open document, per row
       float tk[kTk];                                                      // TopK: open document's list
       int tk_cnt = 0;                                                     // TopK: its tokens in my columns
+      float sm_m = kLowest, sm_s = 0.0F;                                  // SmoothSim: open document's state
+      const float sm_v = qs * p.smooth_scale;                             // SmoothSim: digit units -> values
+      // exponent units in base 2: exp((v - m) / t) = exp2((u - m_u) * qscale * scale * log2(e) / t)
+      const float sm_c = sm_v * 1.4426950408889634F / p.temperature;
 #pragma unroll
       for (int i = 0; i < kTk; ++i) tk[i] = kLowest;
       int32_t run_i[4] = {INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN};    // tensor-scale variant
@@ -1027,7 +1036,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               }
             }
           }
-          if (!kTopK && nseg == 0 && tile_live && c1 == c0 + 64) {
+          if (!kList && nseg == 0 && tile_live && c1 == c0 + 64) {
             // no document ends in this tile and the open document covers the whole chunk: no walk
             if (kFloat) {
               run[0] = row_max16(ra, 0, run[0]);
@@ -1050,7 +1059,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           while (true) {
             const int e = nseg == 0 ? 0x7FFF : (sgi < nseg ? meta->seg_end[sgi] : 0x7FFF);
             const int bnd = min(e, c1);
-            const bool split = !kTopK && kFloat && tile_live && a == c0 && c1 == c0 + 64 && e > c0 && e < c1 &&
+            const bool split = !kList && kFloat && tile_live && a == c0 && c1 == c0 + 64 && e > c0 && e < c1 &&
                                (sgi + 1 < nseg ? meta->seg_end[sgi + 1] : 0x7FFF) > c1;
             if (split) {
               // Exactly one document ends strictly inside the chunk: one pass sends each value to the
@@ -1082,7 +1091,38 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               carry = true;
               a = e;
             } else if (bnd > a && tile_live) {
-              if (kTopK) {
+              if (kSmooth) {
+                // columns [a, bnd) of the open document into this thread's running log-sum-exp, in the
+                // row's digit-plane units u (v = u * qscale * scale): the segment's maximum first, then
+                // s = s * 2^((m - m') c) + sum 2^((u - m') c), c = qscale * scale * log2(e) / temperature
+                const int la = a - c0 - 2 * tc, lb = bnd - c0 - 2 * tc;
+                float mx = kLowest;
+                bool any = false;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+#pragma unroll
+                  for (int b2 = 0; b2 < 2; ++b2) {
+                    const int cc = 8 * j + b2;
+                    const bool in = cc >= la && cc < lb;
+                    mx = in ? fmaxf(mx, __uint_as_float(ra[4 * j + b2])) : mx;
+                    any = any || in;
+                  }
+                }
+                if (any) {
+                  const float mn = fmaxf(sm_m, mx);
+                  float acc_s = sm_s > 0.0F ? sm_s * exp2f((sm_m - mn) * sm_c) : 0.0F;
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) {
+#pragma unroll
+                    for (int b2 = 0; b2 < 2; ++b2) {
+                      const int cc = 8 * j + b2;
+                      if (cc >= la && cc < lb) acc_s += exp2f((__uint_as_float(ra[4 * j + b2]) - mn) * sm_c);
+                    }
+                  }
+                  sm_m = mn;
+                  sm_s = acc_s;
+                }
+              } else if (kTopK) {
                 // columns [a, bnd) of the open document into this thread's list
                 const int la = a - c0 - 2 * tc, lb = bnd - c0 - 2 * tc;
 #pragma unroll
@@ -1141,7 +1181,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             // document meta->seg_doc[sgi] ends: complete each row's maximum across the four threads
             // holding it, stage the row value scaled by the query scale, flush finished documents.
             float best;
-            if (kTopK) {
+            if (kSmooth) {
+              // merge the four threads' (maximum, sum) pairs, then max + temperature * log(sum) in the
+              // document's units
+#pragma unroll
+              for (int delta = 1; delta <= 2; delta <<= 1) {
+                const float om = __shfl_xor_sync(0xFFFFFFFFu, sm_m, delta);
+                const float os = __shfl_xor_sync(0xFFFFFFFFu, sm_s, delta);
+                const float mn = fmaxf(sm_m, om);
+                sm_s = (sm_s > 0.0F ? sm_s * exp2f((sm_m - mn) * sm_c) : 0.0F) +
+                       (os > 0.0F ? os * exp2f((om - mn) * sm_c) : 0.0F);
+                sm_m = mn;
+              }
+              best = sm_s > 0.0F ? sm_m * sm_v + p.temperature * logf(sm_s) : 0.0F;
+            } else if (kTopK) {
               // merge the four threads' lists and counts, then the mean of the top min(K, tokens)
 #pragma unroll
               for (int delta = 1; delta <= 2; delta <<= 1) {
@@ -1174,7 +1227,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               const int32_t bi = tc == 0 ? run_i[0] : tc == 1 ? run_i[1] : tc == 2 ? run_i[2] : run_i[3];
               best = bi == INT32_MIN ? kLowest : __int2float_rn(bi);
             }
-            if (w_store) rowval[(pending * kG + g) * 128 + wrow] = w_valid ? __fmul_rn(best, qs) : 0.0F;
+            if (w_store) rowval[(pending * kG + g) * 128 + wrow] = w_valid ? (kSmooth ? best : __fmul_rn(best, qs)) : 0.0F;
             if (ftid == 0) gdoc[pending] = meta->seg_doc[sgi];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -1184,6 +1237,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
 #pragma unroll
             for (int i = 0; i < kTk; ++i) tk[i] = kLowest;
             tk_cnt = 0;
+            sm_m = kLowest;
+            sm_s = 0.0F;
             if (carry) {
               carry = false;
               a = c1;
@@ -1497,7 +1552,8 @@ bool tc_scan_supported(const DocsView& d, const QueryView& q, const ReduceView& 
   // weighted MaxSim of fp32 queries: the weights fold into the digit planes' row scales
   // TopK2 / TopK4 of fp32 queries: per-row lists in the epilogue (not with the residual stream)
   const bool reducer_ok = r.reducer == kMaxSim || (r.reducer == kWeighted && q.mode == kQueryF32) ||
-                          ((r.reducer == kTopK2 || r.reducer == kTopK4) && q.mode == kQueryF32 && !residual);
+                          ((r.reducer == kTopK2 || r.reducer == kTopK4 || r.reducer == kSmooth) &&
+                           q.mode == kQueryF32 && !residual);
   // the fused residual stream: an int4 or sign-code prefix and an int4 residual, per-token scales on both,
   // fp32 queries (a sign-code prefix has scale 1, so its term is fl(v1 * s1) as in the SIMT kernel)
   const bool residual_ok = !residual || ((d.format == kFormatInt4 || d.format == kFormatBinary) &&
@@ -1612,6 +1668,15 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
     throw CudaFailure("residual tensor-core scan without its int8 copies");
   const int topk = red.reducer == kTopK2 ? 2 : (red.reducer == kTopK4 ? 4 : 0);
   if (topk && !(digits && d.codes8 && !res)) throw CudaFailure("TopK tensor-core scan without the int8 copy");
+  const bool smooth = red.reducer == kSmooth;
+  if (smooth && !(digits && d.codes8 && !res)) throw CudaFailure("SmoothSim tensor-core scan without the int8 copy");
+  if (smooth) {
+    // SmoothSim scales every value before the reduction (the reference's kScaleFirst): the document
+    // scale goes into the epilogue's exponent, not onto the document score
+    prm.smooth_scale = prm.scale;
+    prm.scale = 1.0F;
+    prm.temperature = red.temperature;
+  }
   const CUtensorMap tmap = f16   ? make_operand_map(d.codes16, d.num_tokens, true)
                            : pre ? make_operand_map(d.codes8, d.num_tokens, false)
                                  : CUtensorMap{};
@@ -1628,6 +1693,13 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
   if (res) {
     go(tc::tc_scan_kernel<true, true, false, true, false, true>, tc::tc_scan_kernel<true, true, false, true, true, true>,
        LayoutRes::bytes);
+  } else if (smooth) {
+    if (d.token_scale)
+      go(tc::tc_scan_kernel<true, true, false, true, false, false, 0, false, true>,
+         tc::tc_scan_kernel<true, true, false, true, true, false, 0, false, true>, tc::Layout<true>::bytes);
+    else
+      go(tc::tc_scan_kernel<false, true, false, true, false, false, 0, false, true>,
+         tc::tc_scan_kernel<false, true, false, true, true, false, 0, false, true>, tc::Layout<true>::bytes);
   } else if (topk) {
 #define MSB_TC_TOPK(TS, K) \
   go(tc::tc_scan_kernel<TS, true, false, true, false, false, K>, tc::tc_scan_kernel<TS, true, false, true, true, false, K>, \
