@@ -29,7 +29,8 @@ void launch_check_int4_codes(const uint8_t*, int64_t, unsigned int*, cudaStream_
 void launch_check_scale_range(const float*, int64_t, unsigned int*, cudaStream_t);
 bool tc_scan_supported(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, bool residual);
 void launch_tc_scan(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, float*, void* ws,
-                    size_t ws_bytes, cudaStream_t);
+                    size_t ws_bytes, cudaStream_t, TopkFuse* fuse);
+size_t tc_topk_cand_bytes(const QueryView&, int k);
 size_t tc_scan_workspace_bytes(const DocsView&, const QueryView&, const TargetsView&);
 bool tc_int8_cache_supported(const DocsView&);
 bool popc_scan_supported(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, bool residual);
@@ -46,6 +47,10 @@ static std::atomic<int> g_engine{0};  // 0 auto, 1 SIMT, 2 tensor core, 3 popcou
 static std::atomic<int> g_tc_int8_cache{1};  // keep an int8-expanded copy of int4 corpora for the tc engine
 static std::atomic<int> g_tc_f16_cache{0};   // keep an f16 copy instead (per-token scales): no conversion in the
                                              // epilogue, but twice the MMAs and operand bytes; measured slower
+// Full-scan top-k selected inside the tensor-core scan (per-CTA lists + a merge kernel).  Off by default:
+// bit-identical to the unfused path, but measured slower (the list insertions serialise the epilogue's
+// document flush, and the unfused selection of a [B, D] score matrix costs well under 1 % of a scan).
+static std::atomic<int> g_tc_fused_topk{0};
 static std::atomic<uint64_t> g_corpus_serial{0};
 }  // namespace msb
 
@@ -168,6 +173,10 @@ struct msb_docs {
   int64_t upload_serial = 0;
   cudaEvent_t upload_events[kUploadEvents] = {};
   DeviceBuf w_check;
+  // Fused top-k: candidate blocks, and the corpus's first empty documents (score 0, never in a tile),
+  // found once from the host offsets.
+  DeviceBuf w_topk, empty_ids;
+  int n_empty = -1;
 
   size_t bytes_per_token() const { return format == kFormatInt4 ? dim / 2 : dim / 8; }
   int64_t resident_bytes() const {
@@ -178,7 +187,7 @@ struct msb_docs {
     return static_cast<int64_t>(w_query.cap + w_qcodes.cap + w_qwords.cap + w_qscale.cap + w_qsum.cap +
                                 w_scores.cap + w_cands.cap + w_weights.cap + w_top_s.cap + w_top_i.cap +
                                 w_override.cap + w_fine.cap + w_tc.cap + w_check.cap + w_full.cap +
-                                w_popc.cap);
+                                w_popc.cap + w_topk.cap);
   }
   ~msb_docs() {
     int prev = -1;
@@ -188,7 +197,7 @@ struct msb_docs {
     DeviceBuf* all[] = {&codes,   &offsets,  &token_scale, &doc_scale, &residual_codes, &residual_token_scale,
                         &w_query, &w_qcodes, &w_qwords,    &w_qscale,  &w_qsum,         &w_scores,
                         &w_cands, &w_weights, &w_top_s,    &w_top_i,   &w_override,     &w_fine,
-                        &w_tc,    &codes8,   &codes16,   &w_check,        &codes2_8,  &w_full, &w_popc};
+                        &w_tc,    &codes8,   &codes16,   &w_check,        &codes2_8,  &w_full, &w_popc, &w_topk, &empty_ids};
     for (DeviceBuf* b : all) b->release();
     for (cudaEvent_t& e : upload_events)
       if (e) cudaEventDestroy(e);
@@ -289,7 +298,7 @@ Resolved resolve(msb_docs* h, const msb_score_opts* o, int batch, int qtok, cons
 }
 
 void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, int qtok, const TargetsView& tg,
-              float* d_out, cudaStream_t stream);
+              float* d_out, cudaStream_t stream, TopkFuse* fuse = nullptr);
 
 // Candidate lists (shared or per row) that name at least one document in 16 are scored faster by a full
 // tensor-core scan whose scores are then gathered: per (document, query) that scan costs a few percent
@@ -338,9 +347,10 @@ int token_scales_small(msb_docs* h, const float* d_scales, cudaStream_t stream) 
   return h->token_scale_small;
 }
 
-// Run one scan into d_out [B, T].  d_query is a device pointer.
+// Run one scan into d_out [B, T].  d_query is a device pointer.  With `fuse`, a tensor-core full scan may
+// select the top-k itself (fuse->done); otherwise the scores land in d_out.
 void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, int qtok, const TargetsView& tg,
-              float* d_out, cudaStream_t stream) {
+              float* d_out, cudaStream_t stream, TopkFuse* fuse) {
   const int64_t T = tg.ids ? tg.count : h->num_docs;
   if (batch == 0 || T == 0) return;
   if (qtok == 0) {
@@ -475,11 +485,40 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
     }
     const size_t ws = tc_scan_workspace_bytes(dv, qv, tg);
     h->w_tc.ensure(ws > 0 ? ws : 16, "cudaMalloc tensor-core scan workspace");
-    launch_tc_scan(dv, qv, r.red, tg, d_out, h->w_tc.ptr, h->w_tc.cap, stream);
+    launch_tc_scan(dv, qv, r.red, tg, d_out, h->w_tc.ptr, h->w_tc.cap, stream, tg.ids ? nullptr : fuse);
     h->tc_used = true;
     return;
   }
   launch_simt_scan(r.docs, qv, r.red, tg, r.residual, d_out, stream);
+}
+
+// Fused top-k set-up for a full-scan top-k (k <= 4096): candidate workspace and the empty-document list.
+bool prepare_fused_topk(msb_docs* h, int batch, int k, float* out_s, int64_t* out_i, TopkFuse* f) {
+  if (!g_tc_fused_topk.load() || k > 4096 || batch <= 0) return false;
+  if (h->n_empty < 0) {
+    std::vector<int64_t> ids;
+    for (int64_t d = 0; d < h->num_docs && ids.size() < 4096; ++d)
+      if (h->host_offsets[d + 1] == h->host_offsets[d]) ids.push_back(d);
+    if (!ids.empty()) {
+      h->empty_ids.ensure(sizeof(int64_t) * ids.size(), "cudaMalloc empty document list");
+      check(cudaMemcpy(h->empty_ids.ptr, ids.data(), sizeof(int64_t) * ids.size(), cudaMemcpyHostToDevice),
+            "upload empty document list");
+    }
+    h->n_empty = static_cast<int>(ids.size());
+  }
+  QueryView qv{};
+  qv.batch = batch;
+  const size_t bytes = tc_topk_cand_bytes(qv, k);
+  h->w_topk.ensure(bytes, "cudaMalloc fused top-k candidates");
+  *f = TopkFuse{};
+  f->k = k;
+  f->cand = h->w_topk.ptr;
+  f->cand_bytes = h->w_topk.cap;
+  f->empty_ids = h->empty_ids.as<int64_t>();
+  f->n_empty = h->n_empty;
+  f->out_s = out_s;
+  f->out_i = out_i;
+  return true;
 }
 
 // After a synchronising host-buffer call: surface a bounded-wait timeout of the
@@ -608,6 +647,11 @@ int msb_set_option(const char* name, int64_t value) {
       g_tc_f16_cache.store(static_cast<int>(value));
       return;
     }
+    if (std::strcmp(name, "tc_fused_topk") == 0) {
+      if (value != 0 && value != 1) throw InvalidArgument("tc_fused_topk must be 0 or 1");
+      g_tc_fused_topk.store(static_cast<int>(value));
+      return;
+    }
     throw InvalidArgument(std::string("unknown option: ") + name);
   });
 }
@@ -625,6 +669,10 @@ int msb_get_option(const char* name, int64_t* value) {
     }
     if (std::strcmp(name, "tc_f16_cache") == 0) {
       *value = g_tc_f16_cache.load();
+      return;
+    }
+    if (std::strcmp(name, "tc_fused_topk") == 0) {
+      *value = g_tc_fused_topk.load();
       return;
     }
     throw InvalidArgument(std::string("unknown option: ") + name);
@@ -1016,9 +1064,12 @@ int msb_docs_topk(msb_docs* h, const float* query, int32_t batch, int32_t qtok, 
     h->w_top_s.ensure(sizeof(float) * static_cast<size_t>(batch) * k, "cudaMalloc top score cache");
     h->w_top_i.ensure(sizeof(int64_t) * static_cast<size_t>(batch) * k, "cudaMalloc top index cache");
     TargetsView tg{};
-    run_scan(h, r, d_q, batch, qtok, tg, h->w_scores.as<float>(), s);
-    launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, k, nullptr, false,
-                     h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
+    TopkFuse fuse{};
+    const bool try_fuse = prepare_fused_topk(h, batch, k, h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), &fuse);
+    run_scan(h, r, d_q, batch, qtok, tg, h->w_scores.as<float>(), s, try_fuse ? &fuse : nullptr);
+    if (!fuse.done)
+      launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, k, nullptr, false,
+                       h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
     check(cudaMemcpyAsync(out_scores, h->w_top_s.ptr, sizeof(float) * static_cast<size_t>(batch) * k,
                           cudaMemcpyDeviceToHost, s),
           "copy top scores to host");
@@ -1133,9 +1184,12 @@ int msb_docs_topk_device(msb_docs* h, const float* query, int32_t batch, int32_t
     Resolved r = resolve(h, opts, batch, qtok, opts ? opts->weights : nullptr, opts ? opts->doc_scale_override : nullptr);
     if (batch == 0) return;
     h->w_scores.ensure(sizeof(float) * static_cast<size_t>(batch) * h->num_docs, "cudaMalloc full score cache");
-    run_scan(h, r, query, batch, qtok, TargetsView{}, h->w_scores.as<float>(), s);
-    launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, k, nullptr, false, out_scores, out_ids,
-                     s);
+    TopkFuse fuse{};
+    const bool try_fuse = prepare_fused_topk(h, batch, k, out_scores, out_ids, &fuse);
+    run_scan(h, r, query, batch, qtok, TargetsView{}, h->w_scores.as<float>(), s, try_fuse ? &fuse : nullptr);
+    if (!fuse.done)
+      launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, k, nullptr, false, out_scores,
+                       out_ids, s);
   });
 }
 

@@ -86,6 +86,19 @@ struct TargetsView {
   int per_row;                 // ids is [B, T]
 };
 
+// Fused per-query top-k of a tensor-core full scan: each CTA keeps the k best documents of every query in
+// shared memory and writes them as one candidate block; a merge kernel forms the final [B, k].
+struct TopkFuse {
+  int k;                        // top-k per query row
+  void* cand;                   // candidate blocks, 16 * B * k bytes each (device workspace)
+  size_t cand_bytes;
+  const int64_t* empty_ids;     // the corpus's first empty documents (score 0, never in a tile), device
+  int n_empty;                  // how many of them (at most k are used)
+  float* out_s;                 // [B, k] results (device)
+  int64_t* out_i;
+  bool done;                    // set when the fused path ran (otherwise the caller selects from scores)
+};
+
 // ---------------------------------------------------------------------------
 // Small device helpers.
 // ---------------------------------------------------------------------------

@@ -121,6 +121,8 @@ struct Params {
   int* error;                 // set to a non-zero code on timeout
   float smooth_scale;         // SmoothSim: the document scale applied to every value before the reduction
   float temperature;          // SmoothSim: the temperature (> 0)
+  int topk_k;                 // fused top-k: k (0: write the score matrix instead)
+  unsigned char* cand;        // fused top-k: candidate blocks [gridDim * groups][16 * batch * k bytes]
 };
 
 // Shared-memory layout (bytes, from a 1024-aligned base).
@@ -173,8 +175,12 @@ struct Layout {
   static constexpr int off_row = off_uoff + 2 * kUoffEntries * 8;
   static constexpr int off_bar = off_row + kRowBytes + 128;  // + per-group doc ids
   static constexpr int num_bars = 2 * stages + 2 * kMeta + 2 * kRaw + kAccBufs + 10;
-  static constexpr int bytes = off_bar + num_bars * 8 + 64 + 1024;  // + alignment slack
-  static_assert(bytes <= 227 * 1024, "shared memory budget");
+  // fused top-k lists (fp32 score + int32 document per entry) in what the 227 KB leave, at most 8 KB
+  static constexpr int off_topk = ((off_bar + num_bars * 8 + 64) + 15) / 16 * 16;
+  static constexpr int topk_room = (227 * 1024 - 1024 - off_topk) / 16 * 16;
+  static constexpr int topk_bytes = topk_room < 8192 ? topk_room : 8192;
+  static constexpr int bytes = off_topk + topk_bytes + 1024;  // + alignment slack
+  static_assert(bytes <= 227 * 1024 && topk_bytes >= 0, "shared memory budget");
   static_assert(off_b % 1024 == 0 && b_tile % 1024 == 0 && a_tile % 1024 == 0, "128-byte-swizzled operand tiles");
   static_assert(off_uoff % 16 == 0 && off_raw % 16 == 0 && raw_bytes % 16 == 0 && raw_scale_bytes % 16 == 0,
                 "bulk-copy alignment");
@@ -504,6 +510,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int Q = p.qtok;
+  // fused top-k: per list group (twin mode: one per epilogue group) and query, k entries kept in
+  // (score desc, document asc) order; an entry with document -1 is empty
+  constexpr int kLists = kTwin ? 2 : 1;
+  const int tk_n = p.topk_k > 0 ? kLists * p.batch * p.topk_k : 0;
+  float* tks = reinterpret_cast<float*>(smem + L::off_topk);
+  int32_t* tki = reinterpret_cast<int32_t*>(tks + tk_n);
+  for (int e = threadIdx.x; e < tk_n; e += kThreads) {
+    tks[e] = -INFINITY;
+    tki[e] = -1;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < L::stages; ++s) {
@@ -1246,6 +1262,41 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             ++sgi;
             if (++pending == kSegGroup || (sgi == nseg && last_tile)) {
               if (!epi_sync()) goto done;
+              if (p.topk_k > 0) {
+                // fused top-k: one thread per query takes the group's documents in turn into its list
+                const int K = p.topk_k;
+                for (int qx = ftid; qx < nq; qx += fthreads) {
+                  const int gq = qx < nq0 ? 0 : 1;
+                  const int qq = qx < nq0 ? qx : qx - nq0;
+                  const float* rvq = rowval + (kTwin ? g : gq) * 128 + qq * Q;
+                  const int b = (unit.qpair * kG + gq) * p.qpt + qq;
+                  float* ls = tks + ((kTwin ? g : 0) * p.batch + b) * K;
+                  int32_t* li = tki + ((kTwin ? g : 0) * p.batch + b) * K;
+                  for (int gd = 0; gd < pending; ++gd) {
+                    const float* rv = rvq + gd * kG * 128;
+                    float sacc = 0.0F;
+                    for (int r = 0; r < Q; ++r) sacc = __fadd_rn(sacc, rv[r]);
+                    const float sc = __fmul_rn(sacc, p.scale);
+                    const uint32_t key = float_to_ordered(sc);
+                    const int32_t dd = gdoc[gd];
+                    auto worse = [&](int i) {  // entry i loses to the candidate
+                      const int32_t di = li[i];
+                      if (di < 0) return true;
+                      const uint32_t ki = float_to_ordered(ls[i]);
+                      return key > ki || (key == ki && dd < di);
+                    };
+                    if (!worse(K - 1)) continue;
+                    int pos = K - 1;
+                    while (pos > 0 && worse(pos - 1)) {
+                      ls[pos] = ls[pos - 1];
+                      li[pos] = li[pos - 1];
+                      --pos;
+                    }
+                    ls[pos] = sc;
+                    li[pos] = dd;
+                  }
+                }
+              } else
               for (int x = ftid; x < pending * nq; x += fthreads) {
                 const int gd = x / nq, qx = x % nq;
                 const int gq = qx < nq0 ? 0 : 1;
@@ -1280,6 +1331,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         stg.next<L::stages>();
         if (!kTwin || st.side == 1) acc.next<kAcc>();
         mst.next<kMeta>();
+      }
+    }
+    if (p.topk_k > 0) {
+      // this CTA's (group's) lists as one candidate block: [B, k] fp32 scores, then [B, k] int64 documents
+      // (an empty entry: -inf, INT64_MAX)
+      if (!epi_sync()) goto done;
+      const int K = p.topk_k, lg = kTwin ? g : 0;
+      unsigned char* blk = p.cand + static_cast<size_t>(blockIdx.x * kLists + lg) * 16ull * p.batch * K;
+      const float* ls = tks + lg * p.batch * K;
+      const int32_t* li = tki + lg * p.batch * K;
+      for (int e = ftid; e < p.batch * K; e += fthreads) {
+        const bool full = li[e] >= 0;
+        reinterpret_cast<float*>(blk)[e] = full ? ls[e] : -INFINITY;
+        reinterpret_cast<int64_t*>(blk + 8ull * p.batch * K)[e] = full ? static_cast<int64_t>(li[e]) : INT64_MAX;
       }
     }
   }
@@ -1579,8 +1644,35 @@ struct UnitCacheKey {
   }
 };
 
+void launch_merge_shard_topk(const void*, int, int, int, const int64_t*, float*, int64_t*, cudaStream_t);
+void launch_empty_block(void*, int, int, const int64_t*, int, cudaStream_t);
+
+// Room for the fused top-k lists in the shared-memory layout the launch below picks for this scan.
+int tc_topk_room(const DocsView& d, const QueryView& q, const ReduceView& red) {
+  const bool digits = q.mode == kQueryF32;
+  const bool f16 = !digits && d.format == kFormatInt4 && d.codes16 != nullptr && d.token_scale != nullptr;
+  const bool pre = f16 || d.codes8 != nullptr;
+  const bool res = d.codes2 != nullptr;
+  const bool list = red.reducer == kTopK2 || red.reducer == kTopK4 || red.reducer == kSmooth;
+  if (res) return tc::Layout<true, false, true>::topk_bytes;
+  if (list) return tc::Layout<true>::topk_bytes;
+  if (digits) return pre ? tc::Layout<true>::topk_bytes : tc::Layout<false>::topk_bytes;
+  if (d.token_scale) {
+    if (f16) return tc::Layout<true, true>::topk_bytes;
+    if (d.token_scale_small) return pre ? tc::Layout<true, false, false, true>::topk_bytes
+                                        : tc::Layout<false, false, false, true>::topk_bytes;
+  }
+  return pre ? tc::Layout<true>::topk_bytes : tc::Layout<false>::topk_bytes;
+}
+
+// Candidate workspace of a fused top-k: a block per CTA and list group (at most two) and the empty
+// documents' block.
+size_t tc_topk_cand_bytes(const QueryView& q, int k) {
+  return static_cast<size_t>(2 * sm_count() + 1) * 16ull * q.batch * k;
+}
+
 void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red, const TargetsView&, float* out, void* ws,
-                    size_t ws_bytes, cudaStream_t stream) {
+                    size_t ws_bytes, cudaStream_t stream, TopkFuse* fuse) {
   // The unit table depends only on the corpus and the query tiling; it is
   // built once per (workspace, corpus, tiling) and kept in the workspace.
   static std::mutex cache_mu;
@@ -1596,8 +1688,17 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
     for (auto& e : cache)
       if (e.first == key) num_units = e.second;
   }
+  // Fused top-k when the lists fit the chosen layout (twin mode keeps one set per epilogue group) and the
+  // caller's candidate workspace holds a block per CTA and group plus one for the empty documents.
+  const bool twin_plan = pl.n_qtiles == 1;
+  const int lists = twin_plan ? 2 : 1;
+  const bool fused = fuse != nullptr && fuse->k >= 1 &&
+                     static_cast<int64_t>(lists) * q.batch * fuse->k * 8 <= tc_topk_room(d, q, red) &&
+                     static_cast<size_t>(lists * sms + 1) * 16ull * q.batch * fuse->k <= fuse->cand_bytes;
+  if (fuse) fuse->done = false;
   // Empty documents never appear in a tile; their score is 0.
-  check(cudaMemsetAsync(out, 0, sizeof(float) * static_cast<size_t>(q.batch) * d.num_docs, stream), "zero scores");
+  if (!fused)
+    check(cudaMemsetAsync(out, 0, sizeof(float) * static_cast<size_t>(q.batch) * d.num_docs, stream), "zero scores");
   if (num_units < 0) {
     // Document ranges cut at the token quantiles r * N / n_ranges, each split
     // further to at most kMaxRangeDocs documents; range-major units.
@@ -1632,7 +1733,14 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
       it = it->first.ws == ws ? cache.erase(it) : it + 1;
     cache.emplace_back(key, num_units);
   }
-  if (num_units == 0) return;
+  if (num_units == 0) {
+    if (!fused) return;
+    // every document is empty: the empty documents' block alone
+    launch_empty_block(fuse->cand, q.batch, fuse->k, fuse->empty_ids, std::min(fuse->n_empty, fuse->k), stream);
+    launch_merge_shard_topk(fuse->cand, 1, q.batch, fuse->k, nullptr, fuse->out_s, fuse->out_i, stream);
+    fuse->done = true;
+    return;
+  }
   check(cudaMemsetAsync(err, 0, sizeof(int), stream), "clear tc error flag");
   tc::Params prm{};
   prm.codes = d.codes;
@@ -1655,8 +1763,10 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
   prm.res_scale1 = d.scale;
   prm.res_scale2 = d.scale2;
   prm.num_docs = d.num_docs;
-  prm.out = out;
+  prm.out = fused ? nullptr : out;
   prm.error = err;
+  prm.topk_k = fused ? fuse->k : 0;
+  prm.cand = fused ? static_cast<unsigned char*>(fuse->cand) : nullptr;
   const int grid = std::min<int>(sms, prm.num_items);
   const bool digits = q.mode == kQueryF32;
   const bool f16 = !digits && d.format == kFormatInt4 && d.codes16 != nullptr && d.token_scale != nullptr;
@@ -1738,6 +1848,18 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
 #undef MSB_TC_GO
   count_launch();
   check(cudaGetLastError(), "launch tensor-core scan kernel");
+  if (fused) {
+    // the CTAs' candidate blocks, then the empty documents' block, merged in the single-pass order
+    int blocks = lists * grid;
+    const int n_empty = std::min(fuse->n_empty, fuse->k);
+    if (n_empty > 0) {
+      launch_empty_block(static_cast<unsigned char*>(fuse->cand) + static_cast<size_t>(blocks) * 16ull * q.batch * fuse->k,
+                         q.batch, fuse->k, fuse->empty_ids, n_empty, stream);
+      ++blocks;
+    }
+    launch_merge_shard_topk(fuse->cand, blocks, q.batch, fuse->k, nullptr, fuse->out_s, fuse->out_i, stream);
+    fuse->done = true;
+  }
 }
 
 }  // namespace msb

@@ -216,7 +216,8 @@ void launch_topk_rows(const float* scores, int64_t ld, int rows, int64_t T, int 
 // pads a shard holding fewer than k documents and stays INT64_MAX).  One warp per query row repeats k
 // times: every lane offers the best head among its ranks (lane, lane + 32, ...), a butterfly reduction
 // picks the winner in the single-GPU order (ordered score key desc, global id asc), and the winning
-// rank advances.  Shards are disjoint, so the result equals the top-k of the whole corpus.
+// rank advances.  Shards are disjoint, so the result equals the top-k of the whole corpus.  first_doc may
+// be null (the blocks already hold global ids: the fused top-k of the tensor-core scan).
 constexpr int kMergeWarps = 4;
 constexpr int kMergeMaxWorld = 1024;
 __global__ void __launch_bounds__(kMergeWarps * 32) merge_shard_topk_kernel(
@@ -236,7 +237,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_shard_topk_kernel(
     const unsigned char* b = gathered + static_cast<size_t>(r) * blk;
     key = float_to_ordered(reinterpret_cast<const float*>(b)[row_off + p]);
     const int64_t lid = reinterpret_cast<const int64_t*>(b + 8ull * batch * k)[row_off + p];
-    gid = lid == INT64_MAX ? INT64_MAX : lid + first_doc[r];
+    gid = lid == INT64_MAX ? INT64_MAX : lid + (first_doc ? first_doc[r] : 0);
   };
   for (int j = 0; j < k; ++j) {
     bool have = false;
@@ -302,6 +303,28 @@ __global__ void gather_scores_kernel(const float* __restrict__ scores, int64_t l
     const int64_t b = e / count, j = e - b * count;
     out[e] = scores[b * ld + ids[per_row ? e : j]];
   }
+}
+
+// The empty documents' candidate block of a fused top-k: every query row gets the first min(k, n_empty)
+// empty documents with score 0 (they never appear in a tile), the rest (-inf, INT64_MAX).
+__global__ void empty_block_kernel(unsigned char* __restrict__ blk, int batch, int k, const int64_t* __restrict__ ids,
+                                   int n_empty) {
+  const int64_t n = static_cast<int64_t>(batch) * k;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < n;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int j = static_cast<int>(e % k);
+    reinterpret_cast<float*>(blk)[e] = j < n_empty ? 0.0F : -INFINITY;
+    reinterpret_cast<int64_t*>(blk + 8ull * n)[e] = j < n_empty ? ids[j] : INT64_MAX;
+  }
+}
+
+void launch_empty_block(void* blk, int batch, int k, const int64_t* ids, int n_empty, cudaStream_t stream) {
+  const int64_t n = static_cast<int64_t>(batch) * k;
+  if (n == 0) return;
+  empty_block_kernel<<<static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 1024)), 256, 0, stream>>>(
+      static_cast<unsigned char*>(blk), batch, k, ids, n_empty);
+  count_launch();
+  check(cudaGetLastError(), "launch empty-document block kernel");
 }
 
 void launch_gather_scores(const float* scores, int64_t ld, int rows, const int64_t* ids, int64_t count, bool per_row,
