@@ -234,6 +234,41 @@ def configs_bench(args, impl="ours"):
         del h
 
 
+def c2_engines(args):
+    """Sign-code scans of the C2 corpus (10,171 documents of U[400, 800] tokens, 20 query tokens) on the
+    tensor-core engine and on the AND + popcount engine, batch 1 and 32, int8 and fp32 queries: one timed
+    launch each (CUDA events, after one warm-up), one JSON line per case.  Wrapped by ncu for the committed
+    engine comparison (profiles/popc_vs_tc_c2.txt)."""
+    import torch
+
+    from maxsim_b200 import _lib
+    from maxsim_b200 import _maxsim_cuda as mc
+    from oracle import reference_cpu as ref  # test infrastructure: the sign packer's restatement
+
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(7)
+    docs, offs, cent = _clustered(rng, 10171, 400, 800)
+    qs = _queries(rng, cent, 32, 20)
+    hb = mc.CudaPackedDocs(ref.pack_signs(docs), offs, DIM)
+    del docs
+    prev = _lib.get_engine()
+    for batch in (1, 32):
+        qd = torch.from_numpy(np.ascontiguousarray(qs[:batch])).to(dev)
+        out = torch.empty((batch, 10171), dtype=torch.float32, device=dev)
+        for int8 in (True, False):
+            for eng, name in ((2, "tensor core"), (3, "popcount")):
+                _lib.set_engine(eng)
+                hb.score_batch_device(qd, out, int8_query=int8)
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+                ev[0].record()
+                hb.score_batch_device(qd, out, int8_query=int8)
+                ev[1].record()
+                torch.cuda.synchronize()
+                print(json.dumps({"c2_engines": name, "batch": batch, "query": "int8" if int8 else "fp32",
+                                  "ms": round(ev[0].elapsed_time(ev[1]), 4)}), flush=True)
+    _lib.set_engine(prev)
+
+
 def batch_sweep(args, torch, _lib, handle, queries, device):
     """One line per batch size: scan + top-k of the whole resident corpus, CUDA events on the launching
     stream, against both roofs (algorithmic HBM bytes and int8 tensor ops of that batch)."""
@@ -535,6 +570,8 @@ def main() -> None:
     ap.add_argument("--configs-impl", choices=["ours", "reference"], default="ours",
                     help="--configs through this library or through the reference's own CUDA build (baseline/_ref_cuda)")
     ap.add_argument("--configs-only", default=None, help="comma-separated subset of C0,C1,C2,C3,C4 for --configs")
+    ap.add_argument("--c2-engines", action="store_true",
+                    help="time sign-code scans of the C2 corpus on the tensor-core and popcount engines")
     ap.add_argument("--configs", action="store_true",
                     help="time the reference's smaller benchmark shapes (C0-C3) through the handle and SDK calls "
                          "the reference's own benchmarks time, one JSON line per operation, instead of the bench line")
@@ -560,6 +597,11 @@ def main() -> None:
     from maxsim_b200 import _maxsim_cuda as mc
     from maxsim_b200.sharded import ShardedReranker, ShardInfo, shard_bounds
 
+    if args.c2_engines:
+        if rank == 0:
+            torch.cuda.set_device(local_rank)
+            c2_engines(args)
+        return
     if args.configs:
         if rank == 0:
             torch.cuda.set_device(local_rank)
