@@ -3,7 +3,7 @@
 The blocked scan runs when the query pointer is 16-byte aligned; a query that starts 4 bytes into its
 buffer takes the general kernel.  Both compute each row's dot as one FMA chain over the dims in order,
 so max, weighted and top-k scores must be bit-identical; the smooth reducer sums exponentials in a
-different order and is compared to 1e-6.  Ragged documents (empty, shorter and longer than a warp's
+different order and is compared to 1e-6.  Every case is also held to the float64 oracle at 1e-4.  Ragged documents (empty, shorter and longer than a warp's
 32 lanes and the general kernel's 128 threads), query-token counts that are not multiples of the row group, per-row candidate lists and
 the two-stream residual are all covered, and the scores are checked against the float64 oracle.
 """
@@ -77,7 +77,7 @@ def _scores(h, q, aligned, reducer, weights=None, candidates=None, residual=Fals
 @pytest.mark.parametrize("qtok", [1, 7, 32, 41])
 @pytest.mark.parametrize("reducer", list(REDUCERS))
 def test_blocked_scan_matches_general_scan(residual, gran, qtok, reducer):
-    h, _, _ = _handle(gran, residual)
+    h, p, offsets = _handle(gran, residual)
     rng = np.random.default_rng(qtok)
     q = rng.standard_normal((3, qtok, 128)).astype(np.float32)
     weights = rng.random(qtok).astype(np.float32) + 0.5 if reducer == "weighted_maxsim" else None
@@ -87,6 +87,16 @@ def test_blocked_scan_matches_general_scan(residual, gran, qtok, reducer):
         np.testing.assert_allclose(got, want, rtol=1e-6, atol=1e-6)
     else:
         np.testing.assert_array_equal(got, want)
+    # and both against the float64 oracle (the reference's reducers), 1e-4 of the score magnitude
+    kw = {"reducer": reducer, "weights": weights}
+    if residual:
+        exact = ref.score_residual(q, {"prefix_values": p.prefix_values, "prefix_scale": p.prefix_scale,
+                                       "prefix_token_scale": p.prefix_token_scale,
+                                       "residual_values": p.residual_values, "residual_scale": p.residual_scale,
+                                       "residual_token_scale": p.residual_token_scale}, offsets, **kw)
+    else:
+        exact = ref.score_int4_fp32(q, p.values, offsets, scale=p.scale, token_scale=p.token_scale, **kw)
+    np.testing.assert_allclose(got, exact, rtol=1e-4, atol=1e-4 * max(1.0, float(np.abs(exact).max())))
 
 
 @pytest.mark.parametrize("residual", [False, True])
