@@ -40,6 +40,8 @@ void launch_popc_scan(const DocsView&, const QueryView&, const ReduceView&, cons
 void launch_expand_codes8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t);
 void launch_expand_binary8(const uint8_t* codes, int64_t num_tokens, uint8_t* out, cudaStream_t);
 void launch_expand_codes16(const uint8_t* codes, int64_t num_tokens, uint16_t* out, cudaStream_t);
+void set_tc_row_replicas(int on);
+int get_tc_row_replicas();
 
 static std::atomic<int64_t> g_launches{0};
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
@@ -652,6 +654,11 @@ int msb_set_option(const char* name, int64_t value) {
       g_tc_fused_topk.store(static_cast<int>(value));
       return;
     }
+    if (std::strcmp(name, "tc_row_replicas") == 0) {
+      if (value != 0 && value != 1) throw InvalidArgument("tc_row_replicas must be 0 or 1");
+      set_tc_row_replicas(static_cast<int>(value));
+      return;
+    }
     throw InvalidArgument(std::string("unknown option: ") + name);
   });
 }
@@ -673,6 +680,10 @@ int msb_get_option(const char* name, int64_t* value) {
     }
     if (std::strcmp(name, "tc_fused_topk") == 0) {
       *value = g_tc_fused_topk.load();
+      return;
+    }
+    if (std::strcmp(name, "tc_row_replicas") == 0) {
+      *value = get_tc_row_replicas();
       return;
     }
     throw InvalidArgument(std::string("unknown option: ") + name);

@@ -31,9 +31,11 @@
 //     128-byte swizzle: the UMMA layout) while expander warps only stage the
 //     tile metadata (token scales, document ends).  Without the copy (option
 //     "tc_int8_cache" 0, or no memory for it) the loader copies raw int4 rows
-//     into a 6-deep ring and the expander warps sign-extend each nibble to an
-//     int8 byte in the swizzled layout, in a chunk order that keeps their
-//     shared loads and stores free of bank conflicts.
+//     into a 6-deep ring and the two expander warps take alternate tiles, each
+//     writing 16 x every code (the nibble moved to the top of its byte, three
+//     logic operations per four bytes of codes) in the swizzled layout, in a
+//     chunk order that keeps their shared loads and stores free of bank
+//     conflicts; the epilogue divides the 16 x dot accumulators back exactly.
 //   * TMEM holds two token-tile buffers x two query tiles x 128 columns.  One
 //     commit per token tile both frees its shared-memory stage and hands the
 //     accumulators to the epilogue, which returns them as soon as the tile's
@@ -52,6 +54,8 @@
 //     MaxSim folds the weights into the rows' power-of-two scales.
 //   * Sign-code corpora read a resident +-1 int8 copy through the same TMA path.
 //   * kTwin: passes with one query tile let the two epilogue groups take two document ranges in turn.
+//   * kRep: one tile of at most 64 (32) int8 query rows is copied two (four) times over the TMEM lane
+//     quarters, and each epilogue warp takes a 64- (32-) column slice of every token tile.
 //   * kRes: the fused two-stream residual (int4 or sign-code prefix + int4 residual), two accumulators
 //     per query tile.
 //   * kTopK: the TopK2 / TopK4 reducers, per-thread lists merged across a row's four threads.
@@ -63,6 +67,7 @@
 #include <cuda_fp16.h>  // CUtensorMap (the encoder is fetched through cudaGetDriverEntryPoint)
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -92,6 +97,9 @@ constexpr uint64_t kTimeoutNs = 4000000000ull;                // 4 s per wait
 // one fused multiply-add maps exactly to dot * 2^-23 (see bias_scale2).
 constexpr int kBiasBytes = 128 * 32;
 constexpr int32_t kBiasValue = 32 * 127 * 127;  // 516,128 > |dot| <= 127 * 7 * 128 = 113,792
+// Operand tiles expanded in shared memory hold 16 x the int4 codes (see the expanders), so accumulators
+// hold 16 x the dot; their bias is 32 * 255 * 255 (unsigned 0xFF operands) > 16 * 127 * 8 * 128.
+constexpr int32_t kBiasValue16 = 32 * 255 * 255;  // 2,080,800; 16 * dot + kBiasValue16 < 2^22
 
 struct Unit {
   int64_t d_lo, d_hi;    // documents [d_lo, d_hi), at most kMaxRangeDocs
@@ -259,10 +267,16 @@ __device__ __forceinline__ uint64_t umma_desc_plain(uint32_t saddr) {
 // (dot + kBiasValue) * 2^-23 - kBiasValue * 2^-23 = dot * 2^-23 exactly (|dot| < 2^17; subnormal
 // inputs are kept, no flush to zero), and the packed product dot * 2^-23 * (s * 2^23) is rounded once,
 // to the same float as fl(float(dot) * s).  Two instructions per two values, both on the FMA pipe.
+// kX16: accumulators of 16 * dot + kBiasValue16: (16 dot + kBiasValue16) * 2^-27 - kBiasValue16 * 2^-27
+// is the same dot * 2^-23, exactly.
+template <bool kX16 = false>
 __device__ __forceinline__ void bias_scale2(uint32_t& x0, uint32_t& x1, float2 s23) {
-  constexpr float kNeg = -static_cast<float>(kBiasValue) / 8388608.0F;  // -kBiasValue * 2^-23 (exact)
+  // -bias * 2^-23 (or 2^-27), exact
+  constexpr float kNeg = kX16 ? -static_cast<float>(kBiasValue16) / 134217728.0F
+                              : -static_cast<float>(kBiasValue) / 8388608.0F;
+  constexpr float kMul = kX16 ? 0x1p122F : 0x1p126F;
   const float2 v = __fmul2_rn(__ffma2_rn(make_float2(__uint_as_float(x0), __uint_as_float(x1)),
-                                         make_float2(0x1p126F, 0x1p126F), make_float2(kNeg, kNeg)),
+                                         make_float2(kMul, kMul), make_float2(kNeg, kNeg)),
                               s23);
   x0 = __float_as_uint(v.x);
   x1 = __float_as_uint(v.y);
@@ -351,6 +365,14 @@ __device__ __forceinline__ void tmem_ld16x256b_x8(uint32_t taddr, uint32_t* r) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 16 TMEM lanes x 32 columns: as tmem_ld16x256b_x8 for j = 0..3.
+__device__ __forceinline__ void tmem_ld16x256b_x4(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Maximum of row s (0 or 1) of a 16x256b chunk half X (its 16 values X[4j + 2s], X[4j + 2s + 1]) folded
@@ -368,7 +390,15 @@ __device__ __forceinline__ void topk_insert(float (&v)[K], float x) {
   }
 }
 
+template <int NJ>
 __device__ __forceinline__ float row_max16(const uint32_t* X, int s, float R) {
+  if constexpr (NJ == 4) {  // 8 values: X[4j + 2s], X[4j + 2s + 1], j = 0..3
+    const float m0 = fmax3(R, __uint_as_float(X[2 * s]), __uint_as_float(X[2 * s + 1]));
+    const float m1 = fmax3(__uint_as_float(X[4 + 2 * s]), __uint_as_float(X[4 + 2 * s + 1]), __uint_as_float(X[8 + 2 * s]));
+    const float m2 =
+        fmax3(__uint_as_float(X[8 + 2 * s + 1]), __uint_as_float(X[12 + 2 * s]), __uint_as_float(X[12 + 2 * s + 1]));
+    return fmax3(m0, m1, m2);
+  }
   float m0 = fmax3(__uint_as_float(X[2 * s]), __uint_as_float(X[2 * s + 1]), __uint_as_float(X[16 + 2 * s]));
   float m1 = fmax3(__uint_as_float(X[4 + 2 * s]), __uint_as_float(X[4 + 2 * s + 1]), __uint_as_float(X[20 + 2 * s]));
   const float m2 =
@@ -379,15 +409,27 @@ __device__ __forceinline__ float row_max16(const uint32_t* X, int s, float R) {
   m1 = fmax3(m1, __uint_as_float(X[28 + 2 * s]), __uint_as_float(X[28 + 2 * s + 1]));
   return fmax3(R, fmax3(m0, m1, m2), m3);
 }
+template <int NJ>
 __device__ __forceinline__ int32_t row_max16i(const uint32_t* X, int s, int32_t R) {
   int32_t m0 = max(static_cast<int32_t>(X[2 * s]), static_cast<int32_t>(X[2 * s + 1]));
   int32_t m1 = max(static_cast<int32_t>(X[4 + 2 * s]), static_cast<int32_t>(X[4 + 2 * s + 1]));
 #pragma unroll
-  for (int j = 2; j < 8; j += 2) {
+  for (int j = 2; j < NJ; j += 2) {
     m0 = __vimax3_s32(m0, static_cast<int32_t>(X[4 * j + 2 * s]), static_cast<int32_t>(X[4 * j + 2 * s + 1]));
     m1 = __vimax3_s32(m1, static_cast<int32_t>(X[4 * j + 4 + 2 * s]), static_cast<int32_t>(X[4 * j + 4 + 2 * s + 1]));
   }
   return __vimax3_s32(R, m0, m1);
+}
+
+// Row value r of a flushed document: with replicated query rows (kRep copies of 128 / kRep rows, each
+// the scaled maximum over one column slice) the largest copy.  The query scale is >= 0, so the maximum of
+// the scaled slice maxima equals the scaled maximum over all columns.
+template <int kRep>
+__device__ __forceinline__ float rep_max(const float* rv, int r) {
+  float v = rv[r];
+#pragma unroll
+  for (int c = 1; c < kRep; ++c) v = fmaxf(v, rv[r + c * (128 / kRep)]);
+  return v;
 }
 
 // ---------------------------------------------------------------------------
@@ -467,8 +509,13 @@ __device__ __forceinline__ Step step_of(const Item& it, int64_t i) {
 // scales two values with two packed FMA-pipe instructions (bias_scale2) instead of an int32 -> fp32
 // conversion and a product per value; the token scales are staged as s * 2^23 (the host keeps this
 // variant for corpora whose token scales are below 2^104, so that s * 2^23 is exact).
+// kRep (2 or 4; twin mode, int8 queries, at most 128 / kRep query rows): the query tile is replicated over
+// the four TMEM lane quarters (kRep copies of 128 / kRep rows), so every epilogue warp holds each of its rows
+// for only its slice of 128 / kRep columns of a token tile; a document's row maximum is completed across the
+// kRep copies when its group is flushed.  One or two live warps per group would otherwise do a whole
+// tile's epilogue alone.
 template <bool kTokenScale, bool kPre, bool kF16, bool kDigits = false, bool kTwin = false, bool kRes = false,
-          int kTopK = 0, bool kBias = false, bool kSmooth = false>
+          int kTopK = 0, bool kBias = false, bool kSmooth = false, int kRep = 1>
 __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap,
                                                               const __grid_constant__ CUtensorMap tmap2) {
   using L = Layout<kPre, kF16, kRes, kBias>;
@@ -477,6 +524,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
   static_assert(!kRes || (kPre && kDigits && kTokenScale && !kF16), "the residual stream reads both int8 copies");
   static_assert(kTopK == 0 || (kTopK <= 4 && kPre && kDigits && !kRes), "TopK: digit-plane queries, int8 copies");
   static_assert(!kSmooth || (kTopK == 0 && kPre && kDigits && !kRes), "SmoothSim: digit-plane queries, int8 copies");
+  static_assert(kRep == 1 || ((kRep == 2 || kRep == 4) && kTwin && !kDigits && !kF16 && !kRes && !kSmooth),
+                "replicated query rows: one tile of int8 query rows");
+  constexpr int kQuarters = 4 / kRep;               // lane quarters holding distinct query rows
+  constexpr int kChunkCols = kRep == 4 ? 32 : 64;   // columns of one pair of TMEM loads
+  constexpr int kNJ = kChunkCols / 8;               // 8-column groups per load
+  constexpr int kChunks = kRep == 1 ? 2 : 1;        // load pairs per token tile and warp
+  // Expanding path (operand tiles built from int4 rows in shared memory): the two expander warps take
+  // alternate tiles, each a whole tile, and the tiles hold 16 x the codes (accumulators of 16 x the dot).
+  constexpr bool kAlt = !kPre;
   constexpr bool kList = kTopK > 0 || kSmooth;     // reducers that take the per-segment path in every chunk
   constexpr int kTk = kTopK > 0 ? kTopK : 1;
   constexpr int kAcc = kRes ? 1 : kAccBufs;         // accumulator buffers
@@ -523,24 +579,24 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < L::stages; ++s) {
-      mbar_init(&full[s], kPre ? 1 : kXWarps);  // kPre: the loader's expect_tx + the TMA's bytes
+      mbar_init(&full[s], 1);  // kPre: the loader's expect_tx + the TMA's bytes; else the tile's expander
       mbar_init(&tile_done[s], 1);
     }
     for (int s = 0; s < kMeta; ++s) {
       // kPre: the expanders' metadata and the MMA warp's commit of the tile's products (kXWarps + 1)
-      mbar_init(&m_full[s], kPre ? kXWarps + 1 : kXWarps);
+      mbar_init(&m_full[s], kPre ? kXWarps + 1 : 1);
       mbar_init(&m_empty[s], kTwin ? kEpiWarps / 2 : kEpiWarps);  // twin: only the owning group reads a tile
     }
     for (int s = 0; s < kRaw; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], kXWarps);
+      mbar_init(&raw_empty[s], kAlt ? 1 : kXWarps);
     }
     for (int a = 0; a < kAccBufs; ++a) mbar_init(&acc_empty[a], kEpiWarps);
     for (int a = 0; a < 2; ++a) {
       mbar_init(&a_full[a], kXWarps);
       mbar_init(&a_empty[a], 1);
       mbar_init(&u_full[a], 1);
-      mbar_init(&u_empty[a], 1);
+      mbar_init(&u_empty[a], kAlt ? kXWarps : 1);  // the warps that walk the unit's offsets
     }
     if (kTwin) {
       mbar_init(&epi_bar[0], kEpiWarps / 2);
@@ -553,8 +609,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
   }
   if (kBias) {
     // the constant bias operand, made visible to the tensor core (async proxy) before the first MMA
+    constexpr uint32_t kc = kPre ? 0x7F7F7F7Fu : 0xFFFFFFFFu;  // s8 127, or u8 255 for 16 x the codes
     for (int i = threadIdx.x; i < kBiasBytes / 16; i += kThreads)
-      reinterpret_cast<uint4*>(smem + L::off_bias)[i] = make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
+      reinterpret_cast<uint4*>(smem + L::off_bias)[i] = make_uint4(kc, kc, kc, kc);
     fence_proxy_async();
   }
   if (warp == kMmaWarp) {
@@ -656,9 +713,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             valid = k < 3 && rho < p.qpt * Q && b < p.batch;
             src_row = valid ? static_cast<int64_t>(k) * p.batch * Q + static_cast<int64_t>(b) * Q + qrow : 0;
           } else {
-            b = (qpair * kG + g) * p.qpt + row / Q;
-            qrow = row % Q;
-            valid = row < p.qpt * Q && b < p.batch;
+            const int rr = row & (128 / kRep - 1);  // kRep > 1: the copies of rows 0 .. 128 / kRep - 1
+            b = (qpair * kG + g) * p.qpt + rr / Q;
+            qrow = rr % Q;
+            valid = rr < p.qpt * Q && b < p.batch;
             src_row = valid ? static_cast<int64_t>(b) * Q + qrow : 0;
           }
           const int4* src = reinterpret_cast<const int4*>(p.qwords + src_row * 32);
@@ -691,7 +749,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[abuf]);
       }
-      if (xwarp == 0) {
+      if (kAlt || xwarp == 0) {
         for (int side = 0; side < (kTwin ? 2 : 1); ++side) {
           const int ub = kTwin ? side : (iter & 1);
           const int use = kTwin ? iter : (iter >> 1);
@@ -700,6 +758,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       }
       int64_t next_doc0 = it.un[0].d_lo, next_doc1 = it.un[1].d_lo;  // first documents whose ends are ahead
       for (int64_t i = 0; i < it.nsteps; ++i) {
+        if (kAlt && static_cast<int>(i & 1) != xwarp) {
+          // the other expander warp's tile
+          raw.next<kRaw>();
+          stg.next<L::stages>();
+          mst.next<kMeta>();
+          continue;
+        }
         const Step st = step_of<kTwin>(it, i);
         const Unit& unit = st.side ? it.un[1] : it.un[0];
         const int ub = kTwin ? st.side : (iter & 1);
@@ -724,37 +789,55 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             for (int r = xtid; r < valid; r += kXWarps * 32) sc2[scale_slot(r)] = rs2[(t0 & 3) + r];
           }
         }
-#pragma unroll 1
-        for (int r = xtid; r < (kPre ? 0 : valid); r += kXWarps * 32) {  // tokens of the tile
+        if (!kPre) {
+          // One warp expands the whole tile: lane l takes tokens l + 32u, u = 0..3, each 64 bytes of int4
+          // codes -> 128 bytes of 16 * code (an exact int8: the nibble in the high half of its byte, its
+          // sign bit the byte's), so the products are 16 x the integer dots.  Per 32-bit word: the high
+          // nibbles (odd dims) are w & 0xF0F0F0F0 and the low nibbles (even dims) (w << 4) & 0xF0F0F0F0.
           // Chunk order c = M(a) ^ step with a = (r / 2) % 4 and M multiplication by a generator of GF(4)
           // ({0, 2, 3, 1}): both c and c ^ a run over all four values within each 8-token quarter warp,
           // so the raw loads (bank slot 4(r % 2) + c) and the swizzled stores (slot 2(c ^ a) + r % 2) are
-          // conflict-free.
-          const int qa = (r >> 1) & 3;
+          // conflict-free.  A full tile issues its sixteen loads per lane before the arithmetic.
+          const int qa = (lane >> 1) & 3;
           const int qm = ((qa << 1) & 3) ^ ((qa >> 1) * 3);
-#pragma unroll
-          for (int step = 0; step < 4; ++step) {
-            const int c = qm ^ step;
-            const uint4 v = *reinterpret_cast<const uint4*>(rb + r * 64 + c * 16);
+          auto expand = [&](int r, int c, const uint4 v) {
             const uint32_t w[4] = {v.x, v.y, v.z, v.w};
             uint32_t o[8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              // sign-extend each two's-complement nibble to a byte: n | (n & 8) * 0x1E, no carries between bytes
-              const uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = (w[i] >> 4) & 0x0F0F0F0Fu;
-              o[2 * i] = lo + (lo & 0x08080808u) * 30u;      // even dims (low nibbles)
-              o[2 * i + 1] = hi + (hi & 0x08080808u) * 30u;  // odd dims (high nibbles)
+            for (int k = 0; k < 4; ++k) {
+              o[2 * k] = (w[k] << 4) & 0xF0F0F0F0u;  // even dims (low nibbles)
+              o[2 * k + 1] = w[k] & 0xF0F0F0F0u;     // odd dims (high nibbles)
             }
             *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<uint4*>(Bt + tile_off(r, 2 * c + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+          };
+          if (valid == kTileN) {
+            uint4 v[4][4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int step = 0; step < 4; ++step)
+                v[u][step] = *reinterpret_cast<const uint4*>(rb + (lane + 32 * u) * 64 + (qm ^ step) * 16);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int step = 0; step < 4; ++step) expand(lane + 32 * u, qm ^ step, v[u][step]);
+          } else {
+#pragma unroll 1
+            for (int r = lane; r < valid; r += 32)
+#pragma unroll
+              for (int step = 0; step < 4; ++step)
+                expand(r, qm ^ step, *reinterpret_cast<const uint4*>(rb + r * 64 + (qm ^ step) * 16));
           }
           if (kTokenScale) {
             const float* rs = reinterpret_cast<const float*>(rb + L::raw_code_bytes);
-            meta->scale[scale_slot(r)] = kBias ? __fmul_rn(rs[(t0 & 3) + r], 8388608.0F) : rs[(t0 & 3) + r];
+            for (int r = lane; r < valid; r += 32)
+              meta->scale[scale_slot(r)] = kBias ? __fmul_rn(rs[(t0 & 3) + r], 8388608.0F) : rs[(t0 & 3) + r];
           }
         }
-        // Documents ending inside (t0, t0 + valid]: expander warp 0 walks the unit's offsets in smem.
-        if (xwarp == 0) {
+        // Documents ending inside (t0, t0 + valid]: the tile's warp (expanding path; each warp skips the
+        // ends of the other warp's tiles first) or expander warp 0 walks the unit's offsets in smem.
+        if (kAlt || xwarp == 0) {
           int nseg = 0;
           const int64_t tile_end = t0 + valid;
           int64_t next_doc = st.side ? next_doc1 : next_doc0;
@@ -764,7 +847,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             const int64_t e = in ? uoff[d + 1 - ufirst] : INT64_MAX;
             const int64_t s = in ? uoff[d - ufirst] : INT64_MAX;
             const bool ends = in && e <= tile_end;
-            const bool nonempty = ends && e > s;
+            const bool nonempty = ends && e > t0 && e > s;  // e <= t0: the other warp's tile (kAlt)
             const uint32_t end_mask = __ballot_sync(0xFFFFFFFFu, ends);
             const uint32_t ne_mask = __ballot_sync(0xFFFFFFFFu, nonempty);
             if (nonempty) {
@@ -798,7 +881,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         stg.next<L::stages>();
         mst.next<kMeta>();
       }
-      if (xwarp == 0 && lane == 0) {
+      if ((kAlt || xwarp == 0) && lane == 0) {
         for (int side = 0; side < (kTwin ? 2 : 1); ++side) mbar_arrive(&u_empty[kTwin ? side : (iter & 1)]);
       }
     }
@@ -850,7 +933,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               }
             } else {
               // every accumulator opens at kBiasValue: constant x constant, K = 32
-              if (kBias) mma_i8(d_tmem, c_desc, c_desc, idesc, 0u);
+              // (expanding path: unsigned 0xFF operands, A and B formats 0 = u8)
+              if (kBias) mma_i8(d_tmem, c_desc, c_desc, kPre ? idesc : (idesc & ~((7u << 7) | (7u << 10))), 0u);
               const uint64_t ad0 = umma_desc(ag, 16u, 1024u);
               const uint64_t bd0 = b_desc0 + static_cast<uint64_t>((stg.idx * L::b_tile) >> 4);
 #pragma unroll
@@ -882,6 +966,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     // t % 4 = 0..3 with two butterfly shuffles when a document ends.
     const int q4 = warp & 3;
     const int g = warp >> 2;                      // query tile of the pair
+    const int rq = q4 % kQuarters;                // kRep > 1: the quarter of distinct rows this warp holds
+    const int slice = q4 / kQuarters;             //           and its slice of 128 / kRep columns
     const int etid = threadIdx.x;                 // 0..255
     const int tq = lane >> 2, tc = lane & 3;
     const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
@@ -908,10 +994,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       // Rows of this warp's TMEM lane quarter that hold query tokens; a quarter without any (small
       // batches) skips its loads and arithmetic and only walks the document ends with the others.
       const int tile_rows = max(0, min(p.qpt, p.batch - tile * p.qpt)) * Q;
-      const bool tile_live = (kDigits ? 8 * q4 : 32 * q4) < tile_rows;
+      const bool tile_live = (kDigits ? 8 * q4 : 32 * rq) < tile_rows;
       // the row this thread stores when a document ends: i = t % 4 (digit planes: the one query row of
       // the four lanes, stored by t % 4 = 0)
-      const int wrow = kDigits ? 8 * q4 + tq : q4 * 32 + 16 * (tc >> 1) + 8 * (tc & 1) + tq;
+      const int wrow = kDigits ? 8 * q4 + tq : rq * 32 + 16 * (tc >> 1) + 8 * (tc & 1) + tq;
+      const int wslot = kDigits ? wrow : q4 * 32 + 16 * (tc >> 1) + 8 * (tc & 1) + tq;  // its TMEM lane
       const bool w_store = !kDigits || tc == 0;
       const int wb = tile * p.qpt + wrow / Q;
       const bool w_valid = wrow < p.qpt * Q && wb < p.batch;
@@ -953,34 +1040,42 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         int sgi = 0;
         bool released = false;
 #pragma unroll
-        for (int ci = 0; ci < 2; ++ci) {
-          const int c0 = 64 * ci;
-          if (c0 >= valid) break;
-          const int c1 = min(c0 + 64, valid);  // this chunk's valid columns [c0, c1)
-          uint32_t ra[32], rb[32];              // lanes +0..15 (rows i = 0, 1) and +16..31 (rows i = 2, 3)
-          if (tile_live) {
-            float2 sc[8], sc2[8];
+        for (int ci = 0; ci < kChunks; ++ci) {
+          // kRep == 1: two 64-column chunks; kRep > 1: this warp's slice of the tile, possibly empty
+          const int c0 = kRep == 1 ? 64 * ci : slice * (128 / kRep);
+          if (kRep == 1 && c0 >= valid) break;
+          const int c1 = max(c0, min(c0 + kChunkCols, valid));  // this chunk's valid columns [c0, c1)
+          uint32_t ra[4 * kNJ], rb[4 * kNJ];  // lanes +0..15 (rows i = 0, 1) and +16..31 (rows i = 2, 3)
+          if (tile_live && c1 > c0) {
+            float2 sc[kNJ], sc2[kNJ];
             if (kTokenScale) {
               const float* s2base = reinterpret_cast<const float*>(smem + L::off_scale2 + mst.idx * 160 * 4);
+              // columns c0 + 8j + 2(t % 4) + {0, 1}: slots from (c0 / 64) * 80 + (t % 4) * 20 + ((c0 % 64) / 8) * 2
+              const int sb = (c0 >> 6) * 80 + tc * 20 + ((c0 & 63) >> 3) * 2;
 #pragma unroll
-              for (int k4 = 0; k4 < 4; ++k4) {
-                const float4 x = *reinterpret_cast<const float4*>(meta->scale + (c0 >> 6) * 80 + tc * 20 + 4 * k4);
+              for (int k4 = 0; k4 < kNJ / 2; ++k4) {
+                const float4 x = *reinterpret_cast<const float4*>(meta->scale + sb + 4 * k4);
                 sc[2 * k4] = make_float2(x.x, x.y);
                 sc[2 * k4 + 1] = make_float2(x.z, x.w);
                 if (kRes) {  // the residual stream's scales, in the same slots
-                  const float4 y = *reinterpret_cast<const float4*>(s2base + (c0 >> 6) * 80 + tc * 20 + 4 * k4);
+                  const float4 y = *reinterpret_cast<const float4*>(s2base + sb + 4 * k4);
                   sc2[2 * k4] = make_float2(y.x, y.y);
                   sc2[2 * k4 + 1] = make_float2(y.z, y.w);
                 }
               }
             }
-            tmem_ld16x256b_x8(tbase + c0, ra);
-            tmem_ld16x256b_x8(tbase + (16u << 16) + c0, rb);
+            if constexpr (kNJ == 8) {
+              tmem_ld16x256b_x8(tbase + c0, ra);
+              tmem_ld16x256b_x8(tbase + (16u << 16) + c0, rb);
+            } else {
+              tmem_ld16x256b_x4(tbase + c0, ra);
+              tmem_ld16x256b_x4(tbase + (16u << 16) + c0, rb);
+            }
             tmem_wait_ld();
-            float v1[16];  // residual stream: the prefix's combined digit dots of this thread's row
+            float v1[2 * kNJ];  // residual stream: the prefix's combined digit dots of this thread's row
             if (kRes) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
+              for (int j = 0; j < kNJ; ++j) {
 #pragma unroll
                 for (int b2 = 0; b2 < 2; ++b2) {
                   const int32_t d0 = static_cast<int32_t>(ra[4 * j + b2]);
@@ -993,7 +1088,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               tmem_ld16x256b_x8(tbase + kTileN + (16u << 16) + c0, rb);
               tmem_wait_ld();
             }
-            if (c0 + 64 >= valid) {
+            if (kRep > 1 || c0 + 64 >= valid) {
               // last chunk of the tile is in registers: hand the accumulators back to the MMA now
               tc_fence_before();
               __syncwarp();
@@ -1004,13 +1099,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               // rows 0, 1, 2 are the digit planes' exact dots: d0 + 256 d1 is exact in int32 (|d| <= 2^17),
               // one rounding to float and one fused multiply-add, then fl(dot * s_t); the result in row 0
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
+              for (int j = 0; j < kNJ; ++j) {
 #pragma unroll
                 for (int b2 = 0; b2 < 2; ++b2) {
                   const int32_t d0 = static_cast<int32_t>(ra[4 * j + b2]);
                   const int32_t d1 = static_cast<int32_t>(ra[4 * j + 2 + b2]);
                   const int32_t d2 = static_cast<int32_t>(rb[4 * j + b2]);
-                  float v = __fmaf_rn(__int2float_rn(d2), 65536.0F, __int2float_rn(d0 + 256 * d1));
+                  // expanding path: 16 x the dots, so d0 + 256 d1 >> 4 and d2 * 2^12 (both exact)
+                  float v = kPre ? __fmaf_rn(__int2float_rn(d2), 65536.0F, __int2float_rn(d0 + 256 * d1))
+                                 : __fmaf_rn(__int2float_rn(d2), 4096.0F, __int2float_rn((d0 + 256 * d1) >> 4));
                   if (kRes) {
                     // fl(fl(fl(v1 * scale1) * s1) + fl(fl(v2 * scale2) * s2)), as the SIMT kernel orders it
                     const float a = __fmul_rn(__fmul_rn(v1[2 * j + b2], p.res_scale1), b2 ? sc[j].y : sc[j].x);
@@ -1025,24 +1122,25 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             } else if (kBias) {
               // (dot + kBiasValue) bits -> fl(dot * s_t): two packed instructions per two columns
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                bias_scale2(ra[4 * j], ra[4 * j + 1], sc[j]);
-                bias_scale2(ra[4 * j + 2], ra[4 * j + 3], sc[j]);
-                bias_scale2(rb[4 * j], rb[4 * j + 1], sc[j]);
-                bias_scale2(rb[4 * j + 2], rb[4 * j + 3], sc[j]);
+              for (int j = 0; j < kNJ; ++j) {
+                bias_scale2<!kPre>(ra[4 * j], ra[4 * j + 1], sc[j]);
+                bias_scale2<!kPre>(ra[4 * j + 2], ra[4 * j + 3], sc[j]);
+                bias_scale2<!kPre>(rb[4 * j], rb[4 * j + 1], sc[j]);
+                bias_scale2<!kPre>(rb[4 * j + 2], rb[4 * j + 3], sc[j]);
               }
             } else if (kTokenScale) {
-              // exact int32 dot -> float (all 64 first), then fl(dot * s_t); f16 operands accumulate the
+              // exact int32 dot -> float (all 64 first; expanding path: 16 x dot, shifted back first), then
+              // fl(dot * s_t); f16 operands accumulate the
               // same integer exactly in fp32 (|products| <= 1016, |sums| < 2^17), so nothing to convert
               if (!kF16) {
 #pragma unroll
-                for (int k = 0; k < 32; ++k) {
-                  ra[k] = __float_as_uint(__int2float_rn(static_cast<int32_t>(ra[k])));
-                  rb[k] = __float_as_uint(__int2float_rn(static_cast<int32_t>(rb[k])));
+                for (int k = 0; k < 4 * kNJ; ++k) {
+                  ra[k] = __float_as_uint(__int2float_rn(static_cast<int32_t>(ra[k]) >> (kPre ? 0 : 4)));
+                  rb[k] = __float_as_uint(__int2float_rn(static_cast<int32_t>(rb[k]) >> (kPre ? 0 : 4)));
                 }
               }
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
+              for (int j = 0; j < kNJ; ++j) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const float s1 = (e & 1) ? sc[j].y : sc[j].x;
@@ -1052,20 +1150,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               }
             }
           }
-          if (!kList && nseg == 0 && tile_live && c1 == c0 + 64) {
+          if (!kList && nseg == 0 && tile_live && c1 == c0 + kChunkCols) {
             // no document ends in this tile and the open document covers the whole chunk: no walk
             if (kFloat) {
-              run[0] = row_max16(ra, 0, run[0]);
+              run[0] = row_max16<kNJ>(ra, 0, run[0]);
               if (!kDigits) {
-                run[1] = row_max16(ra, 1, run[1]);
-                run[2] = row_max16(rb, 0, run[2]);
-                run[3] = row_max16(rb, 1, run[3]);
+                run[1] = row_max16<kNJ>(ra, 1, run[1]);
+                run[2] = row_max16<kNJ>(rb, 0, run[2]);
+                run[3] = row_max16<kNJ>(rb, 1, run[3]);
               }
             } else {
-              run_i[0] = row_max16i(ra, 0, run_i[0]);
-              run_i[1] = row_max16i(ra, 1, run_i[1]);
-              run_i[2] = row_max16i(rb, 0, run_i[2]);
-              run_i[3] = row_max16i(rb, 1, run_i[3]);
+              run_i[0] = row_max16i<kNJ>(ra, 0, run_i[0]);
+              run_i[1] = row_max16i<kNJ>(ra, 1, run_i[1]);
+              run_i[2] = row_max16i<kNJ>(rb, 0, run_i[2]);
+              run_i[3] = row_max16i<kNJ>(rb, 1, run_i[3]);
             }
             continue;
           }
@@ -1075,7 +1173,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
           while (true) {
             const int e = nseg == 0 ? 0x7FFF : (sgi < nseg ? meta->seg_end[sgi] : 0x7FFF);
             const int bnd = min(e, c1);
-            const bool split = !kList && kFloat && tile_live && a == c0 && c1 == c0 + 64 && e > c0 && e < c1 &&
+            const bool split = !kList && kFloat && tile_live && a == c0 && c1 == c0 + kChunkCols && e > c0 && e < c1 &&
                                (sgi + 1 < nseg ? meta->seg_end[sgi + 1] : 0x7FFF) > c1;
             if (split) {
               // Exactly one document ends strictly inside the chunk: one pass sends each value to the
@@ -1088,7 +1186,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 lo[i][0] = lo[i][1] = hi[i][0] = hi[i][1] = kLowest;
               }
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
+              for (int j = 0; j < kNJ; ++j) {
                 const bool in0 = 8 * j < le, in1 = 8 * j + 1 < le;
 #pragma unroll
                 for (int i = 0; i < kRows; ++i) {
@@ -1115,7 +1213,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 float mx = kLowest;
                 bool any = false;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                for (int j = 0; j < kNJ; ++j) {
 #pragma unroll
                   for (int b2 = 0; b2 < 2; ++b2) {
                     const int cc = 8 * j + b2;
@@ -1128,7 +1226,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                   const float mn = fmaxf(sm_m, mx);
                   float acc_s = sm_s > 0.0F ? sm_s * exp2f((sm_m - mn) * sm_c) : 0.0F;
 #pragma unroll
-                  for (int j = 0; j < 8; ++j) {
+                  for (int j = 0; j < kNJ; ++j) {
 #pragma unroll
                     for (int b2 = 0; b2 < 2; ++b2) {
                       const int cc = 8 * j + b2;
@@ -1142,7 +1240,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 // columns [a, bnd) of the open document into this thread's list
                 const int la = a - c0 - 2 * tc, lb = bnd - c0 - 2 * tc;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                for (int j = 0; j < kNJ; ++j) {
 #pragma unroll
                   for (int b2 = 0; b2 < 2; ++b2) {
                     const int cc = 8 * j + b2;
@@ -1152,25 +1250,25 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                     }
                   }
                 }
-              } else if (a == c0 && bnd == c0 + 64) {
+              } else if (a == c0 && bnd == c0 + kChunkCols) {
                 // whole chunk inside one document: two independent chains per row
                 if (kFloat) {
-                  run[0] = row_max16(ra, 0, run[0]);
+                  run[0] = row_max16<kNJ>(ra, 0, run[0]);
                   if (!kDigits) {
-                    run[1] = row_max16(ra, 1, run[1]);
-                    run[2] = row_max16(rb, 0, run[2]);
-                    run[3] = row_max16(rb, 1, run[3]);
+                    run[1] = row_max16<kNJ>(ra, 1, run[1]);
+                    run[2] = row_max16<kNJ>(rb, 0, run[2]);
+                    run[3] = row_max16<kNJ>(rb, 1, run[3]);
                   }
                 } else {
-                  run_i[0] = row_max16i(ra, 0, run_i[0]);
-                  run_i[1] = row_max16i(ra, 1, run_i[1]);
-                  run_i[2] = row_max16i(rb, 0, run_i[2]);
-                  run_i[3] = row_max16i(rb, 1, run_i[3]);
+                  run_i[0] = row_max16i<kNJ>(ra, 0, run_i[0]);
+                  run_i[1] = row_max16i<kNJ>(ra, 1, run_i[1]);
+                  run_i[2] = row_max16i<kNJ>(rb, 0, run_i[2]);
+                  run_i[3] = row_max16i<kNJ>(rb, 1, run_i[3]);
                 }
               } else {
                 const int la = a - c0 - 2 * tc, lb = bnd - c0 - 2 * tc;  // element (j, b) is column 8j + b here
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                for (int j = 0; j < kNJ; ++j) {
 #pragma unroll
                   for (int b2 = 0; b2 < 2; ++b2) {
                     const int cc = 8 * j + b2;
@@ -1193,7 +1291,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               }
             }
             if (!split && bnd > a) a = bnd;
-            if (e > c1) break;  // the open document continues past this chunk (or no ends are left)
+            // the open document continues past this chunk (or no ends are left); with replicated rows a
+            // warp's one slice is its only chunk, so it also takes the ends after its slice (documents
+            // that hold no further columns of it), keeping every warp's flushes in step
+            if (e > (kRep > 1 ? valid : c1)) break;
             // document meta->seg_doc[sgi] ends: complete each row's maximum across the four threads
             // holding it, stage the row value scaled by the query scale, flush finished documents.
             float best;
@@ -1241,9 +1342,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 run_i[i] = max(run_i[i], __shfl_xor_sync(0xFFFFFFFFu, run_i[i], 2));
               }
               const int32_t bi = tc == 0 ? run_i[0] : tc == 1 ? run_i[1] : tc == 2 ? run_i[2] : run_i[3];
-              best = bi == INT32_MIN ? kLowest : __int2float_rn(bi);
+              best = bi == INT32_MIN ? kLowest : __int2float_rn(bi >> (kPre ? 0 : 4));  // expanding: 16 x dot
             }
-            if (w_store) rowval[(pending * kG + g) * 128 + wrow] = w_valid ? (kSmooth ? best : __fmul_rn(best, qs)) : 0.0F;
+            if (w_store) rowval[(pending * kG + g) * 128 + wslot] = w_valid ? (kSmooth ? best : __fmul_rn(best, qs)) : 0.0F;
             if (ftid == 0) gdoc[pending] = meta->seg_doc[sgi];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -1275,7 +1376,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                   for (int gd = 0; gd < pending; ++gd) {
                     const float* rv = rvq + gd * kG * 128;
                     float sacc = 0.0F;
-                    for (int r = 0; r < Q; ++r) sacc = __fadd_rn(sacc, rv[r]);
+                    for (int r = 0; r < Q; ++r) sacc = __fadd_rn(sacc, rep_max<kRep>(rv, r));
                     const float sc = __fmul_rn(sacc, p.scale);
                     const uint32_t key = float_to_ordered(sc);
                     const int32_t dd = gdoc[gd];
@@ -1309,11 +1410,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                 for (; k + 8 <= Q; k += 8) {
                   float v[8];
 #pragma unroll
-                  for (int i = 0; i < 8; ++i) v[i] = rv[k + i];
+                  for (int i = 0; i < 8; ++i) v[i] = rep_max<kRep>(rv, k + i);
 #pragma unroll
                   for (int i = 0; i < 8; ++i) sacc = __fadd_rn(sacc, v[i]);
                 }
-                for (; k < Q; ++k) sacc = __fadd_rn(sacc, rv[k]);
+                for (; k < Q; ++k) sacc = __fadd_rn(sacc, rep_max<kRep>(rv, k));
                 p.out[static_cast<int64_t>((unit.qpair * kG + gq) * p.qpt + qq) * p.num_docs + gdoc[gd]] =
                     __fmul_rn(sacc, p.scale);
               }
@@ -1399,6 +1500,11 @@ TcPlan plan_for(const DocsView& d, const QueryView& q, int sms) {
 }
 
 }  // namespace
+
+// Replicated query rows for one small tile of int8 query rows (option tc_row_replicas, on by default).
+static std::atomic<int> g_tc_row_replicas{1};
+void set_tc_row_replicas(int on) { g_tc_row_replicas.store(on); }
+int get_tc_row_replicas() { return g_tc_row_replicas.load(); }
 
 bool tc_int8_cache_supported(const DocsView& d) {
   // TMA row coordinates are 32-bit
@@ -1796,9 +1902,24 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
     check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes), "set tc smem");
     kernel<<<grid, tc::kThreads, smem_bytes, stream>>>(prm, tmap, tmap2);
   };
+  // int8 queries in one tile of at most 64 (32) rows: the rows replicated twice (four times) over the
+  // TMEM lane quarters, so all eight epilogue warps share each token tile
+  const int q_rows = q.batch * q.qtok;
+  const int reps = (!twin || digits || !g_tc_row_replicas.load()) ? 1 : (q_rows <= 32 ? 4 : (q_rows <= 64 ? 2 : 1));
+  auto go_rep = [&](auto plain, auto twin_kernel, auto twin2, auto twin4, int smem_bytes) {
+    if (reps == 4) go(twin4, twin4, smem_bytes);
+    else if (reps == 2) go(twin2, twin2, smem_bytes);
+    else go(plain, twin_kernel, smem_bytes);
+  };
   using LayoutF16 = tc::Layout<true, true>;
 #define MSB_TC_GO(TS, PRE, F16, DIG, LAYOUT) \
   go(tc::tc_scan_kernel<TS, PRE, F16, DIG, false>, tc::tc_scan_kernel<TS, PRE, F16, DIG, true>, LAYOUT::bytes)
+  // int8 queries (one tile: optionally replicated rows); BIAS: biased accumulators
+#define MSB_TC_GO8(TS, PRE, BIAS)                                                                            \
+  go_rep(tc::tc_scan_kernel<TS, PRE, false, false, false, false, 0, BIAS>,                                  \
+         tc::tc_scan_kernel<TS, PRE, false, false, true, false, 0, BIAS>,                                   \
+         tc::tc_scan_kernel<TS, PRE, false, false, true, false, 0, BIAS, false, 2>,                         \
+         tc::tc_scan_kernel<TS, PRE, false, false, true, false, 0, BIAS, false, 4>, tc::Layout<PRE, false, false, BIAS>::bytes)
   using LayoutRes = tc::Layout<true, false, true>;
   if (res) {
     go(tc::tc_scan_kernel<true, true, false, true, false, true>, tc::tc_scan_kernel<true, true, false, true, true, true>,
@@ -1832,19 +1953,16 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
     }
   } else if (d.token_scale) {
     // biased accumulators unless a token scale is too large for the exact s * 2^23
-#define MSB_TC_BIAS(PRE)                                                                          \
-  go(tc::tc_scan_kernel<true, PRE, false, false, false, false, 0, true>,                          \
-     tc::tc_scan_kernel<true, PRE, false, false, true, false, 0, true>, tc::Layout<PRE, false, false, true>::bytes)
     if (f16) MSB_TC_GO(true, true, true, false, LayoutF16);
-    else if (pre && d.token_scale_small) MSB_TC_BIAS(true);
-    else if (pre) MSB_TC_GO(true, true, false, false, tc::Layout<true>);
-    else if (d.token_scale_small) MSB_TC_BIAS(false);
-    else MSB_TC_GO(true, false, false, false, tc::Layout<false>);
-#undef MSB_TC_BIAS
+    else if (pre && d.token_scale_small) MSB_TC_GO8(true, true, true);
+    else if (pre) MSB_TC_GO8(true, true, false);
+    else if (d.token_scale_small) MSB_TC_GO8(true, false, true);
+    else MSB_TC_GO8(true, false, false);
   } else {
-    if (pre) MSB_TC_GO(false, true, false, false, tc::Layout<true>);
-    else MSB_TC_GO(false, false, false, false, tc::Layout<false>);
+    if (pre) MSB_TC_GO8(false, true, false);
+    else MSB_TC_GO8(false, false, false);
   }
+#undef MSB_TC_GO8
 #undef MSB_TC_GO
   count_launch();
   check(cudaGetLastError(), "launch tensor-core scan kernel");
