@@ -188,6 +188,7 @@ struct Layout {
   static constexpr int topk_room = (227 * 1024 - 1024 - off_topk) / 16 * 16;
   static constexpr int topk_bytes = topk_room < 8192 ? topk_room : 8192;
   static constexpr int bytes = off_topk + topk_bytes + 1024;  // + alignment slack
+  static constexpr int bytes_plain = off_topk + 1024;         // without the lists (no fused top-k)
   static_assert(bytes <= 227 * 1024 && topk_bytes >= 0, "shared memory budget");
   static_assert(off_b % 1024 == 0 && b_tile % 1024 == 0 && a_tile % 1024 == 0, "128-byte-swizzled operand tiles");
   static_assert(off_uoff % 16 == 0 && off_raw % 16 == 0 && raw_bytes % 16 == 0 && raw_scale_bytes % 16 == 0,
@@ -514,8 +515,11 @@ __device__ __forceinline__ Step step_of(const Item& it, int64_t i) {
 // for only its slice of 128 / kRep columns of a token tile; a document's row maximum is completed across the
 // kRep copies when its group is flushed.  One or two live warps per group would otherwise do a whole
 // tile's epilogue alone.
+// kFuse: the full-scan top-k is selected in the scan (int8 queries, unreplicated rows): each CTA (twin
+// mode: each epilogue group) keeps the k best documents of every query in shared memory and writes them as
+// one candidate block for a merge kernel.  A template parameter, so that the other scans carry none of it.
 template <bool kTokenScale, bool kPre, bool kF16, bool kDigits = false, bool kTwin = false, bool kRes = false,
-          int kTopK = 0, bool kBias = false, bool kSmooth = false, int kRep = 1>
+          int kTopK = 0, bool kBias = false, bool kSmooth = false, int kRep = 1, bool kFuse = false>
 __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap,
                                                               const __grid_constant__ CUtensorMap tmap2) {
   using L = Layout<kPre, kF16, kRes, kBias>;
@@ -526,6 +530,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
   static_assert(!kSmooth || (kTopK == 0 && kPre && kDigits && !kRes), "SmoothSim: digit-plane queries, int8 copies");
   static_assert(kRep == 1 || ((kRep == 2 || kRep == 4) && kTwin && !kDigits && !kF16 && !kRes && !kSmooth),
                 "replicated query rows: one tile of int8 query rows");
+  static_assert(!kFuse || (kRep == 1 && !kDigits && !kF16 && !kRes && kTopK == 0 && !kSmooth),
+                "fused top-k: int8-query MaxSim");
   constexpr int kQuarters = 4 / kRep;               // lane quarters holding distinct query rows
   constexpr int kChunkCols = kRep == 4 ? 32 : 64;   // columns of one pair of TMEM loads
   constexpr int kNJ = kChunkCols / 8;               // 8-column groups per load
@@ -569,7 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
   // fused top-k: per list group (twin mode: one per epilogue group) and query, k entries kept in
   // (score desc, document asc) order; an entry with document -1 is empty
   constexpr int kLists = kTwin ? 2 : 1;
-  const int tk_n = p.topk_k > 0 ? kLists * p.batch * p.topk_k : 0;
+  const int tk_n = kFuse ? kLists * p.batch * p.topk_k : 0;
   float* tks = reinterpret_cast<float*>(smem + L::off_topk);
   int32_t* tki = reinterpret_cast<int32_t*>(tks + tk_n);
   for (int e = threadIdx.x; e < tk_n; e += kThreads) {
@@ -1363,7 +1369,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
             ++sgi;
             if (++pending == kSegGroup || (sgi == nseg && last_tile)) {
               if (!epi_sync()) goto done;
-              if (p.topk_k > 0) {
+              if (kFuse) {
                 // fused top-k: one thread per query takes the group's documents in turn into its list
                 const int K = p.topk_k;
                 for (int qx = ftid; qx < nq; qx += fthreads) {
@@ -1434,7 +1440,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
         mst.next<kMeta>();
       }
     }
-    if (p.topk_k > 0) {
+    if (kFuse) {
       // this CTA's (group's) lists as one candidate block: [B, k] fp32 scores, then [B, k] int64 documents
       // (an empty entry: -inf, INT64_MAX)
       if (!epi_sync()) goto done;
@@ -1759,15 +1765,10 @@ int tc_topk_room(const DocsView& d, const QueryView& q, const ReduceView& red) {
   const bool f16 = !digits && d.format == kFormatInt4 && d.codes16 != nullptr && d.token_scale != nullptr;
   const bool pre = f16 || d.codes8 != nullptr;
   const bool res = d.codes2 != nullptr;
-  const bool list = red.reducer == kTopK2 || red.reducer == kTopK4 || red.reducer == kSmooth;
-  if (res) return tc::Layout<true, false, true>::topk_bytes;
-  if (list) return tc::Layout<true>::topk_bytes;
-  if (digits) return pre ? tc::Layout<true>::topk_bytes : tc::Layout<false>::topk_bytes;
-  if (d.token_scale) {
-    if (f16) return tc::Layout<true, true>::topk_bytes;
-    if (d.token_scale_small) return pre ? tc::Layout<true, false, false, true>::topk_bytes
-                                        : tc::Layout<false, false, false, true>::topk_bytes;
-  }
+  // the fused variants: int8-query MaxSim on int8 operands
+  if (res || digits || f16 || red.reducer != kMaxSim) return 0;
+  if (d.token_scale && d.token_scale_small)
+    return pre ? tc::Layout<true, false, false, true>::topk_bytes : tc::Layout<false, false, false, true>::topk_bytes;
   return pre ? tc::Layout<true>::topk_bytes : tc::Layout<false>::topk_bytes;
 }
 
@@ -1798,7 +1799,13 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
   // caller's candidate workspace holds a block per CTA and group plus one for the empty documents.
   const bool twin_plan = pl.n_qtiles == 1;
   const int lists = twin_plan ? 2 : 1;
-  const bool fused = fuse != nullptr && fuse->k >= 1 &&
+  // int8 queries in one tile of at most 64 (32) rows: the rows replicated twice (four times) over the
+  // TMEM lane quarters, so all eight epilogue warps share each token tile (preferred to fusing the top-k)
+  const int q_rows = q.batch * q.qtok;
+  const int reps = (!twin_plan || q.mode == kQueryF32 || !g_tc_row_replicas.load())
+                       ? 1
+                       : (q_rows <= 32 ? 4 : (q_rows <= 64 ? 2 : 1));
+  const bool fused = fuse != nullptr && fuse->k >= 1 && reps == 1 &&
                      static_cast<int64_t>(lists) * q.batch * fuse->k * 8 <= tc_topk_room(d, q, red) &&
                      static_cast<size_t>(lists * sms + 1) * 16ull * q.batch * fuse->k <= fuse->cand_bytes;
   if (fuse) fuse->done = false;
@@ -1902,39 +1909,41 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
     check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes), "set tc smem");
     kernel<<<grid, tc::kThreads, smem_bytes, stream>>>(prm, tmap, tmap2);
   };
-  // int8 queries in one tile of at most 64 (32) rows: the rows replicated twice (four times) over the
-  // TMEM lane quarters, so all eight epilogue warps share each token tile
-  const int q_rows = q.batch * q.qtok;
-  const int reps = (!twin || digits || !g_tc_row_replicas.load()) ? 1 : (q_rows <= 32 ? 4 : (q_rows <= 64 ? 2 : 1));
-  auto go_rep = [&](auto plain, auto twin_kernel, auto twin2, auto twin4, int smem_bytes) {
-    if (reps == 4) go(twin4, twin4, smem_bytes);
-    else if (reps == 2) go(twin2, twin2, smem_bytes);
-    else go(plain, twin_kernel, smem_bytes);
+  // int8 queries: replicated rows (reps), or the fused top-k, or the plain scan
+  auto go8 = [&](auto plain, auto twin_kernel, auto twin2, auto twin4, auto fplain, auto ftwin, int smem_plain,
+                 int smem_fused) {
+    if (fused) go(fplain, ftwin, smem_fused);
+    else if (reps == 4) go(twin4, twin4, smem_plain);
+    else if (reps == 2) go(twin2, twin2, smem_plain);
+    else go(plain, twin_kernel, smem_plain);
   };
   using LayoutF16 = tc::Layout<true, true>;
 #define MSB_TC_GO(TS, PRE, F16, DIG, LAYOUT) \
-  go(tc::tc_scan_kernel<TS, PRE, F16, DIG, false>, tc::tc_scan_kernel<TS, PRE, F16, DIG, true>, LAYOUT::bytes)
+  go(tc::tc_scan_kernel<TS, PRE, F16, DIG, false>, tc::tc_scan_kernel<TS, PRE, F16, DIG, true>, LAYOUT::bytes_plain)
   // int8 queries (one tile: optionally replicated rows); BIAS: biased accumulators
-#define MSB_TC_GO8(TS, PRE, BIAS)                                                                            \
-  go_rep(tc::tc_scan_kernel<TS, PRE, false, false, false, false, 0, BIAS>,                                  \
-         tc::tc_scan_kernel<TS, PRE, false, false, true, false, 0, BIAS>,                                   \
-         tc::tc_scan_kernel<TS, PRE, false, false, true, false, 0, BIAS, false, 2>,                         \
-         tc::tc_scan_kernel<TS, PRE, false, false, true, false, 0, BIAS, false, 4>, tc::Layout<PRE, false, false, BIAS>::bytes)
+#define MSB_TC_GO8(TS, PRE, BIAS)                                                                        \
+  go8(tc::tc_scan_kernel<TS, PRE, false, false, false, false, 0, BIAS>,                                 \
+      tc::tc_scan_kernel<TS, PRE, false, false, true, false, 0, BIAS>,                                  \
+      tc::tc_scan_kernel<TS, PRE, false, false, true, false, 0, BIAS, false, 2>,                        \
+      tc::tc_scan_kernel<TS, PRE, false, false, true, false, 0, BIAS, false, 4>,                        \
+      tc::tc_scan_kernel<TS, PRE, false, false, false, false, 0, BIAS, false, 1, true>,                 \
+      tc::tc_scan_kernel<TS, PRE, false, false, true, false, 0, BIAS, false, 1, true>,                  \
+      tc::Layout<PRE, false, false, BIAS>::bytes_plain, tc::Layout<PRE, false, false, BIAS>::bytes)
   using LayoutRes = tc::Layout<true, false, true>;
   if (res) {
     go(tc::tc_scan_kernel<true, true, false, true, false, true>, tc::tc_scan_kernel<true, true, false, true, true, true>,
-       LayoutRes::bytes);
+       LayoutRes::bytes_plain);
   } else if (smooth) {
     if (d.token_scale)
       go(tc::tc_scan_kernel<true, true, false, true, false, false, 0, false, true>,
-         tc::tc_scan_kernel<true, true, false, true, true, false, 0, false, true>, tc::Layout<true>::bytes);
+         tc::tc_scan_kernel<true, true, false, true, true, false, 0, false, true>, tc::Layout<true>::bytes_plain);
     else
       go(tc::tc_scan_kernel<false, true, false, true, false, false, 0, false, true>,
-         tc::tc_scan_kernel<false, true, false, true, true, false, 0, false, true>, tc::Layout<true>::bytes);
+         tc::tc_scan_kernel<false, true, false, true, true, false, 0, false, true>, tc::Layout<true>::bytes_plain);
   } else if (topk) {
 #define MSB_TC_TOPK(TS, K) \
   go(tc::tc_scan_kernel<TS, true, false, true, false, false, K>, tc::tc_scan_kernel<TS, true, false, true, true, false, K>, \
-     tc::Layout<true>::bytes)
+     tc::Layout<true>::bytes_plain)
     if (d.token_scale) {
       if (topk == 2) MSB_TC_TOPK(true, 2);
       else MSB_TC_TOPK(true, 4);
