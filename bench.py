@@ -50,11 +50,11 @@ SEED = 20260713
 CHUNK_PAGES = 2_000
 CPU_SAMPLE_PAGES = 128  # pages per step of the CPU legs (the reference arm and cpu_baseline)
 # DRAM bytes (read + write) of one tc_scan_kernel launch per corpus page, from one ncu capture of a
-# 2,000-page case of the same workload (profiles/tc_scan_kernel_2000pages_full.txt: 272.49 MB read +
-# 6.98 MB written).  The kernel streams the resident int8 copy of the codes (128 B per token, twice
+# 2,000-page case of the same workload (profiles/tc_scan_kernel_2000pages_full.txt: 272.37 MB read +
+# 3.95 MB written).  The kernel streams the resident int8 copy of the codes (128 B per token, twice
 # the int4 bytes) plus the token scales once per launch and the score matrix grows with the pages,
 # so traffic scales with the pages a rank holds.
-TC_DRAM_BYTES_PER_PAGE = (272.488192e6 + 6.975232e6) / 2000
+TC_DRAM_BYTES_PER_PAGE = (272.367872e6 + 3.953664e6) / 2000
 METRIC = "full-scan top-10 queries/s (per-token int4 x int8 query, 100k-page corpus)"
 DTYPE = "int8 x int4 (int32 accumulate, fp32 epilogue)"
 DATA = "synthetic (seeded per-page centroid + noise, generated on the GPU; same corpus and queries in both arms)"
