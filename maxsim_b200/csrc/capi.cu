@@ -6,6 +6,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <new>
 #include <string>
@@ -84,6 +85,25 @@ struct DeviceBuf {
   }
   template <class T>
   T* as() const { return static_cast<T*>(ptr); }
+};
+
+// Page-locked host memory (cudaMallocHost), grown on demand.
+struct PinnedBuf {
+  void* ptr = nullptr;
+  size_t cap = 0;
+  void ensure(size_t bytes, const char* what) {
+    if (bytes <= cap) return;
+    void* next = nullptr;
+    check(cudaMallocHost(&next, bytes), what);
+    if (ptr) cudaFreeHost(ptr);
+    ptr = next;
+    cap = bytes;
+  }
+  void release() {
+    if (ptr) cudaFreeHost(ptr);
+    ptr = nullptr;
+    cap = 0;
+  }
 };
 
 struct DeviceGuard {
@@ -179,6 +199,9 @@ struct msb_docs {
   // found once from the host offsets.
   DeviceBuf w_topk, empty_ids;
   int n_empty = -1;
+  // Page-locked staging of the host-buffer entry points: the query in, the results and the tensor-core
+  // error word out, so that a call makes one asynchronous copy each way and synchronises once.
+  PinnedBuf pin_in, pin_out;
 
   size_t bytes_per_token() const { return format == kFormatInt4 ? dim / 2 : dim / 8; }
   int64_t resident_bytes() const {
@@ -201,6 +224,8 @@ struct msb_docs {
                         &w_cands, &w_weights, &w_top_s,    &w_top_i,   &w_override,     &w_fine,
                         &w_tc,    &codes8,   &codes16,   &w_check,        &codes2_8,  &w_full, &w_popc, &w_topk, &empty_ids};
     for (DeviceBuf* b : all) b->release();
+    pin_in.release();
+    pin_out.release();
     for (cudaEvent_t& e : upload_events)
       if (e) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
@@ -593,12 +618,62 @@ void stage_host_options(msb_docs* h, const msb_score_opts* o, int batch, int qto
   }
 }
 
+// Host inputs and outputs up to this size go through the handle's page-locked staging buffers.
+constexpr size_t kPinnedMax = size_t{8} << 20;
+
 const float* stage_query(msb_docs* h, const float* q, int batch, int qtok, cudaStream_t s) {
   const size_t bytes = sizeof(float) * static_cast<size_t>(batch) * qtok * h->dim;
   if (!bytes) return nullptr;
   h->w_query.ensure(bytes, "cudaMalloc resident query cache");
-  check(cudaMemcpyAsync(h->w_query.ptr, q, bytes, cudaMemcpyHostToDevice, s), "copy query to device");
+  const void* src = q;
+  if (bytes <= kPinnedMax) {
+    // every host-buffer call ends with a stream synchronisation, so the staging buffer is free again
+    h->pin_in.ensure(bytes, "cudaMallocHost query staging");
+    std::memcpy(h->pin_in.ptr, q, bytes);
+    src = h->pin_in.ptr;
+  }
+  check(cudaMemcpyAsync(h->w_query.ptr, src, bytes, cudaMemcpyHostToDevice, s), "copy query to device");
   return h->w_query.as<float>();
+}
+
+// Results of a host-buffer call: device -> caller copies, the tensor-core error word, one synchronisation.
+struct HostCopy {
+  void* dst;
+  const void* src;
+  size_t bytes;
+};
+void finish_host_call(msb_docs* h, cudaStream_t s, std::initializer_list<HostCopy> copies, const char* what) {
+  size_t total = 16;  // the error word first
+  for (const HostCopy& c : copies) total += (c.bytes + 15) & ~size_t{15};
+  if (total > kPinnedMax) {
+    for (const HostCopy& c : copies)
+      check(cudaMemcpyAsync(c.dst, c.src, c.bytes, cudaMemcpyDeviceToHost, s), what);
+    check(cudaStreamSynchronize(s), what);
+    check_tc_flag(h, s);
+    return;
+  }
+  h->pin_out.ensure(total, "cudaMallocHost result staging");
+  unsigned char* pin = static_cast<unsigned char*>(h->pin_out.ptr);
+  const bool flag = h->tc_used;
+  if (flag) check(cudaMemcpyAsync(pin, h->w_tc.ptr, sizeof(int), cudaMemcpyDeviceToHost, s), "read tc error flag");
+  size_t off = 16;
+  for (const HostCopy& c : copies) {
+    check(cudaMemcpyAsync(pin + off, c.src, c.bytes, cudaMemcpyDeviceToHost, s), what);
+    off += (c.bytes + 15) & ~size_t{15};
+  }
+  check(cudaStreamSynchronize(s), what);
+  if (flag) {
+    h->tc_used = false;
+    int code = 0;
+    std::memcpy(&code, pin, sizeof(int));
+    if (code != 0)
+      throw CudaFailure("tensor-core scan aborted: a pipeline wait timed out (code " + std::to_string(code) + ")");
+  }
+  off = 16;
+  for (const HostCopy& c : copies) {
+    std::memcpy(c.dst, pin + off, c.bytes);
+    off += (c.bytes + 15) & ~size_t{15};
+  }
 }
 
 msb_docs* create_common(int32_t format, int32_t dim, int64_t num_tokens, const int64_t* offsets_host,
@@ -1052,9 +1127,7 @@ int msb_docs_score(msb_docs* h, const float* query, int32_t batch, int32_t qtok,
     const size_t obytes = sizeof(float) * static_cast<size_t>(batch) * T;
     h->w_scores.ensure(obytes, "cudaMalloc resident score cache");
     run_scan(h, r, d_q, batch, qtok, tg, h->w_scores.as<float>(), s);
-    check(cudaMemcpyAsync(out, h->w_scores.ptr, obytes, cudaMemcpyDeviceToHost, s), "copy output to host");
-    check(cudaStreamSynchronize(s), "synchronize scoring");
-    check_tc_flag(h, s);
+    finish_host_call(h, s, {{out, h->w_scores.ptr, obytes}}, "copy scores to host");
   });
 }
 
@@ -1081,14 +1154,10 @@ int msb_docs_topk(msb_docs* h, const float* query, int32_t batch, int32_t qtok, 
     if (!fuse.done)
       launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, k, nullptr, false,
                        h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
-    check(cudaMemcpyAsync(out_scores, h->w_top_s.ptr, sizeof(float) * static_cast<size_t>(batch) * k,
-                          cudaMemcpyDeviceToHost, s),
-          "copy top scores to host");
-    check(cudaMemcpyAsync(out_ids, h->w_top_i.ptr, sizeof(int64_t) * static_cast<size_t>(batch) * k,
-                          cudaMemcpyDeviceToHost, s),
-          "copy top indices to host");
-    check(cudaStreamSynchronize(s), "synchronize top-k");
-    check_tc_flag(h, s);
+    finish_host_call(h, s,
+                     {{out_scores, h->w_top_s.ptr, sizeof(float) * static_cast<size_t>(batch) * k},
+                      {out_ids, h->w_top_i.ptr, sizeof(int64_t) * static_cast<size_t>(batch) * k}},
+                     "copy top-k to host");
   });
 }
 
@@ -1150,12 +1219,9 @@ int msb_docs_cascade_topk(msb_docs* h, const float* query, int32_t batch, int32_
       launch_topk_rows(h->w_fine.as<float>(), m, batch, m, k, h->w_cands.as<int64_t>(), true,
                        h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
     }
-    check(cudaMemcpyAsync(out_scores, h->w_top_s.ptr, sizeof(float) * B * k, cudaMemcpyDeviceToHost, s),
-          "copy cascade scores to host");
-    check(cudaMemcpyAsync(out_ids, h->w_top_i.ptr, sizeof(int64_t) * B * k, cudaMemcpyDeviceToHost, s),
-          "copy cascade indices to host");
-    check(cudaStreamSynchronize(s), "synchronize cascade");
-    check_tc_flag(h, s);
+    finish_host_call(h, s, {{out_scores, h->w_top_s.ptr, sizeof(float) * B * k},
+                            {out_ids, h->w_top_i.ptr, sizeof(int64_t) * B * k}},
+                     "copy cascade top-k to host");
   });
 }
 

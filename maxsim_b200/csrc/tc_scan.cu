@@ -1486,11 +1486,34 @@ struct TcPlan {
   int64_t n_ranges;  // token-quantile document ranges before the per-range document cap
 };
 
+constexpr int kMaxDevices = 64;
+
 int sm_count() {
+  static std::atomic<int> cached[kMaxDevices] = {};  // per device, queried once
   int dev = 0, sms = 0;
   check(cudaGetDevice(&dev), "get device");
+  if (dev >= 0 && dev < kMaxDevices && (sms = cached[dev].load(std::memory_order_relaxed)) > 0) return sms;
   check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "query SM count");
+  if (dev >= 0 && dev < kMaxDevices) cached[dev].store(sms, std::memory_order_relaxed);
   return sms;
+}
+
+// The dynamic shared-memory limit of a kernel, raised once per (device, kernel) to the most it was asked for.
+void raise_smem_limit(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<int, const void*>, int>> raised;
+  int dev = 0;
+  check(cudaGetDevice(&dev), "get device");
+  std::lock_guard<std::mutex> lock(mu);
+  for (auto& e : raised)
+    if (e.first.first == dev && e.first.second == kernel) {
+      if (e.second >= bytes) return;
+      check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), "set tc smem");
+      e.second = bytes;
+      return;
+    }
+  check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), "set tc smem");
+  raised.push_back({{dev, kernel}, bytes});
 }
 
 TcPlan plan_for(const DocsView& d, const QueryView& q, int sms) {
@@ -1684,7 +1707,7 @@ void launch_expand_codes8(const uint8_t* codes, int64_t num_tokens, uint8_t* out
 
 namespace {
 // 2D tensor map over the int8 copy: {128 bytes, N rows}, box {128, 128}, 128-byte swizzle, zero fill.
-CUtensorMap make_operand_map(const void* base, int64_t num_tokens, bool f16) {
+CUtensorMap encode_operand_map(const void* base, int64_t num_tokens, bool f16) {
   using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -1713,6 +1736,28 @@ CUtensorMap make_operand_map(const void* base, int64_t num_tokens, bool f16) {
                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw CudaFailure("cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
+  return m;
+}
+
+// The map depends only on (base, rows, f16): the last few are kept, so a search encodes none.
+CUtensorMap make_operand_map(const void* base, int64_t num_tokens, bool f16) {
+  struct Entry {
+    const void* base;
+    int64_t rows;
+    bool f16;
+    CUtensorMap map;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> maps;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Entry& e : maps)
+      if (e.base == base && e.rows == num_tokens && e.f16 == f16) return e.map;
+  }
+  const CUtensorMap m = encode_operand_map(base, num_tokens, f16);
+  std::lock_guard<std::mutex> lock(mu);
+  if (maps.size() >= 16) maps.erase(maps.begin());
+  maps.push_back(Entry{base, num_tokens, f16, m});
   return m;
 }
 }  // namespace
@@ -1906,7 +1951,7 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
   const CUtensorMap tmap2 = res ? make_operand_map(d.codes2_8, d.num_tokens, false) : CUtensorMap{};
   auto go = [&](auto plain, auto twin_kernel, int smem_bytes) {
     auto kernel = twin ? twin_kernel : plain;
-    check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes), "set tc smem");
+    raise_smem_limit(reinterpret_cast<const void*>(kernel), smem_bytes);
     kernel<<<grid, tc::kThreads, smem_bytes, stream>>>(prm, tmap, tmap2);
   };
   // int8 queries: replicated rows (reps), or the fused top-k, or the plain scan
