@@ -1,10 +1,10 @@
-"""Document-sharded search over NCCL on two GPUs against single-GPU search.
+"""Document-sharded search over NCCL on two and four GPUs against single-GPU search.
 
-Two ranks (one process per GPU, NCCL over 127.0.0.1) each hold a contiguous
-document shard; ``ShardedReranker.search`` must return exactly the top-k of
-one handle holding the whole corpus: same ids, same scores, ties across the
-shard boundary resolved to the lower global id.  One case leaves the second
-shard fewer documents than k.  Needs at least two GPUs; skipped otherwise.
+Two or four ranks (one process per GPU, NCCL over 127.0.0.1) each hold a
+contiguous document shard; ``ShardedReranker.search`` must return exactly the
+top-k of one handle holding the whole corpus: same ids, same scores, ties
+across shard boundaries resolved to the lower global id.  One case leaves the
+second shard fewer documents than k.  Skipped with fewer GPUs than ranks.
 """
 
 import os
@@ -50,6 +50,7 @@ def _rank_main(rank, world, port, k, split, result_path):
         off, docs, q = _corpus()
         packed = m.pack_int4_symmetric(docs, off, scale_granularity="token")
         bounds = shard_bounds(off, world) if split is None else np.array([0, split, len(off) - 1], np.int64)
+        assert len(bounds) == world + 1
         lo, hi = int(bounds[rank]), int(bounds[rank + 1])
         t_lo, t_hi = int(off[lo]), int(off[hi])
         local = mc.CudaInt4PackedDocs(np.ascontiguousarray(packed.data[t_lo:t_hi]), shard_offsets(off, lo, hi), 128,
@@ -66,16 +67,16 @@ def _rank_main(rank, world, port, k, split, result_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("k,split", [(10, None), (12, 292)])
-def test_two_gpu_sharded_search_equals_single_gpu(tmp_path, k, split):
+@pytest.mark.parametrize("world,k,split", [(2, 10, None), (2, 12, 292), (4, 10, None)])
+def test_sharded_search_equals_single_gpu(tmp_path, world, k, split):
     import torch
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
     result = str(tmp_path / "sharded.npz")
-    mp.spawn(_rank_main, args=(2, _free_port(), k, split, result), nprocs=2, join=True)
+    mp.spawn(_rank_main, args=(world, _free_port(), k, split, result), nprocs=world, join=True)
     got = np.load(result)
     np.testing.assert_array_equal(got["i"], got["want_i"])
     np.testing.assert_array_equal(got["s"], got["want_s"])
