@@ -33,6 +33,9 @@ void launch_tc_scan(const DocsView&, const QueryView&, const ReduceView&, const 
                     size_t ws_bytes, cudaStream_t, TopkFuse* fuse);
 size_t tc_topk_cand_bytes(const QueryView&, int k);
 size_t tc_scan_workspace_bytes(const DocsView&, const QueryView&, const TargetsView&);
+size_t tc_candidate_units_bytes(const DocsView&, const QueryView&, const TargetsView&);
+void launch_tc_scan_candidates(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, float* scores,
+                               void* ws, void* units, size_t units_bytes, cudaStream_t);
 bool tc_int8_cache_supported(const DocsView&);
 bool popc_scan_supported(const DocsView&, const QueryView&, const ReduceView&, const TargetsView&, bool residual);
 size_t popc_scan_workspace_bytes(const QueryView&);
@@ -171,7 +174,8 @@ struct msb_docs {
   // Workspace (grows monotonically, reused across calls).
   DeviceBuf w_query, w_qcodes, w_qwords, w_qscale, w_qsum, w_scores, w_cands, w_weights, w_top_s, w_top_i,
       w_override, w_fine, w_tc, w_popc,
-      w_full;  // full-scan scores that candidate lists are gathered from
+      w_full,   // full-scan scores that candidate lists are gathered from
+      w_units;  // work units of a candidate-list tensor-core scan
   std::vector<int64_t> host_offsets;
   bool tc_used = false;  // the tensor-core engine ran since the last error check
   uint64_t serial = 0;   // unique corpus id for caches keyed on a corpus
@@ -212,7 +216,7 @@ struct msb_docs {
     return static_cast<int64_t>(w_query.cap + w_qcodes.cap + w_qwords.cap + w_qscale.cap + w_qsum.cap +
                                 w_scores.cap + w_cands.cap + w_weights.cap + w_top_s.cap + w_top_i.cap +
                                 w_override.cap + w_fine.cap + w_tc.cap + w_check.cap + w_full.cap +
-                                w_popc.cap + w_topk.cap);
+                                w_popc.cap + w_topk.cap + w_units.cap);
   }
   ~msb_docs() {
     int prev = -1;
@@ -222,7 +226,8 @@ struct msb_docs {
     DeviceBuf* all[] = {&codes,   &offsets,  &token_scale, &doc_scale, &residual_codes, &residual_token_scale,
                         &w_query, &w_qcodes, &w_qwords,    &w_qscale,  &w_qsum,         &w_scores,
                         &w_cands, &w_weights, &w_top_s,    &w_top_i,   &w_override,     &w_fine,
-                        &w_tc,    &codes8,   &codes16,   &w_check,        &codes2_8,  &w_full, &w_popc, &w_topk, &empty_ids};
+                        &w_tc,    &codes8,   &codes16,   &w_check,        &codes2_8,  &w_full, &w_popc, &w_topk, &empty_ids,
+                        &w_units};
     for (DeviceBuf* b : all) b->release();
     pin_in.release();
     pin_out.release();
@@ -332,6 +337,22 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
 // of the SIMT rescoring of a candidate.  Returns false (nothing done) when the list is shorter, the SIMT
 // engine is forced, or the tensor-core engine does not support the full scan.  (If a binary corpus or
 // the residual stream cannot get its int8 copy, the full scan runs on the SIMT engine: correct, slower.)
+// A [batch, num_docs] score scratch (w_full) for a candidate-list scan; false when the device has no
+// memory for it (the lists are then rescored on the SIMT engine).
+bool candidate_scratch(msb_docs* h, int batch) {
+  const size_t bytes = sizeof(float) * static_cast<size_t>(batch) * h->num_docs;
+  if (bytes <= h->w_full.cap) return true;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  h->w_full.release();
+  h->w_full.ptr = p;
+  h->w_full.cap = bytes;
+  return true;
+}
+
 bool scan_targets_via_full_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, int qtok,
                                 const TargetsView& tg, float* d_out, cudaStream_t stream) {
   if (!tg.ids || g_engine.load() == 1 || tg.count * 16 < h->num_docs || batch <= 0 || qtok <= 0) return false;
@@ -341,18 +362,8 @@ bool scan_targets_via_full_scan(msb_docs* h, const Resolved& r, const float* d_q
   qv.qtok = qtok;
   qv.mode = r.mode;
   if (!tc_scan_supported(r.docs, qv, r.red, TargetsView{}, r.residual)) return false;
-  const size_t bytes = sizeof(float) * static_cast<size_t>(batch) * h->num_docs;
-  if (bytes > h->w_full.cap) {
-    // no room for the full score matrix: rescore the list instead (the shorter output of the SIMT engine)
-    void* p = nullptr;
-    if (cudaMalloc(&p, bytes) != cudaSuccess) {
-      (void)cudaGetLastError();
-      return false;
-    }
-    h->w_full.release();
-    h->w_full.ptr = p;
-    h->w_full.cap = bytes;
-  }
+  // no room for the full score matrix: rescore the list instead (the shorter output of the SIMT engine)
+  if (!candidate_scratch(h, batch)) return false;
   run_scan(h, r, d_query, batch, qtok, TargetsView{}, h->w_full.as<float>(), stream);
   launch_gather_scores(h->w_full.as<float>(), h->num_docs, batch, tg.ids, tg.count, tg.per_row != 0, d_out, stream);
   return true;
@@ -390,7 +401,9 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
   qv.batch = batch;
   qv.qtok = qtok;
   qv.mode = r.mode;
-  const int engine = g_engine.load();
+  // (the popcount engine scans sign codes; a residual stream, as in a cascade's rescoring, takes the
+  // automatic route)
+  const int engine = g_engine.load() == 3 && r.residual ? 0 : g_engine.load();
   if (engine == 3) {
     // AND + popcount over the sign codes (forced; see popc_scan.cu)
     if (!popc_scan_supported(r.docs, qv, r.red, tg, r.residual))
@@ -481,6 +494,11 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
       }
     }
   }
+  if (use_tc && tg.ids && !candidate_scratch(h, batch)) {
+    // candidate lists score into a [B, D] scratch; without memory for it, the SIMT engine
+    if (engine == 2) throw NotSupported("no device memory for the tensor-core candidate scan's score matrix");
+    use_tc = false;
+  }
   if (use_tc && r.mode == kQueryI8 && dv.token_scale) dv.token_scale_small = token_scales_small(h, dv.token_scale, stream);
   const int64_t rows = static_cast<int64_t>(batch) * qtok;
   if (r.mode == kQueryI8) {
@@ -510,9 +528,19 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
       qv.i8_words = h->w_qwords.as<int32_t>();
       qv.row_scale = h->w_qscale.as<float>();
     }
-    const size_t ws = tc_scan_workspace_bytes(dv, qv, tg);
+    const size_t ws = tc_scan_workspace_bytes(dv, qv, TargetsView{});
     h->w_tc.ensure(ws > 0 ? ws : 16, "cudaMalloc tensor-core scan workspace");
-    launch_tc_scan(dv, qv, r.red, tg, d_out, h->w_tc.ptr, h->w_tc.cap, stream, tg.ids ? nullptr : fuse);
+    if (tg.ids) {
+      // Candidate lists shorter than a sixteenth of the corpus: each listed document is a work unit of
+      // the same scan, scored into the [B, D] scratch at its position and gathered
+      h->w_units.ensure(tc_candidate_units_bytes(dv, qv, tg), "cudaMalloc candidate work units");
+      launch_tc_scan_candidates(dv, qv, r.red, tg, h->w_full.as<float>(), h->w_tc.ptr, h->w_units.ptr,
+                                h->w_units.cap, stream);
+      launch_gather_scores(h->w_full.as<float>(), h->num_docs, batch, tg.ids, tg.count, tg.per_row != 0, d_out,
+                           stream);
+    } else {
+      launch_tc_scan(dv, qv, r.red, tg, d_out, h->w_tc.ptr, h->w_tc.cap, stream, fuse);
+    }
     h->tc_used = true;
     return;
   }
@@ -1212,10 +1240,8 @@ int msb_docs_cascade_topk(msb_docs* h, const float* query, int32_t batch, int32_
       tg.count = m;
       tg.per_row = 1;
       // Rescoring of per-row candidate lists: from the full tensor-core residual scan when the lists are
-      // long enough, else on the SIMT engine.
-      if (!scan_targets_via_full_scan(h, rf, d_q, batch, qtok, tg, h->w_fine.as<float>(), s))
-        launch_simt_scan(rf.docs, QueryView{d_q, nullptr, nullptr, nullptr, nullptr, batch, qtok, kQueryF32}, rf.red,
-                         tg, true, h->w_fine.as<float>(), s);
+      // long enough, else from a tensor-core scan of the listed documents (or the SIMT engine).
+      run_scan(h, rf, d_q, batch, qtok, tg, h->w_fine.as<float>(), s);
       launch_topk_rows(h->w_fine.as<float>(), m, batch, m, k, h->w_cands.as<int64_t>(), true,
                        h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
     }

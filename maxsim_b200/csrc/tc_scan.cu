@@ -1781,8 +1781,10 @@ bool tc_scan_supported(const DocsView& d, const QueryView& q, const ReduceView& 
   const bool residual_ok = !residual || ((d.format == kFormatInt4 || d.format == kFormatBinary) &&
                                          q.mode == kQueryF32 && d.token_scale != nullptr && d.codes2 != nullptr &&
                                          d.token_scale2 != nullptr);
-  return residual_ok && format_ok && d.dim == 128 && mode_ok && reducer_ok && tg.ids == nullptr &&
-         q.qtok >= 1 && q.batch >= 1 && d.num_docs <= 0x7FFFFFFF && d.host_offsets != nullptr;
+  // candidate lists run over units built from the lists (launch_tc_scan_candidates)
+  (void)tg;
+  return residual_ok && format_ok && d.dim == 128 && mode_ok && reducer_ok && q.qtok >= 1 && q.batch >= 1 &&
+         d.num_docs <= 0x7FFFFFFF && d.host_offsets != nullptr;
 }
 
 size_t tc_scan_workspace_bytes(const DocsView& d, const QueryView& q, const TargetsView&) {
@@ -1823,82 +1825,33 @@ size_t tc_topk_cand_bytes(const QueryView& q, int k) {
   return static_cast<size_t>(2 * sm_count() + 1) * 16ull * q.batch * k;
 }
 
-void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red, const TargetsView&, float* out, void* ws,
-                    size_t ws_bytes, cudaStream_t stream, TopkFuse* fuse) {
-  // The unit table depends only on the corpus and the query tiling; it is
-  // built once per (workspace, corpus, tiling) and kept in the workspace.
-  static std::mutex cache_mu;
-  static std::vector<std::pair<UnitCacheKey, int>> cache;  // key -> number of units
-  const int sms = sm_count();
-  const TcPlan pl = plan_for(d, q, sms);
-  const UnitCacheKey key{ws, d.corpus_id, pl.n_ranges, pl.n_pairs};
-  int* err = static_cast<int*>(ws);
-  tc::Unit* d_units = reinterpret_cast<tc::Unit*>(static_cast<unsigned char*>(ws) + 256);
-  int num_units = -1;
-  {
-    std::lock_guard<std::mutex> lock(cache_mu);
-    for (auto& e : cache)
-      if (e.first == key) num_units = e.second;
-  }
-  // Fused top-k when the lists fit the chosen layout (twin mode keeps one set per epilogue group) and the
-  // caller's candidate workspace holds a block per CTA and group plus one for the empty documents.
-  const bool twin_plan = pl.n_qtiles == 1;
-  const int lists = twin_plan ? 2 : 1;
-  // int8 queries in one tile of at most 64 (32) rows: the rows replicated twice (four times) over the
-  // TMEM lane quarters, so all eight epilogue warps share each token tile (preferred to fusing the top-k)
+namespace {
+// Query rows copied over the TMEM lane quarters for a pass of one tile of int8 query rows: four copies of
+// at most 32 rows, two of at most 64 (option tc_row_replicas), else 1.
+int row_copies(const TcPlan& pl, const QueryView& q) {
   const int q_rows = q.batch * q.qtok;
-  const int reps = (!twin_plan || q.mode == kQueryF32 || !g_tc_row_replicas.load())
-                       ? 1
-                       : (q_rows <= 32 ? 4 : (q_rows <= 64 ? 2 : 1));
-  const bool fused = fuse != nullptr && fuse->k >= 1 && reps == 1 &&
-                     static_cast<int64_t>(lists) * q.batch * fuse->k * 8 <= tc_topk_room(d, q, red) &&
-                     static_cast<size_t>(lists * sms + 1) * 16ull * q.batch * fuse->k <= fuse->cand_bytes;
-  if (fuse) fuse->done = false;
-  // Empty documents never appear in a tile; their score is 0.
-  if (!fused)
-    check(cudaMemsetAsync(out, 0, sizeof(float) * static_cast<size_t>(q.batch) * d.num_docs, stream), "zero scores");
-  if (num_units < 0) {
-    // Document ranges cut at the token quantiles r * N / n_ranges, each split
-    // further to at most kMaxRangeDocs documents; range-major units.
-    std::vector<tc::Unit> units;
-    const int64_t* off = d.host_offsets;
-    const int64_t D = d.num_docs, N = d.num_tokens;
-    int64_t lo = 0;
-    for (int64_t r = 1; r <= pl.n_ranges && lo < D; ++r) {
-      int64_t hi = D;
-      if (r < pl.n_ranges) {
-        const int64_t target = static_cast<int64_t>((static_cast<__int128>(N) * r) / pl.n_ranges);
-        hi = static_cast<int64_t>(std::lower_bound(off + lo, off + D + 1, target) - off);
-        if (hi > D) hi = D;
-      }
-      while (lo < hi) {
-        const int64_t h2 = std::min<int64_t>(hi, lo + tc::kMaxRangeDocs);  // unit offsets live in shared memory
-        if (off[h2] > off[lo])
-          for (int t = 0; t < pl.n_pairs; ++t) units.push_back(tc::Unit{lo, h2, off[lo], off[h2], t, 0});
-        lo = h2;
-      }
-    }
-    const size_t need = 256 + sizeof(tc::Unit) * units.size();
-    if (need > ws_bytes) throw CudaFailure("tensor-core scan workspace too small");
-    if (!units.empty()) {
-      check(cudaMemcpyAsync(d_units, units.data(), sizeof(tc::Unit) * units.size(), cudaMemcpyHostToDevice, stream),
-            "upload tc work units");
-      check(cudaStreamSynchronize(stream), "synchronize tc unit upload");
-    }
-    num_units = static_cast<int>(units.size());
-    std::lock_guard<std::mutex> lock(cache_mu);
-    for (auto it = cache.begin(); it != cache.end();)
-      it = it->first.ws == ws ? cache.erase(it) : it + 1;
-    cache.emplace_back(key, num_units);
-  }
-  if (num_units == 0) {
-    if (!fused) return;
-    // every document is empty: the empty documents' block alone
-    launch_empty_block(fuse->cand, q.batch, fuse->k, fuse->empty_ids, std::min(fuse->n_empty, fuse->k), stream);
-    launch_merge_shard_topk(fuse->cand, 1, q.batch, fuse->k, nullptr, fuse->out_s, fuse->out_i, stream);
-    fuse->done = true;
-    return;
-  }
+  if (pl.n_qtiles != 1 || q.mode == kQueryF32 || !g_tc_row_replicas.load()) return 1;
+  return q_rows <= 32 ? 4 : (q_rows <= 64 ? 2 : 1);
+}
+
+// Fused top-k when the pass has no row copies, the lists fit the chosen layout (twin mode keeps one set per
+// epilogue group) and the caller's candidate workspace holds a block per CTA and group plus one for the
+// empty documents.
+bool fuse_fits(const DocsView& d, const QueryView& q, const ReduceView& red, const TcPlan& pl, int sms,
+               const TopkFuse* fuse) {
+  const int lists = pl.n_qtiles == 1 ? 2 : 1;
+  return fuse != nullptr && fuse->k >= 1 && row_copies(pl, q) == 1 &&
+         static_cast<int64_t>(lists) * q.batch * fuse->k * 8 <= tc_topk_room(d, q, red) &&
+         static_cast<size_t>(lists * sms + 1) * 16ull * q.batch * fuse->k <= fuse->cand_bytes;
+}
+
+// The scan over a unit table on the device: the kernel variant for the corpus, queries and reducer, then
+// (fused top-k) the merge of the CTAs' candidate blocks.
+void dispatch_tc(const DocsView& d, const QueryView& q, const ReduceView& red, const TcPlan& pl, int sms,
+                 const tc::Unit* d_units, int num_units, float* out, int* err, bool fused, TopkFuse* fuse,
+                 cudaStream_t stream) {
+  const int reps = row_copies(pl, q);
+  const int lists = pl.n_qtiles == 1 ? 2 : 1;
   check(cudaMemsetAsync(err, 0, sizeof(int), stream), "clear tc error flag");
   tc::Params prm{};
   prm.codes = d.codes;
@@ -2032,6 +1985,145 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
     launch_merge_shard_topk(fuse->cand, blocks, q.batch, fuse->k, nullptr, fuse->out_s, fuse->out_i, stream);
     fuse->done = true;
   }
+}
+}  // namespace
+
+void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red, const TargetsView&, float* out, void* ws,
+                    size_t ws_bytes, cudaStream_t stream, TopkFuse* fuse) {
+  // The unit table depends only on the corpus and the query tiling; it is
+  // built once per (workspace, corpus, tiling) and kept in the workspace.
+  static std::mutex cache_mu;
+  static std::vector<std::pair<UnitCacheKey, int>> cache;  // key -> number of units
+  const int sms = sm_count();
+  const TcPlan pl = plan_for(d, q, sms);
+  const UnitCacheKey key{ws, d.corpus_id, pl.n_ranges, pl.n_pairs};
+  int* err = static_cast<int*>(ws);
+  tc::Unit* d_units = reinterpret_cast<tc::Unit*>(static_cast<unsigned char*>(ws) + 256);
+  int num_units = -1;
+  {
+    std::lock_guard<std::mutex> lock(cache_mu);
+    for (auto& e : cache)
+      if (e.first == key) num_units = e.second;
+  }
+  const bool fused = fuse_fits(d, q, red, pl, sms, fuse);
+  if (fuse) fuse->done = false;
+  // Empty documents never appear in a tile; their score is 0.
+  if (!fused)
+    check(cudaMemsetAsync(out, 0, sizeof(float) * static_cast<size_t>(q.batch) * d.num_docs, stream), "zero scores");
+  if (num_units < 0) {
+    // Document ranges cut at the token quantiles r * N / n_ranges, each split
+    // further to at most kMaxRangeDocs documents; range-major units.
+    std::vector<tc::Unit> units;
+    const int64_t* off = d.host_offsets;
+    const int64_t D = d.num_docs, N = d.num_tokens;
+    int64_t lo = 0;
+    for (int64_t r = 1; r <= pl.n_ranges && lo < D; ++r) {
+      int64_t hi = D;
+      if (r < pl.n_ranges) {
+        const int64_t target = static_cast<int64_t>((static_cast<__int128>(N) * r) / pl.n_ranges);
+        hi = static_cast<int64_t>(std::lower_bound(off + lo, off + D + 1, target) - off);
+        if (hi > D) hi = D;
+      }
+      while (lo < hi) {
+        const int64_t h2 = std::min<int64_t>(hi, lo + tc::kMaxRangeDocs);  // unit offsets live in shared memory
+        if (off[h2] > off[lo])
+          for (int t = 0; t < pl.n_pairs; ++t) units.push_back(tc::Unit{lo, h2, off[lo], off[h2], t, 0});
+        lo = h2;
+      }
+    }
+    const size_t need = 256 + sizeof(tc::Unit) * units.size();
+    if (need > ws_bytes) throw CudaFailure("tensor-core scan workspace too small");
+    if (!units.empty()) {
+      check(cudaMemcpyAsync(d_units, units.data(), sizeof(tc::Unit) * units.size(), cudaMemcpyHostToDevice, stream),
+            "upload tc work units");
+      check(cudaStreamSynchronize(stream), "synchronize tc unit upload");
+    }
+    num_units = static_cast<int>(units.size());
+    std::lock_guard<std::mutex> lock(cache_mu);
+    for (auto it = cache.begin(); it != cache.end();)
+      it = it->first.ws == ws ? cache.erase(it) : it + 1;
+    cache.emplace_back(key, num_units);
+  }
+  if (num_units == 0) {
+    if (!fused) return;
+    // every document is empty: the empty documents' block alone
+    launch_empty_block(fuse->cand, q.batch, fuse->k, fuse->empty_ids, std::min(fuse->n_empty, fuse->k), stream);
+    launch_merge_shard_topk(fuse->cand, 1, q.batch, fuse->k, nullptr, fuse->out_s, fuse->out_i, stream);
+    fuse->done = true;
+    return;
+  }
+  dispatch_tc(d, q, red, pl, sms, d_units, num_units, out, err, fused, fuse, stream);
+}
+
+namespace tc {
+// Work units of a candidate-list scan, one per (candidate document, query-tile pair): a shared list gives
+// every pair every candidate, per-row lists give each candidate to the pair holding its row.  An empty
+// candidate document gets an empty unit and its score 0 in the rows concerned (an empty document never
+// appears in a tile); an id outside [0, D) gets an empty unit.  A document listed twice is scanned twice
+// and writes the same values twice.
+__global__ void candidate_units_kernel(const int64_t* __restrict__ ids, int64_t count, int per_row, int batch,
+                                       int qpt, int n_pairs, const int64_t* __restrict__ offsets, int64_t num_docs,
+                                       Unit* __restrict__ units, float* __restrict__ scores) {
+  const int64_t n = per_row ? static_cast<int64_t>(batch) * count : count * n_pairs;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < n;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t d;
+    int pair, row = 0;
+    if (per_row) {
+      row = static_cast<int>(u / count);
+      d = ids[u];
+      pair = (row / qpt) / kG;
+    } else {
+      d = ids[u / n_pairs];
+      pair = static_cast<int>(u % n_pairs);
+    }
+    Unit un{0, 0, 0, 0, pair, 0};
+    if (d >= 0 && d < num_docs) {
+      const int64_t lo = offsets[d], hi = offsets[d + 1];
+      un.d_lo = d;
+      un.d_hi = hi > lo ? d + 1 : d;
+      un.tok_lo = lo;
+      un.tok_hi = hi > lo ? hi : lo;
+      if (hi <= lo) {
+        if (per_row) {
+          scores[static_cast<int64_t>(row) * num_docs + d] = 0.0F;
+        } else {
+          const int r0 = pair * kG * qpt, r1 = min(batch, r0 + kG * qpt);
+          for (int r = r0; r < r1; ++r) scores[static_cast<int64_t>(r) * num_docs + d] = 0.0F;
+        }
+      }
+    }
+    units[u] = un;
+  }
+}
+}  // namespace tc
+
+// Units a candidate-list scan needs (tc::Unit each).
+size_t tc_candidate_units_bytes(const DocsView& d, const QueryView& q, const TargetsView& tg) {
+  const TcPlan pl = plan_for(d, q, sm_count());
+  const int64_t n = tg.per_row ? static_cast<int64_t>(q.batch) * tg.count : tg.count * pl.n_pairs;
+  return sizeof(tc::Unit) * static_cast<size_t>(n > 0 ? n : 1);
+}
+
+// A candidate-list scan on the tensor cores: the documents the lists name, each its own work unit, scored
+// into `scores` [B, D] at their document positions (only those positions are written; the caller gathers
+// them).  `ws` holds the kernel's error word, `units` the unit table.
+void launch_tc_scan_candidates(const DocsView& d, const QueryView& q, const ReduceView& red, const TargetsView& tg,
+                               float* scores, void* ws, void* units, size_t units_bytes, cudaStream_t stream) {
+  const int sms = sm_count();
+  const TcPlan pl = plan_for(d, q, sms);
+  const int64_t n = tg.per_row ? static_cast<int64_t>(q.batch) * tg.count : tg.count * pl.n_pairs;
+  if (n <= 0) return;
+  if (n > 0x3FFFFFFF || sizeof(tc::Unit) * static_cast<size_t>(n) > units_bytes)
+    throw CudaFailure("candidate unit workspace too small");
+  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 148LL * 8));
+  tc::candidate_units_kernel<<<blocks, 256, 0, stream>>>(tg.ids, tg.count, tg.per_row ? 1 : 0, q.batch, pl.qpt,
+                                                         pl.n_pairs, d.offsets, d.num_docs,
+                                                         static_cast<tc::Unit*>(units), scores);
+  count_launch();
+  check(cudaGetLastError(), "launch candidate unit kernel");
+  dispatch_tc(d, q, red, pl, sms, static_cast<const tc::Unit*>(units), static_cast<int>(n), scores,
+              static_cast<int*>(ws), false, nullptr, stream);
 }
 
 }  // namespace msb

@@ -350,8 +350,9 @@ def test_residual_stream_replaced_on_the_handle(engine):
 
 
 def test_candidate_lists_long_enough_read_the_full_scan(engine):
-    """A candidate list naming at least one document in 16 is read out of the full tensor-core scan, so its
-    scores equal the full scan's columns exactly; a shorter list is rescored on the SIMT engine."""
+    """A candidate list naming at least one document in 16 is read out of the full tensor-core scan, a
+    shorter one scanned by the same kernel over its documents only: either way its scores equal the full
+    scan's columns exactly, and the SIMT engine's within 1e-4."""
     import maxsim_b200 as m
 
     docs, off, packed, res, dev = _residual_corpus(320, 90, seed=61)
@@ -372,8 +373,9 @@ def test_candidate_lists_long_enough_read_the_full_scan(engine):
         full = run()
         np.testing.assert_array_equal(run(long_list), full[:, long_list])
         got_short = run(short_list)
+        np.testing.assert_array_equal(got_short, full[:, short_list])
         engine.set_engine(1)
-        np.testing.assert_array_equal(got_short, run(short_list))
+        np.testing.assert_allclose(got_short, run(short_list), rtol=1e-4, atol=1e-4)
 
 
 @pytest.mark.parametrize("batch,qtok", [(1, 32), (3, 16)])
