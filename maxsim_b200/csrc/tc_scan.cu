@@ -697,14 +697,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
     const int xwarp = warp - kXWarp0;
     Ring raw, stg, mst;
     int iter = 0;
+    // the tile pair whose query rows each A buffer holds: within a launch they depend on the pair alone, so
+    // a buffer that already holds the item's pair is handed to the MMA again unwritten (runs of units of
+    // one pair: small batches, candidate lists)
+    int32_t a_held[2] = {-1, -1};
     for (int w = blockIdx.x; w < p.num_items; w += gridDim.x, ++iter) {
       const Item it = load_item<kTwin>(p, w);
       const int32_t qpair = it.un[0].qpair;  // twin mode: both units hold the one query tile
       const int abuf = iter % L::a_bufs;
       const int ause = iter / L::a_bufs;
       if (ause >= 1 && !mbar_wait(&a_empty[abuf], (ause - 1) & 1, abort_flag, p.error, 11)) goto done;
+      const bool a_build = a_held[abuf] != qpair;
+      a_held[abuf] = qpair;
 #pragma unroll 1
-      for (int row = xtid; row < 128; row += kXWarps * 32) {  // query rows of each tile of the pair
+      for (int row = xtid; row < (a_build ? 128 : 0); row += kXWarps * 32) {  // query rows of each tile of the pair
 #pragma unroll
         for (int g = 0; g < kG; ++g) {
           unsigned char* A = smem + L::off_a + (abuf * kG + g) * L::a_tile;
