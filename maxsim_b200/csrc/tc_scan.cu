@@ -19,6 +19,10 @@
 //     corpus, 2 x SM-count of them, ordered range-major, so every CTA gets the
 //     same number of equal-sized units and the CTAs working on one range run
 //     together and share its codes through L2.
+//   * Candidate lists: a list naming at least one document in 16 is read out of a
+//     full scan; a shorter one gets one unit per (listed document, query-tile
+//     pair), built on the device (candidate_units_kernel), and the same kernel
+//     scores the listed documents into a [B, D] scratch that is gathered.
 //   * Persistent CTAs (one per SM), 12 warps: warps 0-7 epilogue (query tile
 //     warp / 4, TMEM lane quarter warp % 4), warp 8 TMEM allocation and MMA
 //     issue (one thread), warps 9-10 expanders, warp 11 loader.  Fewer
