@@ -382,17 +382,14 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 
 // Maximum of row s (0 or 1) of a 16x256b chunk half X (its 16 values X[4j + 2s], X[4j + 2s + 1]) folded
 // into R: four independent chains of three-input maxima.
-// Insertion of x into a descending list of K values (the SIMT reducer's order: equal values keep their
-// places, so sums over the list do not depend on the insertion order of ties).
+// Insertion of x into a descending list of K values, keeping the K largest: v'[0] = max(v[0], x),
+// v'[i] = max(v[i], min(v[i-1], x)) (2K - 1 min / max instead of K compare-and-swaps).  The list is the
+// same multiset, in the same descending order, as the SIMT reducer's insertion gives, so its sum is too.
 template <int K>
 __device__ __forceinline__ void topk_insert(float (&v)[K], float x) {
 #pragma unroll
-  for (int i = 0; i < K; ++i) {
-    const float cur = v[i];
-    const bool take = x > cur;
-    v[i] = take ? x : cur;
-    x = take ? cur : x;
-  }
+  for (int i = K - 1; i > 0; --i) v[i] = fmaxf(v[i], fminf(v[i - 1], x));
+  v[0] = fmaxf(v[0], x);
 }
 
 template <int NJ>
