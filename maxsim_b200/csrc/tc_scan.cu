@@ -1218,7 +1218,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               carry = true;
               a = e;
             } else if (bnd > a && tile_live) {
-              if (kSmooth) {
+              if (kSmooth && a == c0 && bnd == c0 + kChunkCols) {
+                // the whole chunk inside the open document: no column tests, two partial sums
+                const float mn = fmaxf(sm_m, row_max16<kNJ>(ra, 0, kLowest));
+                float acc0 = sm_s > 0.0F ? sm_s * exp2f((sm_m - mn) * sm_c) : 0.0F, acc1 = 0.0F;
+#pragma unroll
+                for (int j = 0; j < kNJ; ++j) {
+                  acc0 += exp2f((__uint_as_float(ra[4 * j]) - mn) * sm_c);
+                  acc1 += exp2f((__uint_as_float(ra[4 * j + 1]) - mn) * sm_c);
+                }
+                sm_m = mn;
+                sm_s = acc0 + acc1;
+              } else if (kSmooth) {
                 // columns [a, bnd) of the open document into this thread's running log-sum-exp, in the
                 // row's digit-plane units u (v = u * qscale * scale): the segment's maximum first, then
                 // s = s * 2^((m - m') c) + sum 2^((u - m') c), c = qscale * scale * log2(e) / temperature
