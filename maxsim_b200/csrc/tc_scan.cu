@@ -1260,6 +1260,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                   sm_m = mn;
                   sm_s = acc_s;
                 }
+              } else if (kTopK && a == c0 && bnd == c0 + kChunkCols) {
+                // the whole chunk inside the open document: every column, no tests
+#pragma unroll
+                for (int j = 0; j < kNJ; ++j) {
+                  topk_insert<kTk>(tk, __uint_as_float(ra[4 * j]));
+                  topk_insert<kTk>(tk, __uint_as_float(ra[4 * j + 1]));
+                }
+                tk_cnt += 2 * kNJ;
               } else if (kTopK) {
                 // columns [a, bnd) of the open document into this thread's list
                 const int la = a - c0 - 2 * tc, lb = bnd - c0 - 2 * tc;
