@@ -499,7 +499,7 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
     if (engine == 2) throw NotSupported("no device memory for the tensor-core candidate scan's score matrix");
     use_tc = false;
   }
-  if (use_tc && r.mode == kQueryI8 && dv.token_scale) dv.token_scale_small = token_scales_small(h, dv.token_scale, stream);
+  if (use_tc && dv.token_scale) dv.token_scale_small = token_scales_small(h, dv.token_scale, stream);
   const int64_t rows = static_cast<int64_t>(batch) * qtok;
   if (r.mode == kQueryI8) {
     h->w_qcodes.ensure(static_cast<size_t>(rows) * h->dim, "cudaMalloc int8 query codes");

@@ -286,6 +286,15 @@ __device__ __forceinline__ void bias_scale2(uint32_t& x0, uint32_t& x1, float2 s
   x0 = __float_as_uint(v.x);
   x1 = __float_as_uint(v.y);
 }
+// Two biased accumulators (as above) to dot * 2^-23, exactly, as a float pair.
+template <bool kX16 = false>
+__device__ __forceinline__ float2 bias_unscale2(uint32_t x0, uint32_t x1) {
+  constexpr float kNeg = kX16 ? -static_cast<float>(kBiasValue16) / 134217728.0F
+                              : -static_cast<float>(kBiasValue) / 8388608.0F;
+  constexpr float kMul = kX16 ? 0x1p122F : 0x1p126F;
+  return __ffma2_rn(make_float2(__uint_as_float(x0), __uint_as_float(x1)), make_float2(kMul, kMul),
+                    make_float2(kNeg, kNeg));
+}
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
@@ -524,8 +533,8 @@ template <bool kTokenScale, bool kPre, bool kF16, bool kDigits = false, bool kTw
 __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __grid_constant__ CUtensorMap tmap,
                                                               const __grid_constant__ CUtensorMap tmap2) {
   using L = Layout<kPre, kF16, kRes, kBias>;
-  static_assert(!kBias || (kTokenScale && !kDigits && !kF16 && !kRes && kTopK == 0),
-                "biased accumulators: int8 queries with per-token scales");
+  static_assert(!kBias || (!kF16 && !kRes && (kDigits || (kTokenScale && kTopK == 0))),
+                "biased accumulators: int8 queries with per-token scales, or digit-plane queries");
   static_assert(!kRes || (kPre && kDigits && kTokenScale && !kF16), "the residual stream reads both int8 copies");
   static_assert(kTopK == 0 || (kTopK <= 4 && kPre && kDigits && !kRes), "TopK: digit-plane queries, int8 copies");
   static_assert(!kSmooth || (kTopK == 0 && kPre && kDigits && !kRes), "SmoothSim: digit-plane queries, int8 copies");
@@ -1015,7 +1024,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
       const bool w_store = !kDigits || tc == 0;
       const int wb = tile * p.qpt + wrow / Q;
       const bool w_valid = wrow < p.qpt * Q && wb < p.batch;
-      const float qs = w_valid ? __ldg(p.qscale + static_cast<int64_t>(wb) * Q + wrow % Q) : 0.0F;
+      // (biased digit planes without token scales: row values are 2^-23 x, the query scale 2^23 x; exact)
+      constexpr float kQsFold = (kDigits && kBias && !kTokenScale) ? 8388608.0F : 1.0F;
+      const float qs = w_valid ? __ldg(p.qscale + static_cast<int64_t>(wb) * Q + wrow % Q) * kQsFold : 0.0F;
       const int nq0 = max(0, min(p.qpt, p.batch - (unit.qpair * kG) * p.qpt));
       const int nq1 = kTwin ? 0 : max(0, min(p.qpt, p.batch - (unit.qpair * kG + 1) * p.qpt));
       const int nq = nq0 + nq1;
@@ -1108,7 +1119,23 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
               if (lane == 0) mbar_arrive(&acc_empty[acc.idx]);
               released = true;
             }
-            if (kDigits) {
+            if (kDigits && kBias) {
+              // biased planes: each exactly d * 2^-23 by one packed FMA; then fl(d0 + 256 d1) and
+              // fl(that + 65536 d2) by two more, the same roundings as the int32 / fmaf path below, scaled by
+              // 2^-23 (token scales are staged as s * 2^23, so fl(v * s) comes out unscaled; without token
+              // scales the row values stay 2^-23 x and the query scale takes the 2^23)
+#pragma unroll
+              for (int j = 0; j < kNJ; ++j) {
+                const float2 p0 = bias_unscale2<!kPre>(ra[4 * j], ra[4 * j + 1]);
+                const float2 p1 = bias_unscale2<!kPre>(ra[4 * j + 2], ra[4 * j + 3]);
+                const float2 p2 = bias_unscale2<!kPre>(rb[4 * j], rb[4 * j + 1]);
+                float2 v = __ffma2_rn(p2, make_float2(65536.0F, 65536.0F),
+                                      __ffma2_rn(p1, make_float2(256.0F, 256.0F), p0));
+                if (kTokenScale) v = __fmul2_rn(v, sc[j]);
+                ra[4 * j] = __float_as_uint(v.x);
+                ra[4 * j + 1] = __float_as_uint(v.y);
+              }
+            } else if (kDigits) {
               // rows 0, 1, 2 are the digit planes' exact dots: d0 + 256 d1 is exact in int32 (|d| <= 2^17),
               // one rounding to float and one fused multiply-add, then fl(dot * s_t); the result in row 0
 #pragma unroll
@@ -1957,33 +1984,32 @@ void dispatch_tc(const DocsView& d, const QueryView& q, const ReduceView& red, c
   if (res) {
     go(tc::tc_scan_kernel<true, true, false, true, false, true>, tc::tc_scan_kernel<true, true, false, true, true, true>,
        LayoutRes::bytes_plain);
-  } else if (smooth) {
-    if (d.token_scale)
-      go(tc::tc_scan_kernel<true, true, false, true, false, false, 0, false, true>,
-         tc::tc_scan_kernel<true, true, false, true, true, false, 0, false, true>, tc::Layout<true>::bytes_plain);
-    else
-      go(tc::tc_scan_kernel<false, true, false, true, false, false, 0, false, true>,
-         tc::tc_scan_kernel<false, true, false, true, true, false, 0, false, true>, tc::Layout<true>::bytes_plain);
-  } else if (topk) {
-#define MSB_TC_TOPK(TS, K) \
-  go(tc::tc_scan_kernel<TS, true, false, true, false, false, K>, tc::tc_scan_kernel<TS, true, false, true, true, false, K>, \
-     tc::Layout<true>::bytes_plain)
-    if (d.token_scale) {
-      if (topk == 2) MSB_TC_TOPK(true, 2);
-      else MSB_TC_TOPK(true, 4);
-    } else {
-      if (topk == 2) MSB_TC_TOPK(false, 2);
-      else MSB_TC_TOPK(false, 4);
-    }
-#undef MSB_TC_TOPK
   } else if (digits) {
-    if (d.token_scale) {
-      if (pre) MSB_TC_GO(true, true, false, true, tc::Layout<true>);
-      else MSB_TC_GO(true, false, false, true, tc::Layout<false>);
+    // digit planes: biased accumulators unless a token scale is too large for the exact s * 2^23
+    const bool bias = d.token_scale == nullptr || d.token_scale_small;
+#define MSB_TC_DIG(TS, PRE, K, SM, B)                                                     \
+  go(tc::tc_scan_kernel<TS, PRE, false, true, false, false, K, B, SM>,                   \
+     tc::tc_scan_kernel<TS, PRE, false, true, true, false, K, B, SM>, tc::Layout<PRE, false, false, B>::bytes_plain)
+#define MSB_TC_DIG2(TS, PRE, K, SM) \
+  if (bias) MSB_TC_DIG(TS, PRE, K, SM, true); else MSB_TC_DIG(TS, PRE, K, SM, false)
+    if (smooth) {
+      if (d.token_scale) MSB_TC_DIG2(true, true, 0, true);
+      else MSB_TC_DIG2(false, true, 0, true);
+    } else if (topk == 2) {
+      if (d.token_scale) MSB_TC_DIG2(true, true, 2, false);
+      else MSB_TC_DIG2(false, true, 2, false);
+    } else if (topk == 4) {
+      if (d.token_scale) MSB_TC_DIG2(true, true, 4, false);
+      else MSB_TC_DIG2(false, true, 4, false);
+    } else if (d.token_scale) {
+      if (pre) MSB_TC_DIG2(true, true, 0, false);
+      else MSB_TC_DIG2(true, false, 0, false);
     } else {
-      if (pre) MSB_TC_GO(false, true, false, true, tc::Layout<true>);
-      else MSB_TC_GO(false, false, false, true, tc::Layout<false>);
+      if (pre) MSB_TC_DIG2(false, true, 0, false);
+      else MSB_TC_DIG2(false, false, 0, false);
     }
+#undef MSB_TC_DIG2
+#undef MSB_TC_DIG
   } else if (d.token_scale) {
     // biased accumulators unless a token scale is too large for the exact s * 2^23
     if (f16) MSB_TC_GO(true, true, true, false, LayoutF16);
