@@ -103,17 +103,22 @@ int64_t msb_launch_count(void);
  * dim 128, scalar document scale), and use the SIMT engine when there is no
  * memory for it.  fp32 queries of up to 32 tokens run on the tensor-core
  * engine as three int8 digit planes of each row's 23-bit fixed-point value
- * (exact integer dots, one rounding), for MaxSim, weighted MaxSim and TopK2 /
- * TopK4.  The
+ * (exact integer dots, one rounding), for MaxSim, weighted MaxSim, TopK2 /
+ * TopK4 and SmoothSim.  The
  * fused residual stream (use_residual) runs there too, reading a second int8
  * copy of the residual codes (128 B per token, dropped when the residual is
  * replaced or cleared).  Candidate lists that name at least one document in
  * 16 are scored by a full tensor-core scan whose [batch, num_docs] scores
- * (workspace) are then gathered.  "tc_f16_cache": 1 keeps an f16
+ * (workspace) are then gathered; shorter lists by the same scan over the
+ * listed documents only, into the same kind of workspace.  "tc_f16_cache": 1
+ * keeps an f16
  * copy instead (256 B per token, per-token-scale corpora) and runs kind::f16
  * MMAs whose fp32 accumulators hold the exact integer dots, so the epilogue
  * converts nothing; 0 (default) because its doubled MMA and operand traffic
- * made it slower.  Unknown names return MSB_ERR_INVALID_ARGUMENT. */
+ * made it slower.  "tc_row_replicas": 1 (default) copies a pass's query rows
+ * (int8, at most 64) over the tensor memory's lane quarters.  "tc_fused_topk":
+ * 1 selects the full-scan top-k inside the int8-query scan (bit-identical, 0 by
+ * default: measured slower).  Unknown names return MSB_ERR_INVALID_ARGUMENT. */
 int msb_set_option(const char* name, int64_t value);
 int msb_get_option(const char* name, int64_t* value);
 
