@@ -20,7 +20,9 @@ void launch_simt_scan(const DocsView&, const QueryView&, const ReduceView&, cons
                       cudaStream_t);
 void launch_quantize_rows(const float*, int64_t, int, int8_t*, float*, int32_t*, int32_t*, bool, cudaStream_t);
 void launch_split_query_digits(const float*, int64_t, int32_t*, float*, const float*, int, int, cudaStream_t);
-void launch_topk_rows(const float*, int64_t, int, int64_t, int, const int64_t*, bool, float*, int64_t*, cudaStream_t);
+void launch_topk_rows(const float*, int64_t, int, int64_t, int, const int64_t*, bool, float*, int64_t*, cudaStream_t,
+                      void* ws = nullptr, size_t ws_bytes = 0);
+size_t topk_rows_workspace_bytes(int rows, int64_t T, int k);
 void launch_merge_shard_topk(const void*, int, int, int, const int64_t*, float*, int64_t*, cudaStream_t);
 void launch_gather_scores(const float*, int64_t, int, const int64_t*, int64_t, bool, float*, cudaStream_t);
 void launch_pack_int4(const float*, int64_t, int, bool, uint8_t*, float*, float*, void*, cudaStream_t);
@@ -174,8 +176,9 @@ struct msb_docs {
   // Workspace (grows monotonically, reused across calls).
   DeviceBuf w_query, w_qcodes, w_qwords, w_qscale, w_qsum, w_scores, w_cands, w_weights, w_top_s, w_top_i,
       w_override, w_fine, w_tc, w_popc,
-      w_full,   // full-scan scores that candidate lists are gathered from
-      w_units;  // work units of a candidate-list tensor-core scan
+      w_full,    // full-scan scores that candidate lists are gathered from
+      w_units,   // work units of a candidate-list tensor-core scan
+      w_select;  // per-chunk lists of a two-stage top-k over few long rows
   std::vector<int64_t> host_offsets;
   bool tc_used = false;  // the tensor-core engine ran since the last error check
   uint64_t serial = 0;   // unique corpus id for caches keyed on a corpus
@@ -216,7 +219,7 @@ struct msb_docs {
     return static_cast<int64_t>(w_query.cap + w_qcodes.cap + w_qwords.cap + w_qscale.cap + w_qsum.cap +
                                 w_scores.cap + w_cands.cap + w_weights.cap + w_top_s.cap + w_top_i.cap +
                                 w_override.cap + w_fine.cap + w_tc.cap + w_check.cap + w_full.cap +
-                                w_popc.cap + w_topk.cap + w_units.cap);
+                                w_popc.cap + w_topk.cap + w_units.cap + w_select.cap);
   }
   ~msb_docs() {
     int prev = -1;
@@ -227,7 +230,7 @@ struct msb_docs {
                         &w_query, &w_qcodes, &w_qwords,    &w_qscale,  &w_qsum,         &w_scores,
                         &w_cands, &w_weights, &w_top_s,    &w_top_i,   &w_override,     &w_fine,
                         &w_tc,    &codes8,   &codes16,   &w_check,        &codes2_8,  &w_full, &w_popc, &w_topk, &empty_ids,
-                        &w_units};
+                        &w_units, &w_select};
     for (DeviceBuf* b : all) b->release();
     pin_in.release();
     pin_out.release();
@@ -545,6 +548,15 @@ void run_scan(msb_docs* h, const Resolved& r, const float* d_query, int batch, i
     return;
   }
   launch_simt_scan(r.docs, qv, r.red, tg, r.residual, d_out, stream);
+}
+
+// Top-k of `rows` full score rows with the handle's selection workspace (a few long rows are selected in
+// chunks by several blocks each, then merged).
+void topk_full_rows(msb_docs* h, const float* scores, int rows, int k, float* out_s, int64_t* out_id, cudaStream_t s) {
+  const size_t ws = topk_rows_workspace_bytes(rows, h->num_docs, k);
+  if (ws) h->w_select.ensure(ws, "cudaMalloc top-k selection workspace");
+  launch_topk_rows(scores, h->num_docs, rows, h->num_docs, k, nullptr, false, out_s, out_id, s, ws ? h->w_select.ptr : nullptr,
+                   ws ? h->w_select.cap : 0);
 }
 
 // Fused top-k set-up for a full-scan top-k (k <= 4096): candidate workspace and the empty-document list.
@@ -1179,9 +1191,7 @@ int msb_docs_topk(msb_docs* h, const float* query, int32_t batch, int32_t qtok, 
     TopkFuse fuse{};
     const bool try_fuse = prepare_fused_topk(h, batch, k, h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), &fuse);
     run_scan(h, r, d_q, batch, qtok, tg, h->w_scores.as<float>(), s, try_fuse ? &fuse : nullptr);
-    if (!fuse.done)
-      launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, k, nullptr, false,
-                       h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
+    if (!fuse.done) topk_full_rows(h, h->w_scores.as<float>(), batch, k, h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
     finish_host_call(h, s,
                      {{out_scores, h->w_top_s.ptr, sizeof(float) * static_cast<size_t>(batch) * k},
                       {out_ids, h->w_top_i.ptr, sizeof(int64_t) * static_cast<size_t>(batch) * k}},
@@ -1224,8 +1234,7 @@ int msb_docs_cascade_topk(msb_docs* h, const float* query, int32_t batch, int32_
     if (m == h->num_docs) {
       h->w_scores.ensure(sizeof(float) * B * h->num_docs, "cudaMalloc full score cache");
       run_scan(h, rf, d_q, batch, qtok, TargetsView{}, h->w_scores.as<float>(), s);
-      launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, k, nullptr, false,
-                       h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
+      topk_full_rows(h, h->w_scores.as<float>(), batch, k, h->w_top_s.as<float>(), h->w_top_i.as<int64_t>(), s);
     } else {
       h->w_scores.ensure(sizeof(float) * B * h->num_docs, "cudaMalloc coarse score cache");
       h->w_cands.ensure(sizeof(int64_t) * B * m, "cudaMalloc cascade candidate cache");
@@ -1233,8 +1242,7 @@ int msb_docs_cascade_topk(msb_docs* h, const float* query, int32_t batch, int32_
       run_scan(h, rp, d_q, batch, qtok, TargetsView{}, h->w_scores.as<float>(), s);
       // Per-row top-M of the prefix scores (values land in the second half of w_fine).
       float* top_m_scores = h->w_fine.as<float>() + B * m;
-      launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, m, nullptr, false, top_m_scores,
-                       h->w_cands.as<int64_t>(), s);
+      topk_full_rows(h, h->w_scores.as<float>(), batch, m, top_m_scores, h->w_cands.as<int64_t>(), s);
       TargetsView tg{};
       tg.ids = h->w_cands.as<int64_t>();
       tg.count = m;
@@ -1290,9 +1298,7 @@ int msb_docs_topk_device(msb_docs* h, const float* query, int32_t batch, int32_t
     TopkFuse fuse{};
     const bool try_fuse = prepare_fused_topk(h, batch, k, out_scores, out_ids, &fuse);
     run_scan(h, r, query, batch, qtok, TargetsView{}, h->w_scores.as<float>(), s, try_fuse ? &fuse : nullptr);
-    if (!fuse.done)
-      launch_topk_rows(h->w_scores.as<float>(), h->num_docs, batch, h->num_docs, k, nullptr, false, out_scores,
-                       out_ids, s);
+    if (!fuse.done) topk_full_rows(h, h->w_scores.as<float>(), batch, k, out_scores, out_ids, s);
   });
 }
 

@@ -78,9 +78,14 @@ __global__ void __launch_bounds__(kTopkThreads) topk_sort_kernel(const float* __
   }
 }
 
+// Block (row, c) selects the top k of targets [c * chunk, min(T, (c + 1) * chunk)) of its row.  One chunk per
+// row (chunk >= T): the row's top-k into out_s / out_id.  Several chunks: each block writes its sorted list,
+// with global target ids, as block c of `blocks` (16 * rows * k bytes per chunk: [rows, k] scores, then
+// [rows, k] int64 ids), the layout merge_shard_topk_kernel merges.
 __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(const float* __restrict__ scores, int64_t ld,
                                                                     int64_t T, int k, float* __restrict__ out_s,
-                                                                    int64_t* __restrict__ out_id) {
+                                                                    int64_t* __restrict__ out_id, int64_t chunk,
+                                                                    unsigned char* __restrict__ blocks) {
   extern __shared__ unsigned char smem_raw[];
   __shared__ uint32_t hist[256];
   __shared__ uint32_t s_prefix, s_mask, s_remaining, s_taken, s_ties_taken;
@@ -90,7 +95,14 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(const float* 
   uint64_t* key = reinterpret_cast<uint64_t*>(smem_raw);
   uint32_t* pos = reinterpret_cast<uint32_t*>(key + n);
   const int row = blockIdx.x;
-  const float* s = scores + static_cast<int64_t>(row) * ld;
+  const int64_t start = static_cast<int64_t>(blockIdx.y) * chunk;
+  const float* s = scores + static_cast<int64_t>(row) * ld + start;
+  T = T - start < chunk ? T - start : chunk;  // this block's targets (at least k: the host sizes chunks)
+  if (blocks) {
+    const int64_t rows = gridDim.x;
+    out_s = reinterpret_cast<float*>(blocks + static_cast<int64_t>(blockIdx.y) * 16 * rows * k);
+    out_id = reinterpret_cast<int64_t*>(blocks + static_cast<int64_t>(blockIdx.y) * 16 * rows * k + 8 * rows * k);
+  }
 
   if (threadIdx.x == 0) {
     s_prefix = 0;
@@ -173,7 +185,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_select_kernel(const float* 
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
     uint32_t p = pos[i];
     out_s[static_cast<int64_t>(row) * k + i] = s[p];
-    out_id[static_cast<int64_t>(row) * k + i] = static_cast<int64_t>(p);
+    out_id[static_cast<int64_t>(row) * k + i] = start + static_cast<int64_t>(p);
   }
 }
 
@@ -183,8 +195,31 @@ static int next_pow2(int64_t v) {
   return n;
 }
 
+void launch_merge_shard_topk(const void* gathered, int world, int batch, int k, const int64_t* first_doc, float* out_s,
+                             int64_t* out_id, cudaStream_t stream);
+
+// Rows shorter than this are selected by one block each: below it the selection's fixed per-pass costs,
+// not the row's length, set a block's time, and a second launch would only add to them.
+constexpr int64_t kChunkedSelectMin = 32768;
+
+// Chunks per row of a two-stage selection (1: one block per row), given the workspace it may use.
+int select_chunks(int rows, int64_t T, int k, size_t ws_bytes) {
+  if (T < kChunkedSelectMin) return 1;
+  int64_t c = (T + 2047) / 2048;                              // about 2,048 targets a block
+  c = std::min<int64_t>(c, std::max<int64_t>(1, 296 / rows));  // enough blocks for the SMs, no more
+  c = std::min<int64_t>(c, std::min<int64_t>(64, T / k));
+  // every chunk, the last one included, holds at least k targets; the lists fit the workspace
+  while (c > 1 && (T - (c - 1) * ((T + c - 1) / c) < k || static_cast<size_t>(c) * 16 * rows * k > ws_bytes)) --c;
+  return static_cast<int>(c);
+}
+
+size_t topk_rows_workspace_bytes(int rows, int64_t T, int k) {
+  return T < kChunkedSelectMin ? 0 : static_cast<size_t>(64) * 16 * rows * k;
+}
+
 void launch_topk_rows(const float* scores, int64_t ld, int rows, int64_t T, int k, const int64_t* tie_ids,
-                      bool tie_batched, float* out_s, int64_t* out_id, cudaStream_t stream) {
+                      bool tie_batched, float* out_s, int64_t* out_id, cudaStream_t stream, void* ws,
+                      size_t ws_bytes) {
   if (rows <= 0) return;
   if (k < 1 || k > T) throw InvalidArgument("k must be between 1 and the number of targets");
   if (T > 0xFFFFFFF0LL) throw NotSupported("top-k rows longer than 2^32 - 16 are not supported");
@@ -204,7 +239,18 @@ void launch_topk_rows(const float* scores, int64_t ld, int rows, int64_t T, int 
                                static_cast<int>(smem)),
           "raise top-k shared memory limit");
   }
-  topk_select_kernel<<<rows, kTopkThreads, smem, stream>>>(scores, ld, T, k, out_s, out_id);
+  // Few long rows: chunks of a row selected by separate blocks (rows x chunks), then merged
+  const int chunks = ws ? select_chunks(rows, T, k, ws_bytes) : 1;
+  if (chunks > 1) {
+    const int64_t chunk = (T + chunks - 1) / chunks;
+    topk_select_kernel<<<dim3(rows, chunks), kTopkThreads, smem, stream>>>(scores, ld, T, k, nullptr, nullptr, chunk,
+                                                                             static_cast<unsigned char*>(ws));
+    count_launch();
+    check(cudaGetLastError(), "launch chunked top-k select kernel");
+    launch_merge_shard_topk(ws, chunks, rows, k, nullptr, out_s, out_id, stream);
+    return;
+  }
+  topk_select_kernel<<<rows, kTopkThreads, smem, stream>>>(scores, ld, T, k, out_s, out_id, T, nullptr);
   count_launch();
   check(cudaGetLastError(), "launch top-k select kernel");
 }
