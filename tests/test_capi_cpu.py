@@ -50,6 +50,24 @@ def test_option_errors_map_to_value_error():
     assert _lib.get_engine() in (0, 1, 2)
 
 
+@pytest.mark.parametrize("name,default", [("tc_int8_cache", 1), ("tc_f16_cache", 0), ("tc_row_replicas", 1),
+                                          ("tc_fused_topk", 0)])
+def test_boolean_options_round_trip(name, default):
+    """Every tensor-core routing option reads back what was set, defaults as documented, and refuses values
+    other than 0 and 1."""
+    from maxsim_b200 import _lib
+
+    assert _lib.get_option(name) == default
+    try:
+        for v in (1 - default, default):
+            _lib.set_option(name, v)
+            assert _lib.get_option(name) == v
+        with pytest.raises(ValueError, match=f"{name} must be 0 or 1"):
+            _lib.set_option(name, 2)
+    finally:
+        _lib.set_option(name, default)
+
+
 def test_handle_validation_happens_before_device_work():
     """Offsets / scale errors are ValueError (reference std::invalid_argument)."""
     from maxsim_b200 import _maxsim_cuda as mc
