@@ -273,7 +273,8 @@ def batch_sweep(args, torch, _lib, handle, queries, device):
     """One line per batch size: scan + top-k of the whole resident corpus, CUDA events on the launching
     stream, against both roofs (algorithmic HBM bytes and int8 tensor ops of that batch)."""
     hbm_peak, bf16_peak, _, peak_kind = _peaks()
-    int8_peak = 2.0 * bf16_peak
+    int8_peak = _int8_gemm_tops(torch, device) or 2.0 * bf16_peak
+    peak_kind += ", int8: measured cuBLASLt GEMM burst (else 2 x bf16)"
     n_tok = NUM_PAGES * PAGE_TOKENS
     stream = torch.cuda.Stream(device)
     torch.cuda.set_stream(stream)
@@ -306,15 +307,46 @@ def batch_sweep(args, torch, _lib, handle, queries, device):
 
 
 def _peaks():
-    """(HBM GB/s, bf16 TF/s burst, bf16 TF/s sustained, source).  No int8 figure is measured on this pool:
-    the int8 dense tensor rate is taken as 2 x the bf16 figure (the B200's nominal ratio), an assumption
-    stated beside every fraction computed from it."""
+    """(HBM GB/s, bf16 TF/s burst, bf16 TF/s sustained, source) from MEASURED_PEAKS.json (else the pool's
+    fallback figures).  The file has no int8 figure: ``_int8_gemm_tops`` measures one in the same run."""
     path = REPO / "MEASURED_PEAKS.json"
     if path.exists():
         d = json.loads(path.read_text())
         burst = float(d["bf16_tflops"])
         return float(d["hbm_gbs"]), burst, float(d.get("bf16_tflops_sustained", burst)), "measured"
     return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+INT8_GEMM_N = 8192
+
+
+def _int8_gemm_tops(torch, device, reps=20, warm=5):
+    """Measured int8 tensor-core rate of this GPU: a cuBLASLt int8 x int8 -> int32 GEMM
+    (``torch._int_mm``, 8192 x 8192 x 8192, B column-major), CUDA events over ``reps`` calls after
+    ``warm`` untimed ones (a burst, like the bf16 figure of MEASURED_PEAKS.json).  The denominator of the
+    headline kernel's tensor roofline; None if the library call is unavailable."""
+    n = INT8_GEMM_N
+    g = torch.Generator(device=device)
+    g.manual_seed(1)
+    try:
+        a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=device, generator=g)
+        b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=device, generator=g).t()
+        for _ in range(warm):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize(device)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(reps):
+            torch._int_mm(a, b)
+        t1.record()
+        torch.cuda.synchronize(device)
+        ms = t0.elapsed_time(t1) / reps
+    except (RuntimeError, AttributeError):
+        return None
+    finally:
+        a = b = None
+        torch.cuda.empty_cache()
+    return 2.0 * n ** 3 / (ms * 1e-3) / 1e12
 
 
 # ---------------------------------------------------------------------------
@@ -746,22 +778,29 @@ def main() -> None:
                                   f"median of 3 steps"}
 
     hbm_peak, bf16_peak, bf16_sustained, peak_kind = _peaks()
+    int8_measured = _int8_gemm_tops(torch, device)  # after the timed regions
     n_local = (page_hi - page_lo) * PAGE_TOKENS
     algo_bytes = n_local * (DIM // 2 + 4) + 8 * (page_hi - page_lo + 1) + BATCH * QUERY_TOKENS * DIM + BATCH * TOP_K * 12
     algo_ops = 2.0 * BATCH * QUERY_TOKENS * n_local * DIM
     achieved_gbs = algo_bytes / (kernel_ms * 1e-3) / 1e9
     achieved_tops = algo_ops / (kernel_ms * 1e-3) / 1e12
-    int8_peak = 2.0 * bf16_peak
+    int8_assumed = 2.0 * bf16_peak
+    int8_peak = int8_measured if int8_measured else int8_assumed
     hbm_time = algo_bytes / (hbm_peak * 1e9)
     tc_time = algo_ops / (int8_peak * 1e12)
     bound = "tensor" if tc_time > hbm_time else "hbm"
     if bound == "tensor":
         roof = {"bound": "tensor", "achieved": achieved_tops, "peak": int8_peak, "unit": "TOP/s",
                 "frac": achieved_tops / int8_peak,
-                "peak_note": f"ASSUMED int8 dense rate = 2 x the {peak_kind} bf16 cuBLAS burst ({bf16_peak} TF/s); "
-                             f"no int8 peak is measured on this pool",
-                "frac_vs_sustained": achieved_tops / (2.0 * bf16_sustained),
-                "sustained_peak": 2.0 * bf16_sustained}
+                "peak_note": (f"measured in this run: cuBLASLt int8 GEMM burst (torch._int_mm, {INT8_GEMM_N}^3, "
+                              f"CUDA events)" if int8_measured else
+                              f"ASSUMED int8 dense rate = 2 x the {peak_kind} bf16 cuBLAS burst ({bf16_peak} TF/s); "
+                              f"the int8 GEMM measurement was unavailable"),
+                "frac_vs_2x_bf16_burst": achieved_tops / int8_assumed,
+                "frac_vs_2x_bf16_sustained": achieved_tops / (2.0 * bf16_sustained),
+                "int8_gemm_measured_tops": int8_measured,
+                "bf16_peaks_source": f"{peak_kind} (MEASURED_PEAKS.json: burst {bf16_peak}, sustained "
+                                     f"{bf16_sustained} TF/s)"}
     else:
         roof = {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
                 "frac": achieved_gbs / hbm_peak, "peak_note": peak_kind}
