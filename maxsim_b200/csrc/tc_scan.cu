@@ -1851,8 +1851,10 @@ struct UnitCacheKey {
   uint64_t corpus_id;
   int64_t n_ranges;
   int n_pairs;
+  bool split;  // the last pair's units at the end of the table (see launch_tc_scan)
   bool operator==(const UnitCacheKey& o) const {
-    return ws == o.ws && corpus_id == o.corpus_id && n_ranges == o.n_ranges && n_pairs == o.n_pairs;
+    return ws == o.ws && corpus_id == o.corpus_id && n_ranges == o.n_ranges && n_pairs == o.n_pairs &&
+           split == o.split;
   }
 };
 
@@ -1902,10 +1904,10 @@ bool fuse_fits(const DocsView& d, const QueryView& q, const ReduceView& red, con
 // (fused top-k) the merge of the CTAs' candidate blocks.
 void dispatch_tc(const DocsView& d, const QueryView& q, const ReduceView& red, const TcPlan& pl, int sms,
                  const tc::Unit* d_units, int num_units, float* out, int* err, bool fused, TopkFuse* fuse,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, bool clear_err = true) {
   const int reps = row_copies(pl, q);
   const int lists = pl.n_qtiles == 1 ? 2 : 1;
-  check(cudaMemsetAsync(err, 0, sizeof(int), stream), "clear tc error flag");
+  if (clear_err) check(cudaMemsetAsync(err, 0, sizeof(int), stream), "clear tc error flag");
   tc::Params prm{};
   prm.codes = d.codes;
   prm.token_scale = d.token_scale;
@@ -2048,24 +2050,30 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
   static std::vector<std::pair<UnitCacheKey, int>> cache;  // key -> number of units
   const int sms = sm_count();
   const TcPlan pl = plan_for(d, q, sms);
-  const UnitCacheKey key{ws, d.corpus_id, pl.n_ranges, pl.n_pairs};
+  UnitCacheKey key{ws, d.corpus_id, pl.n_ranges, pl.n_pairs, false};
   int* err = static_cast<int*>(ws);
   tc::Unit* d_units = reinterpret_cast<tc::Unit*>(static_cast<unsigned char*>(ws) + 256);
+  const bool fused = fuse_fits(d, q, red, pl, sms, fuse);
+  if (fuse) fuse->done = false;
+  // An odd number (> 1) of int8 query tiles: the last tile would fill only half of its pair's units (four
+  // of the eight epilogue warps working), so it runs as a launch of its own in twin mode, its two epilogue
+  // groups taking two document ranges in turn, after the full pairs' launch.  The table then lists the
+  // full pairs' units (range-major) and after them the last tile's, one per range.
+  const bool split = !fused && q.mode == kQueryI8 && pl.n_qtiles > 1 && (pl.n_qtiles & 1) != 0;
+  key.split = split;
   int num_units = -1;
   {
     std::lock_guard<std::mutex> lock(cache_mu);
     for (auto& e : cache)
       if (e.first == key) num_units = e.second;
   }
-  const bool fused = fuse_fits(d, q, red, pl, sms, fuse);
-  if (fuse) fuse->done = false;
   // Empty documents never appear in a tile; their score is 0.
   if (!fused)
     check(cudaMemsetAsync(out, 0, sizeof(float) * static_cast<size_t>(q.batch) * d.num_docs, stream), "zero scores");
   if (num_units < 0) {
     // Document ranges cut at the token quantiles r * N / n_ranges, each split
     // further to at most kMaxRangeDocs documents; range-major units.
-    std::vector<tc::Unit> units;
+    std::vector<tc::Unit> units, tail;
     const int64_t* off = d.host_offsets;
     const int64_t D = d.num_docs, N = d.num_tokens;
     int64_t lo = 0;
@@ -2078,11 +2086,15 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
       }
       while (lo < hi) {
         const int64_t h2 = std::min<int64_t>(hi, lo + tc::kMaxRangeDocs);  // unit offsets live in shared memory
-        if (off[h2] > off[lo])
-          for (int t = 0; t < pl.n_pairs; ++t) units.push_back(tc::Unit{lo, h2, off[lo], off[h2], t, 0});
+        if (off[h2] > off[lo]) {
+          for (int t = 0; t < pl.n_pairs - (split ? 1 : 0); ++t) units.push_back(tc::Unit{lo, h2, off[lo], off[h2], t, 0});
+          // split: the last tile's unit, as query tile 0 of its own launch
+          if (split) tail.push_back(tc::Unit{lo, h2, off[lo], off[h2], 0, 0});
+        }
         lo = h2;
       }
     }
+    units.insert(units.end(), tail.begin(), tail.end());
     const size_t need = 256 + sizeof(tc::Unit) * units.size();
     if (need > ws_bytes) throw CudaFailure("tensor-core scan workspace too small");
     if (!units.empty()) {
@@ -2102,6 +2114,26 @@ void launch_tc_scan(const DocsView& d, const QueryView& q, const ReduceView& red
     launch_empty_block(fuse->cand, q.batch, fuse->k, fuse->empty_ids, std::min(fuse->n_empty, fuse->k), stream);
     launch_merge_shard_topk(fuse->cand, 1, q.batch, fuse->k, nullptr, fuse->out_s, fuse->out_i, stream);
     fuse->done = true;
+    return;
+  }
+  if (split) {
+    const int n_tail = num_units / pl.n_pairs;  // every range lists n_pairs units
+    dispatch_tc(d, q, red, pl, sms, d_units, num_units - n_tail, out, err, false, nullptr, stream);
+    // the last tile's queries as a one-tile batch of their own: query rows, scales and score rows offset
+    const int b0 = (pl.n_qtiles - 1) * pl.qpt;
+    const int64_t r0 = static_cast<int64_t>(b0) * q.qtok;
+    QueryView q1 = q;
+    q1.batch = q.batch - b0;
+    if (q.f32) q1.f32 = q.f32 + r0 * d.dim;
+    if (q.i8) q1.i8 = q.i8 + r0 * d.dim;
+    q1.i8_words = q.i8_words + r0 * (d.dim / 4);
+    q1.row_scale = q.row_scale + r0;
+    if (q.row_sum) q1.row_sum = q.row_sum + r0;
+    TcPlan pl1 = pl;
+    pl1.n_qtiles = 1;
+    pl1.n_pairs = 1;
+    dispatch_tc(d, q1, red, pl1, sms, d_units + (num_units - n_tail), n_tail, out + static_cast<int64_t>(b0) * d.num_docs,
+                err, false, nullptr, stream, false);
     return;
   }
   dispatch_tc(d, q, red, pl, sms, d_units, num_units, out, err, fused, fuse, stream);

@@ -3,8 +3,8 @@
 ``bench.py`` times 64 queries x 24 tokens (int8 per row) against 1,030-token
 pages through the default tensor-core path: the resident int8 copy of the
 codes read by tiled TMA, biased accumulators (per-token scales), 13 query
-tiles of 5 queries (so 7 tile pairs, the last one half empty) and 2 x SM-count
-document ranges.  The tests here run that geometry on 2,048 pages and require
+tiles of 5 queries (6 full tile pairs, then the 13th tile in a twin-mode launch
+of its own) and 2 x SM-count document ranges.  The tests here run that geometry on 2,048 pages and require
 the whole score matrix and the top-10 ids and scores to equal the C oracle's
 restatement of the reference kernel exactly (the int8 x int4 dots are
 integers; the fp32 epilogue is the reference's).  They also pin the variant

@@ -69,7 +69,8 @@ def tc_operands(request):
 
 
 @pytest.mark.parametrize("gran", ["token", "tensor"])
-@pytest.mark.parametrize("batch,qtok", [(1, 1), (3, 24), (11, 24), (4, 32), (2, 100), (2, 128), (7, 20)])
+@pytest.mark.parametrize("batch,qtok", [(1, 1), (3, 24), (11, 24), (12, 24), (23, 24), (4, 32), (2, 100), (2, 128),
+                                        (7, 20)])
 def test_tc_int8_scores_exact(oracle_c, gran, batch, qtok):
     import maxsim_b200 as m
 
