@@ -1179,13 +1179,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_scan_kernel(Params p, const __
                   rb[k] = __float_as_uint(__int2float_rn(static_cast<int32_t>(rb[k]) >> (kPre ? 0 : 4)));
                 }
               }
+              // fl(dot * s_t) two columns at a time (packed products round each element as a scalar one)
 #pragma unroll
               for (int j = 0; j < kNJ; ++j) {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float s1 = (e & 1) ? sc[j].y : sc[j].x;
-                  ra[4 * j + e] = __float_as_uint(__fmul_rn(__uint_as_float(ra[4 * j + e]), s1));
-                  rb[4 * j + e] = __float_as_uint(__fmul_rn(__uint_as_float(rb[4 * j + e]), s1));
+                for (int e = 0; e < 4; e += 2) {
+                  const float2 x = __fmul2_rn(make_float2(__uint_as_float(ra[4 * j + e]), __uint_as_float(ra[4 * j + e + 1])), sc[j]);
+                  const float2 y = __fmul2_rn(make_float2(__uint_as_float(rb[4 * j + e]), __uint_as_float(rb[4 * j + e + 1])), sc[j]);
+                  ra[4 * j + e] = __float_as_uint(x.x);
+                  ra[4 * j + e + 1] = __float_as_uint(x.y);
+                  rb[4 * j + e] = __float_as_uint(y.x);
+                  rb[4 * j + e + 1] = __float_as_uint(y.y);
                 }
               }
             }
