@@ -18,6 +18,9 @@ It imports the reference's Python package from ``<reference>/src`` (with the
                        (``tests/test_int4_int8q.py``, ``tests/test_binary_int8q.py``)
 * ``index_<mode>.npz`` -- ``Index.save`` files written by the reference for
                        every corpus mode (npz layout golden)
+* ``binres.npz``    -- the binary-prefix residual cascade scored and cascaded
+                       by the reference's residual code (``--only-binres``
+                       writes this file alone)
 * ``sdk_search.json`` -- ``Reranker(device="cpu").search`` results
 * ``sdk_rerank.json`` -- ``Reranker(device="cpu").rerank`` results on a candidate list
 
@@ -70,16 +73,57 @@ def _ragged(num_docs, seed, dim=128, lo=1, hi=9, empty_at=2):
     return docs, offsets
 
 
+def binary_residual_golden(cascade, experimental) -> None:
+    """``binres.npz``: the binary-prefix residual cascade (sign bits scaled by the per-token mean |x|, plus
+    the per-token int4 residual of x - mean|x| * sign(x)) scored by the reference's own code.  The reference
+    has no sign-code prefix, but its residual cascade takes any symmetric int4 prefix: the signs as int4
+    codes +-1 with prefix scale 1 and the mean |x| as the prefix's token scales reconstruct exactly the
+    sign-code prefix, and the residual is packed by the reference's per-token int4 packer.  Its CPU
+    ``residual_score`` (the fused reconstruction) and ``cascade_topk`` (prefix scan, stable top-M, rescoring)
+    then give the scores and cascades this format must reproduce."""
+    docs, off = _ragged(120, seed=81, lo=2, hi=16, empty_at=5)
+    query = np.random.default_rng(83).standard_normal((3, 16, 128)).astype(np.float32)
+    weights = np.random.default_rng(84).uniform(0.5, 1.5, size=16).astype(np.float32)
+    signs = np.where(docs >= 0, 1, -1).astype(np.int8)
+    mean_abs = np.mean(np.abs(docs), axis=1, dtype=np.float64).astype(np.float32)
+    residual = (docs - mean_abs[:, None] * signs.astype(np.float32)).astype(np.float32)
+    rpk = experimental.pack_int4_symmetric(residual, off, scale_granularity="token")
+    assert float(rpk.scale) == 1.0
+    packed = cascade.ResidualInt4PackedDocs(
+        prefix_data=experimental._pack_signed_int4_values(signs), prefix_values=signs, prefix_scale=1.0,
+        prefix_token_scale=mean_abs, residual_data=rpk.data, residual_values=rpk.values,
+        residual_scale=float(rpk.scale), residual_token_scale=rpk.token_scale, doc_offsets=rpk.doc_offsets,
+        dim=128, num_docs=int(off.shape[0] - 1), device="cpu")
+    out = dict(docs=docs, offsets=off, query=query, weights=weights, prefix_token_scale=mean_abs,
+               residual_values=rpk.values, residual_data=rpk.data, residual_token_scale=rpk.token_scale)
+    for reducer in REDUCERS:
+        kw = dict(reducer=reducer, temperature=0.1 if reducer == "smoothsim" else 1.0)
+        if reducer == "weighted_maxsim":
+            kw["query_weights"] = weights
+        out[f"{reducer}_full"] = cascade.residual_score(query, packed, device="cpu", **kw)
+    for m in (10, 40, 120):
+        cs, ci = cascade.cascade_topk(query, packed, 5, candidates=m, device="cpu")
+        out[f"cascade_m{m}_scores"] = cs
+        out[f"cascade_m{m}_indices"] = ci
+    np.savez_compressed(HERE / "binres.npz", **out)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", default=os.environ.get("MAXSIM_REFERENCE"),
                         help="path of the reference source tree (or set MAXSIM_REFERENCE)")
+    parser.add_argument("--only-binres", action="store_true", help="write binres.npz alone")
     args = parser.parse_args()
     if not args.reference:
         parser.error("give --reference or set MAXSIM_REFERENCE")
     ref_root = Path(args.reference)
     ms = _load_reference(ref_root)
     from maxsim import cascade, experimental  # reference modules
+
+    binary_residual_golden(cascade, experimental)
+    if args.only_binres:
+        print("binres.npz written to", HERE)
+        return
 
     out_formats: dict[str, np.ndarray] = {}
     out_scores: dict[str, np.ndarray] = {}

@@ -1,9 +1,12 @@
-"""Binary-prefix residual cascade on the GPU against the oracle restatement.
+"""Binary-prefix residual cascade on the GPU against the oracle restatement and the reference's own code.
 
 Format: sign bits scaled by the per-token mean |x|, plus a per-token int4
-residual of x - mean|x| * sign(x).  The reference has no such format (its
-cascade uses an int4 prefix), so parity is against the oracle's restatement:
-fp32 scores within the fp32 tolerance, top-k ids exact.
+residual of x - mean|x| * sign(x).  The reference has no sign-code prefix, but
+its residual cascade accepts any symmetric int4 prefix: the signs as int4 codes
++-1 with the mean |x| as the prefix's token scales are the same format, and
+``tests/golden/binres.npz`` holds what the reference's ``residual_score`` and
+``cascade_topk`` return for it.  Parity: fp32 scores within the fp32
+tolerance, top-k ids exact, against both.
 """
 
 import numpy as np
@@ -75,3 +78,34 @@ def test_cascade_rejects_bad_sizes(corpus):
         m.binary_cascade_topk(q, dev, 6, candidates=5)
     with pytest.raises(ValueError):
         m.binary_cascade_topk(q, dev, 5, candidates=301)
+
+
+@pytest.fixture(scope="module")
+def reference_made(golden):
+    """The fixture the reference's own residual code scored (``tests/golden/binres.npz``), uploaded."""
+    import maxsim_b200 as m
+
+    g = golden("binres.npz")
+    return g, m.binary_residual_to_device(m.pack_binary_residual_int4(g["docs"], g["offsets"]))
+
+
+@pytest.mark.parametrize("reducer", ["maxsim", "weighted_maxsim", "topk2", "topk4", "smoothsim"])
+def test_scores_match_reference_golden(reference_made, reducer):
+    import maxsim_b200 as m
+
+    g, dev = reference_made
+    kw = dict(reducer=reducer, temperature=0.1 if reducer == "smoothsim" else 1.0)
+    if reducer == "weighted_maxsim":
+        kw["query_weights"] = g["weights"]
+    np.testing.assert_allclose(m.binary_residual_score(g["query"], dev, **kw), g[f"{reducer}_full"],
+                               rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("m_cand", [10, 40, 120])
+def test_cascade_matches_reference_golden(reference_made, m_cand):
+    import maxsim_b200 as m
+
+    g, dev = reference_made
+    s, i = m.binary_cascade_topk(g["query"], dev, 5, candidates=m_cand)
+    np.testing.assert_array_equal(i, g[f"cascade_m{m_cand}_indices"])
+    np.testing.assert_allclose(s, g[f"cascade_m{m_cand}_scores"], rtol=RTOL, atol=ATOL)

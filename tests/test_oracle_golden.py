@@ -227,3 +227,38 @@ def test_binary_residual_host_pack_matches_oracle():
     p = ref.unpack_signs(want["bits"], 128) * want["prefix_token_scale"][:, None]
     r = want["residual_values"] * want["residual_token_scale"][:, None]
     assert np.abs(docs - (p + r)).mean() < 0.25 * np.abs(docs - p).mean()
+
+
+def test_binary_residual_oracle_matches_reference(golden):
+    """The binary-prefix residual format: the oracle's packing and scores against the reference's own
+    residual code run on the same format (signs as int4 codes +-1 with the per-token mean |x| as prefix
+    token scales, ``tests/golden/make_golden.py``)."""
+    g = golden("binres.npz")
+    res = ref.pack_binary_residual(g["docs"])
+    np.testing.assert_array_equal(res["prefix_token_scale"], g["prefix_token_scale"])
+    np.testing.assert_array_equal(res["residual_values"], g["residual_values"])
+    np.testing.assert_array_equal(res["residual_data"], g["residual_data"])
+    np.testing.assert_array_equal(res["residual_token_scale"], g["residual_token_scale"])
+    for reducer in REDUCERS:
+        kw = dict(reducer=reducer, temperature=0.1 if reducer == "smoothsim" else 1.0)
+        if reducer == "weighted_maxsim":
+            kw["weights"] = g["weights"]
+        got = ref.score_binary_residual(g["query"], res, g["offsets"], **kw)
+        np.testing.assert_allclose(got, g[f"{reducer}_full"], rtol=1e-4, atol=1e-4)
+    for m in (10, 40, 120):
+        s, i = ref.binary_cascade_topk(g["query"], res, g["offsets"], 5, m)
+        np.testing.assert_array_equal(i, g[f"cascade_m{m}_indices"])
+        np.testing.assert_allclose(s, g[f"cascade_m{m}_scores"], rtol=1e-4, atol=1e-4)
+
+
+def test_binary_residual_packer_matches_reference(golden):
+    """The library's host packer writes the same streams as the reference-built fixture."""
+    import maxsim_b200 as m
+
+    g = golden("binres.npz")
+    p = m.pack_binary_residual_int4(g["docs"], g["offsets"])
+    np.testing.assert_array_equal(p.prefix_token_scale, g["prefix_token_scale"])
+    np.testing.assert_array_equal(p.residual_values, g["residual_values"])
+    np.testing.assert_array_equal(p.residual_data, g["residual_data"])
+    np.testing.assert_array_equal(p.residual_token_scale, g["residual_token_scale"])
+    np.testing.assert_array_equal(ref.unpack_signs(p.prefix_data, 128) > 0, g["docs"] >= 0)
